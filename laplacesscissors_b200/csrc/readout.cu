@@ -1,0 +1,716 @@
+// Fused readout-margin validation on B200 tensor cores.
+//
+// For many hidden states h_i and target tokens t_i this computes, without ever
+// storing logits,
+//     z_i        = W (Q h_i) + b                        (W: [V, H] bf16 lm_head)
+//     margin_i   = f64(z_i[t_i]) - f64(max_{j != t_i} z_i[j])   (lowest index on ties)
+//     argmax_i   = first index of max_j z_i[j]
+// which is what verify_cached does per prefix with Model::readout, argmax and
+// minimum_margin (src/diagnosis.rs:493-580, 490-492, 58-70; src/model.rs:664-685).
+//
+// The edit Q = I + U^T (R - I) U (rank r, U orthonormal rows; a plane is r = 2)
+// enters as a rank-r correction, the identity CompactReadout uses
+// (src/diagnosis.rs:608-666):
+//     W Q h = W h + F c,   F = W U^T  [V, r],   c = (R - I) U h  [r]
+// The main product W h runs on tcgen05 with bf16 operands and f32 accumulation in
+// TMEM: a bf16 hidden state is exact; an f32 hidden state is split into hi + lo
+// bf16 planes (two MMAs).  F c is appended as one extra K block of split-bf16
+// terms [c_hi | c_lo | c_hi] x [F_hi | F_hi | F_lo], so the correction keeps
+// ~16 more bits than a bf16 rounding of Q h would.
+//
+// Kernel structure (one persistent CTA per SM, 6 warps):
+//   warp 0     TMA producer: A (hidden) and B (lm_head) tiles, 128B swizzle
+//   warp 1     TMEM owner and single-thread MMA issuer (tcgen05.mma kind::f16)
+//   warps 2-5  epilogue: tcgen05.ld of the 128 x 256 f32 accumulator, per-row
+//              best-other / target logit, one 64-bit atomicMax per row and tile
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of one tile overlap
+// the MMAs of the next.  Tiles are ordered with the hidden-row block fastest so
+// concurrently running CTAs share each lm_head block through L2.
+// No load uses cluster multicast; every TMA source is this GPU's own memory.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <math.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "device_common.cuh"
+#include "lsx_internal.h"
+
+namespace lsx {
+
+constexpr int RM = 128;  // hidden rows per tile (TMEM lanes)
+constexpr int RN = 256;  // vocab columns per tile
+constexpr int RK = 64;   // K per stage: 64 bf16 = 128 bytes = one swizzle atom row
+constexpr int kReadoutThreads = 192;
+constexpr int kTileBytesA = RM * RK * 2;  // 16 KB
+constexpr int kTileBytesB = RN * RK * 2;  // 32 KB
+
+struct ReadoutParams {
+    int M, V, H;
+    int k_blocks, ext_blocks, m_tiles, n_tiles;
+    const uint32_t* targets;
+    const float* bias;
+    unsigned long long* other_key;  // [M] packed (value, index) of the best non-target
+    float* target_logit;            // [M]
+    int* status;                    // [0] device error code, [1] non-finite flag
+};
+
+// ---------------------------------------------------------------- PTX ------
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major tile whose rows are 128 bytes,
+// stored by TMA with 128-byte swizzle: 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);        // start address
+    d |= (uint64_t)1 << 16;                        // leading byte offset (unused with swizzle)
+    d |= (uint64_t)(1024 >> 4) << 32;              // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                        // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;                        // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: kind::f16, bf16 A and B (K-major), f32 accumulate, M x N.
+constexpr uint32_t kIdesc = (1u << 4)            // D format f32
+                            | (1u << 7)          // A format bf16
+                            | (1u << 10)         // B format bf16
+                            | ((RN >> 3) << 17)  // N
+                            | ((RM >> 4) << 24); // M
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    long long start = clock64();
+    while (!mbar_try_wait(a, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - start > kWaitCycles) return false;
+    }
+    return true;
+}
+
+template <int PLANES, int STAGES>
+__global__ void __launch_bounds__(kReadoutThreads, 1)
+    readout_margin_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
+                          const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_ea,
+                          const __grid_constant__ CUtensorMap map_eb, const ReadoutParams p) {
+    constexpr int kStageBytes = PLANES * kTileBytesA + kTileBytesB;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tmem_full = empty + STAGES;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued_count = const_cast<int*>(abort_flag) + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = p.m_tiles * p.n_tiles;
+    const int k_total = p.k_blocks + p.ext_blocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 4 * 32);
+        }
+        *abort_flag = 0;
+        *issued_count = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {  // TMEM: two 256-column f32 accumulators
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const int m0 = (tile % p.m_tiles) * RM;
+                const int n0 = (tile / p.m_tiles) * RN;
+                for (int kb = 0; kb < k_total; ++kb) {
+                    if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * kStageBytes;
+                    uint8_t* sb = sa + PLANES * kTileBytesA;
+                    if (kb < p.k_blocks) {
+                        mbar_expect_tx(&full[stage], kStageBytes);
+                        tma_load_2d(sa, &map_a, kb * RK, m0, &full[stage]);
+                        if (PLANES == 2) tma_load_2d(sa + kTileBytesA, &map_a2, kb * RK, m0, &full[stage]);
+                        tma_load_2d(sb, &map_b, kb * RK, n0, &full[stage]);
+                    } else {
+                        const int e = kb - p.k_blocks;
+                        mbar_expect_tx(&full[stage], kTileBytesA + kTileBytesB);
+                        tma_load_2d(sa, &map_ea, e * RK, m0, &full[stage]);
+                        tma_load_2d(sb, &map_eb, e * RK, n0, &full[stage]);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            *issued_count = issued;
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---------------- MMA issuer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                if (!wait_or_abort(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * RN);
+                for (int kb = 0; kb < k_total; ++kb) {
+                    if (!wait_or_abort(&full[stage], phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+                    const uint32_t sb = sa + PLANES * kTileBytesA;
+                    const uint64_t bdesc = smem_desc_sw128(sb);
+                    const int planes = kb < p.k_blocks ? PLANES : 1;
+                    for (int pl = 0; pl < planes; ++pl) {
+                        const uint64_t adesc = smem_desc_sw128(sa + pl * kTileBytesA);
+#pragma unroll
+                        for (int k = 0; k < RK / 16; ++k) {
+                            // +32 bytes along K inside the swizzle atom per 16-element step
+                            const uint32_t accumulate = (kb | pl | k) != 0;
+                            tc_mma(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc, accumulate);
+                        }
+                    }
+                    tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+    } else {  // ---------------- epilogue warps 2..5 ----------------
+        const int quarter = warp & 3;  // TMEM lane group this warp may access
+        const int row_local = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool nonfinite = false;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+            const int m0 = (tile % p.m_tiles) * RM;
+            const int n0 = (tile / p.m_tiles) * RN;
+            const bool ok = wait_or_abort(&tmem_full[acc], acc_phase, abort_flag);
+            if (__any_sync(0xffffffffu, !ok)) {
+                if (lane == 0) {
+                    atomicExch(&p.status[0], kDeviceTimeoutEpilogue);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int row = m0 + row_local;
+            const bool live = row < p.M;
+            const int tcol = live ? (int)p.targets[row] - n0 : -1;
+            float best = -INFINITY, tval = 0.f;
+            int best_col = -1;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
+#pragma unroll 1
+            for (int c = 0; c < RN / 32; ++c) {
+                uint32_t r[32];
+                tc_ld32(taddr + (uint32_t)(c * 32), r);
+                tc_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int col = c * 32 + i;
+                    if (n0 + col < p.V) {
+                        float z = __uint_as_float(r[i]);
+                        if (p.bias) z += __ldg(&p.bias[n0 + col]);
+                        nonfinite |= !isfinite(z);
+                        if (col == tcol) tval = z;
+                        else if (z > best) {
+                            best = z;
+                            best_col = col;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);
+            if (live) {
+                if (best_col >= 0) atomicMax(&p.other_key[row], pack_arg(best, (uint32_t)(n0 + best_col)));
+                if (tcol >= 0 && tcol < RN && n0 + tcol < p.V) p.target_logit[row] = tval;
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (__any_sync(0xffffffffu, nonfinite) && lane == 0) atomicOr(&p.status[1], 1);
+    }
+
+    __syncthreads();
+    if (*abort_flag) {
+        // Leave nothing in flight: wait (bounded) for every TMA stage that was issued.
+        if (threadIdx.x == 0) {
+            const int issued = *issued_count;
+            for (int s = 0; s < STAGES && s < issued; ++s) {
+                const int last = issued - 1 - ((issued - 1 - s) % STAGES);  // latest use of stage s
+                mbar_wait_bounded(&full[s], (uint32_t)((last / STAGES) & 1));
+            }
+        }
+        __syncthreads();
+    }
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
+}
+
+// ------------------------------------------------------------ prep kernels --
+// F = W U^T for ranks [k0, k0 + kc), written as split bf16 into the extension
+// block of B: columns [k] = hi(F), [r + k] = hi(F), [2r + k] = lo(F).
+__global__ void __launch_bounds__(256) edit_image_kernel(const __nv_bfloat16* __restrict__ W, int V, int H,
+                                                         const float* __restrict__ basis, int rank, int k0, int kc,
+                                                         __nv_bfloat16* __restrict__ ext_b, int ext_k) {
+    extern __shared__ float us[];  // kc x H
+    for (int i = threadIdx.x; i < kc * H; i += blockDim.x) us[i] = basis[(size_t)k0 * H + i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j = blockIdx.x * 8 + warp; j < V; j += gridDim.x * 8) {
+        float acc[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+        const uint4* row = reinterpret_cast<const uint4*>(W + (size_t)j * H);
+        for (int c = lane; c < H / 8; c += 32) {
+            uint4 w = row[c];
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+            float wf[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float2 f = __bfloat1622float2(h2[q]);
+                wf[2 * q] = f.x;
+                wf[2 * q + 1] = f.y;
+            }
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                if (k < kc) {
+                    const float* u = us + k * H + c * 8;
+                    float s = acc[k];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) s = fmaf(wf[q], u[q], s);
+                    acc[k] = s;
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k < kc) {
+                float f = warp_allsum(acc[k]);
+                if (lane == 0) {
+                    __nv_bfloat16 hi = __float2bfloat16_rn(f);
+                    __nv_bfloat16 lo = __float2bfloat16_rn(f - __bfloat162float(hi));
+                    __nv_bfloat16* dst = ext_b + (size_t)j * ext_k;
+                    dst[k0 + k] = hi;
+                    dst[rank + k0 + k] = hi;
+                    dst[2 * rank + k0 + k] = lo;
+                }
+            }
+        }
+    }
+}
+
+// c = (R - I) U h per hidden row, written as [c_hi | c_lo | c_hi] into the
+// extension block of A; also splits f32 hidden rows into bf16 hi/lo planes.
+__global__ void __launch_bounds__(256) edit_coefficients_kernel(const void* __restrict__ hidden, int hidden_kind,
+                                                                int M, int H, const float* __restrict__ basis,
+                                                                const float* __restrict__ delta, int rank,
+                                                                __nv_bfloat16* __restrict__ ext_a, int ext_k,
+                                                                __nv_bfloat16* __restrict__ plane_hi,
+                                                                __nv_bfloat16* __restrict__ plane_lo) {
+    __shared__ float coords[8][256];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x * 8 + warp;
+    if (i >= M) return;
+    auto h_at = [&](int j) -> float {
+        if (hidden_kind == LSX_F32) return ((const float*)hidden)[(size_t)i * H + j];
+        return __bfloat162float(((const __nv_bfloat16*)hidden)[(size_t)i * H + j]);
+    };
+    if (plane_hi) {
+        for (int j = lane; j < H; j += 32) {
+            float h = h_at(j);
+            __nv_bfloat16 hi = __float2bfloat16_rn(h);
+            plane_hi[(size_t)i * H + j] = hi;
+            plane_lo[(size_t)i * H + j] = __float2bfloat16_rn(h - __bfloat162float(hi));
+        }
+    }
+    if (rank == 0) return;
+    for (int k = 0; k < rank; ++k) {
+        float d = 0.f;
+        for (int j = lane; j < H; j += 32) d = fmaf(basis[(size_t)k * H + j], h_at(j), d);
+        d = warp_allsum(d);
+        if (lane == 0) coords[warp][k] = d;
+    }
+    __syncwarp();
+    __nv_bfloat16* dst = ext_a + (size_t)i * ext_k;
+    for (int k = lane; k < ext_k; k += 32) dst[k] = __float2bfloat16_rn(0.f);
+    __syncwarp();
+    for (int k = lane; k < rank; k += 32) {
+        float c = 0.f;
+        for (int q = 0; q < rank; ++q) c = fmaf(delta[k * rank + q], coords[warp][q], c);
+        __nv_bfloat16 hi = __float2bfloat16_rn(c);
+        __nv_bfloat16 lo = __float2bfloat16_rn(c - __bfloat162float(hi));
+        dst[k] = hi;
+        dst[rank + k] = lo;
+        dst[2 * rank + k] = hi;
+    }
+}
+
+__global__ void readout_init_kernel(unsigned long long* other_key, float* target_logit, int M, int* status) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < M) {
+        other_key[i] = 0ull;
+        target_logit[i] = __int_as_float(0x7fc00000);
+    }
+    if (i < 2) status[i] = 0;
+}
+
+// margin and first argmax from (best other, target logit): argmax is the target
+// when it beats the best other, or ties it with a lower index.
+__global__ void readout_finalize_kernel(const unsigned long long* other_key, const float* target_logit,
+                                        const uint32_t* targets, int M, double* margin, uint32_t* argmax,
+                                        float* target_out) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M) return;
+    const unsigned long long k = other_key[i];
+    const float ov = packed_value(k);
+    const uint32_t oi = packed_index(k);
+    const float tv = target_logit[i];
+    const uint32_t t = targets[i];
+    if (margin) margin[i] = (double)tv - (double)ov;
+    if (argmax) argmax[i] = (tv > ov || (tv == ov && t < oi)) ? t : oi;
+    if (target_out) target_out[i] = tv;
+}
+
+// ------------------------------------------------------------ host side ----
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+        else
+            (void)cudaGetLastError();
+    }
+    return fn;
+}
+
+// 2-D bf16 tensor map of a row-major [rows, cols] matrix with a (64 x box_rows)
+// box and 128-byte swizzle; out-of-range elements read as zero.
+int make_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(LSX_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    LSX_ENSURE((uintptr_t)base % 16 == 0 && row_bytes % 16 == 0, "tensor map operands must be 16-byte aligned");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)RK, box_rows};
+    cuuint32_t elem[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LSX_E_CUDA, "cuTensorMapEncodeTiled failed with " + std::to_string((int)r));
+    return LSX_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+    size_t ext_k, planes_off, planes_bytes, ext_a_off, ext_b_off, basis_off, delta_off, key_off, tlog_off,
+        status_off, total;
+};
+
+Layout layout_for(size_t vocab, size_t width, size_t rows, size_t rank, bool f32_hidden) {
+    Layout L{};
+    L.ext_k = rank ? ((3 * rank + RK - 1) / RK) * RK : 0;
+    size_t at = 0;
+    L.planes_off = at;
+    L.planes_bytes = f32_hidden ? rows * width * 2 : 0;
+    at = align256(at + 2 * L.planes_bytes);
+    L.ext_a_off = at;
+    at = align256(at + rows * L.ext_k * 2);
+    L.ext_b_off = at;
+    at = align256(at + vocab * L.ext_k * 2);
+    L.basis_off = at;
+    at = align256(at + rank * width * 4);
+    L.delta_off = at;
+    at = align256(at + rank * rank * 4);
+    L.key_off = at;
+    at = align256(at + rows * 8);
+    L.tlog_off = at;
+    at = align256(at + rows * 4);
+    L.status_off = at;
+    at = align256(at + 16);
+    L.total = at;
+    return L;
+}
+
+template <int PLANES, int STAGES>
+size_t readout_smem() {
+    return (size_t)STAGES * (PLANES * kTileBytesA + kTileBytesB) + 1024 + (2 * STAGES + 4) * 8 + 16;
+}
+
+}  // namespace
+
+// Enqueues the whole validation on ctx->stream.  All pointers are device pointers.
+int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
+                           const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
+                           const lsx_rotation* rotation, double* margin, uint32_t* argmax, float* target_logit,
+                           void* workspace, size_t workspace_bytes, int* host_status) {
+    LSX_ENSURE(weight && weight->kind == LSX_BF16, "the readout weight must be a BF16 tensor");
+    LSX_ENSURE(vocab > 1 && width > 0 && weight->count == vocab * width, "check the readout weight dimensions");
+    LSX_ENSURE(!bias || (bias->kind == LSX_F32 && bias->count == vocab), "the readout bias is F32 [vocab]");
+    LSX_ENSURE(hidden_kind == LSX_F32 || hidden_kind == LSX_BF16, "hidden states are F32 or BF16");
+    LSX_ENSURE(rows > 0 && rows <= 2147483647ull && vocab <= 2147483647ull, "check the row count");
+    LSX_ENSURE(width % 8 == 0, "the readout width must be a multiple of 8");
+    if (rotation) LSX_ENSURE(rotation->width == width, "the rotation width does not match the readout");
+    const size_t rank = rotation ? rotation->rank : 0;
+    const bool f32_hidden = hidden_kind == LSX_F32;
+    Layout L = layout_for(vocab, width, rows, rank, f32_hidden);
+    LSX_ENSURE(workspace && workspace_bytes >= L.total, "the readout workspace is too small");
+    uint8_t* ws = (uint8_t*)workspace;
+    cudaStream_t s = ctx->stream;
+    int* status = (int*)(ws + L.status_off);
+    unsigned long long* keys = (unsigned long long*)(ws + L.key_off);
+    float* tlog = (float*)(ws + L.tlog_off);
+    __nv_bfloat16* plane_hi = f32_hidden ? (__nv_bfloat16*)(ws + L.planes_off) : nullptr;
+    __nv_bfloat16* plane_lo = f32_hidden ? plane_hi + rows * width : nullptr;
+    __nv_bfloat16* ext_a = (__nv_bfloat16*)(ws + L.ext_a_off);
+    __nv_bfloat16* ext_b = (__nv_bfloat16*)(ws + L.ext_b_off);
+    const int M = (int)rows, V = (int)vocab, H = (int)width;
+
+    readout_init_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, M, status);
+    LSX_CUDA(cudaGetLastError(), "readout init");
+    if (rank > 0) {
+        // Edit basis and R - I in f32 from the f64 host copies.
+        std::vector<float> b(rank * width), d(rank * rank);
+        for (size_t i = 0; i < b.size(); ++i) b[i] = (float)rotation->basis64[i];
+        for (size_t i = 0; i < d.size(); ++i) d[i] = (float)rotation->delta64[i];
+        float* dbasis = (float*)(ws + L.basis_off);
+        float* ddelta = (float*)(ws + L.delta_off);
+        LSX_CUDA(cudaMemcpyAsync(dbasis, b.data(), b.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
+        LSX_CUDA(cudaMemcpyAsync(ddelta, d.data(), d.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
+        LSX_CUDA(cudaStreamSynchronize(s), "edit upload");  // host vectors go out of scope
+        LSX_CUDA(cudaMemsetAsync(ext_b, 0, vocab * L.ext_k * 2, s), "extension clear");
+        const int kc_max = std::max(1, std::min(16, (int)(65536 / (width * 4))));
+        for (int k0 = 0; k0 < (int)rank; k0 += kc_max) {
+            const int kc = std::min(kc_max, (int)rank - k0);
+            const size_t smem = (size_t)kc * width * 4;
+            edit_image_kernel<<<std::min(ctx->sm_count * 8, (V + 7) / 8), 256, smem, s>>>(
+                (const __nv_bfloat16*)weight->data, V, H, dbasis, (int)rank, k0, kc, ext_b, (int)L.ext_k);
+            LSX_CUDA(cudaGetLastError(), "edit image");
+        }
+        edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, dbasis, ddelta, (int)rank,
+                                                             ext_a, (int)L.ext_k, plane_hi, plane_lo);
+        LSX_CUDA(cudaGetLastError(), "edit coefficients");
+    } else if (f32_hidden) {
+        edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, nullptr, nullptr, 0, nullptr,
+                                                             0, plane_hi, plane_lo);
+        LSX_CUDA(cudaGetLastError(), "hidden split");
+    }
+
+    CUtensorMap ma, ma2, mb, mea, meb;
+    const void* a_base = f32_hidden ? (const void*)plane_hi : hidden;
+    LSX_TRY(make_map(&ma, a_base, width, rows, width * 2, RM));
+    LSX_TRY(make_map(&ma2, f32_hidden ? (const void*)plane_lo : a_base, width, rows, width * 2, RM));
+    LSX_TRY(make_map(&mb, weight->data, width, vocab, width * 2, RN));
+    if (rank > 0) {
+        LSX_TRY(make_map(&mea, ext_a, L.ext_k, rows, L.ext_k * 2, RM));
+        LSX_TRY(make_map(&meb, ext_b, L.ext_k, vocab, L.ext_k * 2, RN));
+    } else {
+        mea = ma;
+        meb = mb;
+    }
+    ReadoutParams p{};
+    p.M = M;
+    p.V = V;
+    p.H = H;
+    p.k_blocks = (H + RK - 1) / RK;
+    p.ext_blocks = (int)(L.ext_k / RK);
+    p.m_tiles = (M + RM - 1) / RM;
+    p.n_tiles = (V + RN - 1) / RN;
+    p.targets = targets;
+    p.bias = bias ? (const float*)bias->data : nullptr;
+    p.other_key = keys;
+    p.target_logit = tlog;
+    p.status = status;
+    const int total = p.m_tiles * p.n_tiles;
+    const int grid = std::min(total, ctx->sm_count);
+    if (f32_hidden) {
+        auto k = readout_margin_kernel<2, 3>;
+        size_t smem = readout_smem<2, 3>();
+        LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "readout smem attribute");
+        k<<<grid, kReadoutThreads, smem, s>>>(ma, ma2, mb, mea, meb, p);
+    } else {
+        auto k = readout_margin_kernel<1, 4>;
+        size_t smem = readout_smem<1, 4>();
+        LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "readout smem attribute");
+        k<<<grid, kReadoutThreads, smem, s>>>(ma, ma2, mb, mea, meb, p);
+    }
+    LSX_CUDA(cudaGetLastError(), "readout margin launch");
+    readout_finalize_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, targets, M, margin, argmax, target_logit);
+    LSX_CUDA(cudaGetLastError(), "readout finalize");
+    if (host_status) {
+        LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
+    }
+    return LSX_OK;
+}
+
+}  // namespace lsx
+
+using namespace lsx;
+
+extern "C" {
+
+size_t lsx_readout_workspace_bytes(size_t vocab, size_t width, size_t rows, const lsx_rotation* rotation) {
+    // Sized for F32 hidden states (the larger case).
+    return layout_for(vocab, width, rows, rotation ? rotation->rank : 0, true).total;
+}
+
+int lsx_readout_margin_device(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab,
+                              size_t width, const void* hidden, lsx_dtype hidden_kind, size_t rows,
+                              const uint32_t* targets, const lsx_rotation* rotation, double* margin_out,
+                              uint32_t* argmax_out, float* target_logit_out, void* workspace,
+                              size_t workspace_bytes) {
+    LSX_ENSURE(ctx && hidden && targets, "invalid argument");
+    cudaSetDevice(ctx->device);
+    return readout_margin_enqueue(ctx, weight, bias, vocab, width, hidden, hidden_kind, rows, targets, rotation,
+                                  margin_out, argmax_out, target_logit_out, workspace, workspace_bytes, nullptr);
+}
+
+int lsx_readout_margin(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
+                       const void* hidden, lsx_dtype hidden_kind, size_t rows, const uint32_t* targets,
+                       const lsx_rotation* rotation, double* margin_out, uint32_t* argmax_out,
+                       float* target_logit_out) {
+    LSX_ENSURE(ctx && weight && hidden && targets, "invalid argument");
+    LSX_ENSURE(hidden_kind == LSX_F32 || hidden_kind == LSX_BF16, "hidden states are F32 or BF16");
+    LSX_ENSURE(rows > 0 && vocab > 1, "check the row count");
+    for (size_t i = 0; i < rows; ++i) LSX_ENSURE(targets[i] < vocab, "check the target token range");
+    cudaSetDevice(ctx->device);
+    const size_t hbytes = rows * width * (hidden_kind == LSX_F32 ? 4 : 2);
+    const size_t ws_bytes = lsx_readout_workspace_bytes(vocab, width, rows, rotation);
+    const size_t out_bytes = rows * (8 + 4 + 4);
+    const size_t total = align256(hbytes) + align256(rows * 4) + align256(out_bytes) + ws_bytes;
+    void* block = nullptr;
+    LSX_TRY(device_alloc(ctx, total, &block));
+    uint8_t* b = (uint8_t*)block;
+    void* d_hidden = b;
+    uint32_t* d_targets = (uint32_t*)(b + align256(hbytes));
+    uint8_t* d_out = b + align256(hbytes) + align256(rows * 4);
+    double* d_margin = (double*)d_out;
+    uint32_t* d_argmax = (uint32_t*)(d_out + rows * 8);
+    float* d_tlog = (float*)(d_out + rows * 12);
+    void* ws = d_out + align256(out_bytes);
+    cudaStream_t s = ctx->stream;
+    int status[2] = {0, 0};
+    int rc = LSX_OK;
+    cudaError_t e = cudaMemcpyAsync(d_hidden, hidden, hbytes, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_targets, targets, rows * 4, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("readout upload", e));
+    if (rc == LSX_OK)
+        rc = readout_margin_enqueue(ctx, weight, bias, vocab, width, d_hidden, hidden_kind, rows, d_targets, rotation,
+                                    d_margin, d_argmax, d_tlog, ws, ws_bytes, status);
+    if (rc == LSX_OK) {
+        e = cudaSuccess;
+        if (margin_out) e = cudaMemcpyAsync(margin_out, d_margin, rows * 8, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && argmax_out) e = cudaMemcpyAsync(argmax_out, d_argmax, rows * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess && target_logit_out)
+            e = cudaMemcpyAsync(target_logit_out, d_tlog, rows * 4, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("readout margin", e));
+    }
+    device_release(ctx, block);
+    if (rc != LSX_OK) return rc;
+    if (status[0] != 0) return fail(LSX_E_CUDA, "readout kernel reported status " + std::to_string(status[0]));
+    if (status[1] != 0) return fail(LSX_E_NONFINITE, "check the finiteness of the readout scores");
+    return LSX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,249 @@
+"""The readout-validation and generation functions of src/diagnosis.rs over liblsx.
+
+argmax / other / minimum_margin restate the reference's host rules
+(src/diagnosis.rs:58-80, 490-492) for host arrays.  generate_frames runs the
+greedy loop on the device (lsx_model_generate).  verify_cached evaluates every
+target prefix of every observed path in ONE fused tensor-core launch
+(lsx_readout_margin: margin and first argmax without storing logits) and keeps
+the reference's aggregation and acceptance rule (src/diagnosis.rs:493-580).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from ._lib import BF16, F32, check, lib
+from .gpu import Gpu, Tensor, _dp, _fp, _up
+from .model import DeviceRotation, Frame, Model
+
+
+class BudgetExpired(RuntimeError):  # src/diagnosis.rs:22-29
+    pass
+
+
+class Deadline:  # src/diagnosis.rs:30-48
+    def __init__(self, seconds: float):
+        self.end = time.monotonic() + seconds
+
+    @staticmethod
+    def after(seconds: float) -> "Deadline":
+        return Deadline(seconds)
+
+    def check(self) -> None:
+        if time.monotonic() >= self.end:
+            raise BudgetExpired("the diagnosis time budget is used up")
+
+
+def _finite_scores(values: np.ndarray) -> np.ndarray:
+    v = np.asarray(values, dtype=np.float32)
+    if v.size == 0 or not np.all(np.isfinite(v)):
+        raise ValueError("finite vocabulary scores are required")
+    return v
+
+
+def argmax(values) -> int:  # src/diagnosis.rs:58-70: first maximum
+    v = _finite_scores(values)
+    return int(np.argmax(v))
+
+
+def _total_key(v: np.ndarray) -> np.ndarray:
+    i = v.astype(np.float32).view(np.int32).astype(np.int64)
+    return np.where(i < 0, i ^ 0x7FFFFFFF, i)
+
+
+def other(logits, target: int) -> int:  # src/diagnosis.rs:71-80
+    v = np.asarray(logits, dtype=np.float32)
+    if not (v.size > 1 and 0 <= target < v.size):
+        raise ValueError("check the vocabulary range of the answer token")
+    key = _total_key(v)
+    key[target] = np.iinfo(np.int64).min
+    return int(np.argmax(key))  # lowest index among equal keys
+
+
+def minimum_margin(scores, target: int) -> float:  # src/diagnosis.rs:490-492
+    v = np.asarray(scores, dtype=np.float32)
+    return float(np.float64(v[target]) - np.float64(v[other(v, target)]))
+
+
+def prefill(model: Model, gpu: Gpu, prompt, edit: DeviceRotation | None, deadline: Deadline) -> Frame:
+    """src/diagnosis.rs:81-99: reset, then feed the prompt token by token."""
+    if not (0 < len(prompt) <= model.max_context()):
+        raise ValueError("check the input token length")
+    model.reset()
+    frame = None
+    for token in prompt:
+        deadline.check()
+        frame = model.advance(gpu, int(token), edit)
+    return frame
+
+
+@dataclass
+class Generation:  # src/diagnosis.rs:100-105 (token ids; text decoding is the caller's)
+    tokens: list[int]
+    stopped: bool
+
+
+def generate_frames(model: Model, gpu: Gpu, stop_tokens, prompt, maximum: int,
+                    edit: DeviceRotation | None, deadline: Deadline) -> tuple[Generation, list[Frame]]:
+    """src/diagnosis.rs:106-149, with the whole loop on the device."""
+    deadline.check()
+    tokens, stopped, frames = model.generate(prompt, maximum, stop_tokens, edit, frames=True)
+    return Generation([int(t) for t in tokens], stopped), frames
+
+
+def generate(model: Model, gpu: Gpu, stop_tokens, prompt, maximum: int, edit: DeviceRotation | None,
+             deadline: Deadline) -> Generation:
+    deadline.check()
+    tokens, stopped, _ = model.generate(prompt, maximum, stop_tokens, edit, frames=False)
+    return Generation([int(t) for t in tokens], stopped)
+
+
+# ------------------------------------------------------------ validation ----
+def readout_margin(gpu: Gpu, weight: Tensor, bias: Tensor | None, vocab: int, width: int, hidden: np.ndarray,
+                   targets: np.ndarray, rotation: DeviceRotation | None = None):
+    """Fused readout margin over host rows (lsx_readout_margin).  `hidden` is
+    float32 [n, width] or uint16 bf16 bits [n, width].  Returns (margin f64,
+    argmax u32, target logit f32)."""
+    h = np.ascontiguousarray(hidden)
+    kind = BF16 if h.dtype == np.uint16 else F32
+    if kind == F32:
+        h = np.ascontiguousarray(h, dtype=np.float32)
+    n = h.shape[0]
+    t = np.ascontiguousarray(targets, dtype=np.uint32)
+    margin = np.empty(n, dtype=np.float64)
+    amax = np.empty(n, dtype=np.uint32)
+    tl = np.empty(n, dtype=np.float32)
+    check(lib.lsx_readout_margin(gpu.handle, weight.handle, bias.handle if bias else None, int(vocab), int(width),
+                                 h.ctypes.data_as(C.c_void_p), kind, n, _up(t),
+                                 rotation.handle if rotation else None, _dp(margin), _up(amax), _fp(tl)))
+    return margin, amax, tl
+
+
+@dataclass
+class ObservedPath:  # the observed prefixes of one case (src/diagnosis.rs ObservedPath)
+    case: int
+    protected: bool
+    tokens: list[int]
+    frames: list[Frame]
+    answer_matches: bool = True  # generation.text == case.answer() when the tokens match
+
+
+@dataclass
+class Verification:  # src/diagnosis.rs Verification
+    method: str
+    target_min_margin: float
+    protected_max_logit_change: float
+    protected_max_scaled_change: float
+    certified_paths: list[bool]
+    generations: list[Generation]
+    protected_sequences_preserved: bool
+    requested_answers_generated: bool
+    readout_calls: int
+    decoder_steps: int
+    accepted: bool
+
+
+def verify_cached(model: Model, gpu: Gpu, stop_tokens, edit, paths: list[ObservedPath], margin: float,
+                  tolerance: float, deadline: Deadline) -> Verification:
+    """src/diagnosis.rs:493-580.  Target prefixes: one fused margin/argmax launch
+    for all of them.  Protected prefixes: Model::readout per prefix and the
+    reference's f64 change statistics against the cached logits."""
+    width = model.hidden_size
+    device = DeviceRotation.upload_edit(gpu, edit, width)
+    weight, bias = model.head_tensors()
+    V = model.vocab_size()
+    stop = set(int(s) for s in stop_tokens)
+    # Fused pass over every target prefix.
+    rows, targets, owners = [], [], []
+    for pi, path in enumerate(paths):
+        if path.protected:
+            continue
+        for k, (expected, frame) in enumerate(zip(path.tokens, path.frames)):
+            rows.append(np.asarray(frame.hidden, dtype=np.float32))
+            targets.append(int(expected))
+            owners.append((pi, k))
+    fused = {}
+    minimum = float("inf")
+    if rows:
+        deadline.check()
+        m, a, _ = readout_margin(gpu, weight, bias, V, width, np.stack(rows), np.asarray(targets), device)
+        minimum = float(np.min(m))
+        for (pi, k), am in zip(owners, a):
+            fused[(pi, k)] = int(am)
+    maximum = 0.0
+    scaled = 0.0
+    preserved = True
+    repaired = True
+    calls = len(rows)
+    generations, certificates = [], []
+    for pi, path in enumerate(paths):
+        matched = True
+        tokens: list[int] = []
+        stopped = False
+        for k, (expected, frame) in enumerate(zip(path.tokens, path.frames)):
+            if path.protected:
+                deadline.check()
+                scores = model.readout(gpu, frame.hidden, device)
+                calls += 1
+                change = np.abs(frame.logits.astype(np.float64) - scores.astype(np.float64))
+                maximum = max(maximum, float(change.max()))
+                scaled = max(scaled, float((change / (1.0 + np.abs(frame.logits.astype(np.float64)))).max()))
+                actual = argmax(scores) if matched else None
+            else:
+                actual = fused[(pi, k)] if matched else None
+            if matched:
+                tokens.append(actual)
+                stopped = actual in stop
+                matched = actual == int(expected)
+        if path.protected:
+            preserved &= matched
+        else:
+            repaired &= matched
+        correct = matched and stopped and path.answer_matches
+        if not path.protected:
+            repaired &= correct
+        generations.append(Generation(tokens, stopped))
+        certificates.append(matched)
+    accepted = minimum >= margin and scaled <= tolerance and preserved and repaired
+    return Verification("native_readout_on_observed_prefixes", minimum, maximum, scaled, certificates, generations,
+                        preserved, repaired, calls, 0, accepted)
+
+
+class CompactReadout:
+    """src/diagnosis.rs:608-666: z = z0 + F ((R - I) x) per observation, on the
+    device with the f32 matvec exactly as the reference evaluates it."""
+
+    def __init__(self, gpu: Gpu, images: list[np.ndarray], baseline: list[np.ndarray],
+                 coordinates: list[np.ndarray]):
+        rank = len(images)
+        vocab = len(images[0])
+        if not (len(baseline) == len(coordinates) and all(len(z) == vocab for z in baseline)):
+            raise ValueError("check the baseline scores and observation count of the compact readout")
+        rows = np.stack([np.asarray(im, dtype=np.float32) for im in images], axis=1)  # [vocab, rank]
+        self.image = gpu.upload_f32(rows)
+        self.baseline = [gpu.upload_f32(z) for z in baseline]
+        self.coordinates = np.stack([np.asarray(c, dtype=np.float64) for c in coordinates], axis=1)  # [rank, n]
+        self.vocabulary = vocab
+        self.rank = rank
+
+    def evaluate(self, gpu: Gpu, rotation: np.ndarray, deadline: Deadline) -> list[np.ndarray]:
+        rank = rotation.shape[0]
+        delta = (rotation - np.eye(rank)) @ self.coordinates
+        out = []
+        for i, base in enumerate(self.baseline):
+            deadline.check()
+            coefficients = gpu.upload_f32(delta[:, i].astype(np.float32))
+            scores = gpu.read(gpu.linear(coefficients, self.image, base, self.vocabulary, rank))
+            if not np.all(np.isfinite(scores)):
+                raise ValueError("check the finite scores of the compact readout")
+            out.append(scores)
+        return out
+
+
+__all__ = [
+    "argmax", "other", "minimum_margin", "prefill", "generate_frames", "generate", "Generation", "ObservedPath",
+    "Verification", "verify_cached", "CompactReadout", "readout_margin", "Deadline", "BudgetExpired",
+]

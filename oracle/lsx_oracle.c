@@ -1,0 +1,413 @@
+/*
+ * lsx_oracle.c -- TEST INFRASTRUCTURE ONLY (see lsx_oracle.h).
+ *
+ * CPU restatement of the reference's decode and readout-validation path.  Each
+ * function names the reference lines it follows.  Products of stored weights and
+ * f32 activations are formed exactly in f64 and summed in f64; vectors between
+ * ops are rounded to f32 as the reference's device tensors are.
+ */
+#include "lsx_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+const char* lsxo_version(void) { return "lsx-oracle 1"; }
+
+static inline float bf16_to_f32(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* IEEE binary16 -> f32, exact (half 2.7.1's widening, Cargo.lock of the reference). */
+static inline float f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu;
+    uint32_t man = h & 0x3ffu;
+    uint32_t u;
+    if (exp == 0) {
+        if (man == 0) {
+            u = sign;
+        } else { /* subnormal: renormalise */
+            int e = -1;
+            do { man <<= 1; ++e; } while (!(man & 0x400u));
+            man &= 0x3ffu;
+            u = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
+        }
+    } else if (exp == 31) {
+        u = sign | 0x7f800000u | (man << 13);
+    } else {
+        u = sign | ((exp + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static inline double load(const void* m, int kind, size_t i) {
+    switch (kind) {
+    case LSXO_F32: return (double)((const float*)m)[i];
+    case LSXO_F16: return (double)f16_to_f32(((const uint16_t*)m)[i]);
+    default: return (double)bf16_to_f32(((const uint16_t*)m)[i]);
+    }
+}
+
+/* kernels/ops.py:7-11 */
+void lsxo_take_row(const void* matrix, int kind, size_t row, size_t width, float* out) {
+    for (size_t i = 0; i < width; ++i) out[i] = (float)load(matrix, kind, row * width + i);
+}
+
+static double dot_row(const void* matrix, int kind, size_t row, const float* x, size_t cols) {
+    double s = 0.0;
+    size_t base = row * cols;
+    if (kind == LSXO_BF16) {
+        const uint16_t* w = (const uint16_t*)matrix + base;
+        for (size_t c = 0; c < cols; ++c) s += (double)bf16_to_f32(w[c]) * (double)x[c];
+    } else if (kind == LSXO_F32) {
+        const float* w = (const float*)matrix + base;
+        for (size_t c = 0; c < cols; ++c) s += (double)w[c] * (double)x[c];
+    } else {
+        const uint16_t* w = (const uint16_t*)matrix + base;
+        for (size_t c = 0; c < cols; ++c) s += (double)f16_to_f32(w[c]) * (double)x[c];
+    }
+    return s;
+}
+
+/* kernels/ops.py:14-28 (f64 accumulation of exact products) */
+void lsxo_matvec(const void* matrix, int kind, const float* x, const float* bias, size_t rows,
+                 size_t cols, float* out, int threads) {
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#pragma omp parallel for num_threads(threads) schedule(static) if (rows * cols > (1u << 16))
+#else
+    (void)threads;
+#endif
+    for (long r = 0; r < (long)rows; ++r) {
+        double s = dot_row(matrix, kind, (size_t)r, x, cols);
+        if (bias) s += (double)bias[r];
+        out[r] = (float)s;
+    }
+}
+
+/* kernels/ops.py:31-45 */
+void lsxo_norm(const float* x, const float* gain, const float* bias, size_t groups, size_t width,
+               float epsilon, int center, float* out) {
+    for (size_t g = 0; g < groups; ++g) {
+        const float* row = x + g * width;
+        double mean = 0.0;
+        if (center) {
+            for (size_t i = 0; i < width; ++i) mean += row[i];
+            mean /= (double)width;
+        }
+        double sq = 0.0;
+        for (size_t i = 0; i < width; ++i) {
+            double d = (double)row[i] - mean;
+            sq += d * d;
+        }
+        double inverse = 1.0 / sqrt(sq / (double)width + (double)epsilon);
+        for (size_t i = 0; i < width; ++i) {
+            double y = ((double)row[i] - mean) * inverse * (double)gain[i];
+            if (bias) y += (double)bias[i];
+            out[g * width + i] = (float)y;
+        }
+    }
+}
+
+/* kernels/ops.py:48-66; phase = position * theta^(-2 pair / rotary) in f64 as
+   tests/qwen_reference.rs:61-76 and tests/gpu.rs:118-131 state it. */
+void lsxo_rope(const float* x, size_t heads, size_t dim, double theta, size_t rotary,
+               int interleaved, size_t position, float* out) {
+    size_t width = heads * dim;
+    memcpy(out, x, width * sizeof(float));
+    size_t half = rotary / 2;
+    for (size_t h = 0; h < heads; ++h) {
+        for (size_t pair = 0; pair < half; ++pair) {
+            size_t a, b;
+            if (interleaved) {
+                a = h * dim + 2 * pair;
+                b = a + 1;
+            } else {
+                a = h * dim + pair;
+                b = a + half;
+            }
+            double phase = (double)position / pow(theta, 2.0 * (double)pair / (double)rotary);
+            double s = sin(phase), c = cos(phase);
+            double xa = x[a], xb = x[b];
+            out[a] = (float)(xa * c - xb * s);
+            out[b] = (float)(xb * c + xa * s);
+        }
+    }
+}
+
+/* kernels/ops.py:69-73 */
+void lsxo_cache_write(const float* k, const float* v, float* keys, float* values, size_t position,
+                      size_t width) {
+    memcpy(keys + position * width, k, width * sizeof(float));
+    memcpy(values + position * width, v, width * sizeof(float));
+}
+
+/* kernels/ops.py:76-101 with f64 scores and softmax (tests/gpu.rs:210-239) */
+void lsxo_attention(const float* q, const float* keys, const float* values, size_t position,
+                    size_t qheads, size_t kvheads, size_t dim, double scale, float* out) {
+    size_t width = kvheads * dim;
+    size_t ratio = qheads / kvheads;
+    double* scores = (double*)malloc((position + 1) * sizeof(double));
+    for (size_t head = 0; head < qheads; ++head) {
+        size_t kv = head / ratio;
+        double m = -INFINITY;
+        for (size_t t = 0; t <= position; ++t) {
+            double s = 0.0;
+            for (size_t d = 0; d < dim; ++d)
+                s += (double)q[head * dim + d] * (double)keys[t * width + kv * dim + d];
+            s *= scale;
+            scores[t] = s;
+            if (s > m) m = s;
+        }
+        double denom = 0.0;
+        for (size_t t = 0; t <= position; ++t) {
+            scores[t] = exp(scores[t] - m);
+            denom += scores[t];
+        }
+        for (size_t d = 0; d < dim; ++d) {
+            double acc = 0.0;
+            for (size_t t = 0; t <= position; ++t)
+                acc += scores[t] * (double)values[t * width + kv * dim + d];
+            out[head * dim + d] = (float)(acc / denom);
+        }
+    }
+    free(scores);
+}
+
+/* kernels/ops.py:104-116 */
+void lsxo_gated(const float* gate, const float* up, size_t n, int kind, float* out) {
+    for (size_t i = 0; i < n; ++i) {
+        double x = gate[i], a;
+        switch (kind) {
+        case 0: a = x / (1.0 + exp(-x)); break;
+        case 1: a = 0.5 * x * (1.0 + erf(x * 0.7071067811865476)); break;
+        case 2: a = x > 0.0 ? x : 0.0; break;
+        default: a = 0.5 * x * (1.0 + tanh(0.7978845608028654 * (x + 0.044715 * x * x * x))); break;
+        }
+        out[i] = (float)(a * (double)up[i]);
+    }
+}
+
+/* kernels/ops.py:119-122; the reference compiles without FMA contraction
+   (kernels/compile.py:35), so the product and the sum round separately. */
+void lsxo_combine(const float* x, const float* y, float factor, size_t n, float* out) {
+    for (size_t i = 0; i < n; ++i) {
+        volatile float p = factor * y[i];
+        out[i] = x[i] + p;
+    }
+}
+
+/* kernels/ops.py:125-135 */
+void lsxo_plane_rotation(const float* h, const float* u, const float* v, float cosine_minus_one,
+                         float sine, size_t width, float* out) {
+    double hu = 0.0, hv = 0.0;
+    for (size_t i = 0; i < width; ++i) {
+        hu += (double)h[i] * (double)u[i];
+        hv += (double)h[i] * (double)v[i];
+    }
+    double a = cosine_minus_one, b = sine;
+    for (size_t i = 0; i < width; ++i)
+        out[i] = (float)((double)h[i] + (double)u[i] * (a * hu + b * hv) +
+                         (double)v[i] * (a * hv - b * hu));
+}
+
+/* src/rotation.rs:50-53 */
+void lsxo_plane_coefficients(double t, double* a, double* b) {
+    *a = -2.0 * t * t / (1.0 + t * t);
+    *b = 2.0 * t / (1.0 + t * t);
+}
+
+/* src/rotation.rs:54-68 */
+void lsxo_plane_apply(const double* u, const double* v, double tangent, size_t width,
+                      const double* h, double* out) {
+    double a, b;
+    lsxo_plane_coefficients(tangent, &a, &b);
+    double x = 0.0, y = 0.0;
+    for (size_t i = 0; i < width; ++i) {
+        x += u[i] * h[i];
+        y += v[i] * h[i];
+    }
+    for (size_t i = 0; i < width; ++i) out[i] = h[i] + u[i] * (a * x + b * y) + v[i] * (a * y - b * x);
+}
+
+/* src/response.rs:61-77 */
+void lsxo_subspace_apply(const double* basis, const double* transform, size_t rank, size_t width,
+                         const double* h, double* out) {
+    double* x = (double*)calloc(rank, sizeof(double));
+    double* delta = (double*)calloc(rank, sizeof(double));
+    for (size_t i = 0; i < rank; ++i)
+        for (size_t j = 0; j < width; ++j) x[i] += basis[i * width + j] * h[j];
+    for (size_t i = 0; i < rank; ++i)
+        for (size_t j = 0; j < rank; ++j)
+            delta[i] += (transform[i * rank + j] - (i == j ? 1.0 : 0.0)) * x[j];
+    memcpy(out, h, width * sizeof(double));
+    for (size_t i = 0; i < rank; ++i)
+        for (size_t j = 0; j < width; ++j) out[j] += delta[i] * basis[i * width + j];
+    free(x);
+    free(delta);
+}
+
+/* src/diagnosis.rs:58-70 */
+uint32_t lsxo_argmax(const float* z, size_t n) {
+    size_t best = 0;
+    for (size_t i = 1; i < n; ++i)
+        if (z[i] > z[best]) best = i;
+    return (uint32_t)best;
+}
+
+/* f32::total_cmp key: larger key <=> larger in IEEE total order. */
+static inline int64_t total_key(float f) {
+    int32_t i;
+    memcpy(&i, &f, 4);
+    return (int64_t)(i ^ (int32_t)(((uint32_t)(i >> 31)) >> 1));
+}
+
+/* src/diagnosis.rs:71-80: max_by(total_cmp).then(b.cmp(a)) keeps the lowest index. */
+size_t lsxo_other(const float* z, size_t n, uint32_t target) {
+    size_t best = (size_t)-1;
+    int64_t key = 0;
+    for (size_t i = 0; i < n; ++i) {
+        if (i == target) continue;
+        int64_t k = total_key(z[i]);
+        if (best == (size_t)-1 || k > key) {
+            best = i;
+            key = k;
+        }
+    }
+    return best;
+}
+
+/* src/diagnosis.rs:490-492 */
+double lsxo_minimum_margin(const float* z, size_t n, uint32_t target) {
+    return (double)z[target] - (double)z[lsxo_other(z, n, target)];
+}
+
+/* src/attribution.rs:49-60 */
+double lsxo_loss(const float* z, size_t n, uint32_t target) {
+    double top = -INFINITY;
+    for (size_t i = 0; i < n; ++i)
+        if ((double)z[i] > top) top = z[i];
+    double s = 0.0;
+    for (size_t i = 0; i < n; ++i) s += exp((double)z[i] - top);
+    return top + log(s) - (double)z[target];
+}
+
+/* src/model.rs:620-631 */
+void lsxo_embedding(const lsxo_model* m, uint32_t token, float* out) {
+    lsxo_take_row(m->embedding, m->embedding_kind, token, m->hidden, out);
+    if (m->embedding_scale != 1.0f) lsxo_combine(out, out, m->embedding_scale - 1.0f, m->hidden, out);
+}
+
+/* src/model.rs:729-853 */
+void lsxo_decode(const lsxo_model* m, size_t position, const float* residual_in, float* hidden,
+                 float* logits, int threads) {
+    size_t H = m->hidden, qw = m->qheads * m->head_dim, kw = m->kvheads * m->head_dim;
+    size_t I = m->intermediate;
+    size_t big = qw > H ? qw : H;
+    if (I > big) big = I;
+    float* residual = (float*)malloc(H * sizeof(float));
+    float* norm = (float*)malloc(big * sizeof(float));
+    float* q = (float*)malloc(qw * sizeof(float));
+    float* k = (float*)malloc(kw * sizeof(float));
+    float* v = (float*)malloc(kw * sizeof(float));
+    float* t = (float*)malloc(big * sizeof(float));
+    float* mixed = (float*)malloc(qw * sizeof(float));
+    float* gate = (float*)malloc(I * sizeof(float));
+    float* up = (float*)malloc(I * sizeof(float));
+    float* feature = (float*)malloc(I * sizeof(float));
+    float* proj = (float*)malloc(H * sizeof(float));
+    memcpy(residual, residual_in, H * sizeof(float));
+    for (size_t l = 0; l < m->layers; ++l) {
+        const lsxo_block* b = &m->blocks[l];
+        lsxo_norm(residual, b->input_gain, b->input_bias, 1, H, m->epsilon, m->center, norm);
+        lsxo_matvec(b->q, b->kind, norm, b->q_bias, qw, H, q, threads);
+        lsxo_matvec(b->k, b->kind, norm, b->k_bias, kw, H, k, threads);
+        lsxo_matvec(b->v, b->kind, norm, b->v_bias, kw, H, v, threads);
+        if (b->q_gain) {
+            lsxo_norm(q, b->q_gain, NULL, m->qheads, m->head_dim, m->qk_epsilon, 0, t);
+            memcpy(q, t, qw * sizeof(float));
+        }
+        if (b->k_gain) {
+            lsxo_norm(k, b->k_gain, NULL, m->kvheads, m->head_dim, m->qk_epsilon, 0, t);
+            memcpy(k, t, kw * sizeof(float));
+        }
+        if (m->rotary > 0) {
+            lsxo_rope(q, m->qheads, m->head_dim, m->theta, m->rotary, m->interleaved, position, t);
+            memcpy(q, t, qw * sizeof(float));
+            lsxo_rope(k, m->kvheads, m->head_dim, m->theta, m->rotary, m->interleaved, position, t);
+            memcpy(k, t, kw * sizeof(float));
+        }
+        lsxo_cache_write(k, v, b->keys, b->values, position, kw);
+        lsxo_attention(q, b->keys, b->values, position, m->qheads, m->kvheads, m->head_dim,
+                       m->score_scale, mixed);
+        lsxo_matvec(b->o, b->kind, mixed, b->o_bias, H, qw, proj, threads);
+        lsxo_combine(residual, proj, 1.0f, H, residual);
+        lsxo_norm(residual, b->post_gain, b->post_bias, 1, H, m->epsilon, m->center, norm);
+        lsxo_matvec(b->gate, b->kind, norm, b->gate_bias, I, H, gate, threads);
+        lsxo_matvec(b->up, b->kind, norm, b->up_bias, I, H, up, threads);
+        lsxo_gated(gate, up, I, m->activation, feature);
+        lsxo_matvec(b->down, b->kind, feature, b->down_bias, H, I, proj, threads);
+        lsxo_combine(residual, proj, 1.0f, H, residual);
+    }
+    lsxo_norm(residual, m->final_gain, m->final_bias, 1, H, m->epsilon, m->center, hidden);
+    if (logits)
+        lsxo_matvec(m->head, m->head_kind, hidden, m->head_bias, m->vocab, H, logits, threads);
+    free(residual); free(norm); free(q); free(k); free(v); free(t); free(mixed);
+    free(gate); free(up); free(feature); free(proj);
+}
+
+/* Blocked readout: stream the head once per block of rows (the reference re-reads it
+   once per row, src/diagnosis.rs:512-537; the result per row is the same). */
+#define ORACLE_ROW_BLOCK 8
+void lsxo_readout_rows(const void* head, int kind, const float* bias, size_t vocab, size_t width,
+                       const float* inputs, size_t n, const uint32_t* targets, double* margin,
+                       uint32_t* argmax, float* target_logit, int threads) {
+    float* z = (float*)malloc(vocab * ORACLE_ROW_BLOCK * sizeof(float));
+#ifdef _OPENMP
+    if (threads <= 0) threads = omp_get_max_threads();
+#else
+    (void)threads;
+#endif
+    for (size_t r0 = 0; r0 < n; r0 += ORACLE_ROW_BLOCK) {
+        size_t rb = n - r0 < ORACLE_ROW_BLOCK ? n - r0 : ORACLE_ROW_BLOCK;
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(threads) schedule(static)
+#endif
+        for (long j = 0; j < (long)vocab; ++j) {
+            double acc[ORACLE_ROW_BLOCK] = {0};
+            if (kind == LSXO_BF16) {
+                const uint16_t* w = (const uint16_t*)head + (size_t)j * width;
+                for (size_t c = 0; c < width; ++c) {
+                    double wc = (double)bf16_to_f32(w[c]);
+                    for (size_t r = 0; r < rb; ++r) acc[r] += wc * (double)inputs[(r0 + r) * width + c];
+                }
+            } else {
+                for (size_t c = 0; c < width; ++c) {
+                    double wc = load(head, kind, (size_t)j * width + c);
+                    for (size_t r = 0; r < rb; ++r) acc[r] += wc * (double)inputs[(r0 + r) * width + c];
+                }
+            }
+            for (size_t r = 0; r < rb; ++r) {
+                double s = acc[r] + (bias ? (double)bias[j] : 0.0);
+                z[r * vocab + (size_t)j] = (float)s;
+            }
+        }
+        for (size_t r = 0; r < rb; ++r) {
+            const float* zr = z + r * vocab;
+            uint32_t t = targets[r0 + r];
+            if (margin) margin[r0 + r] = lsxo_minimum_margin(zr, vocab, t);
+            if (argmax) argmax[r0 + r] = lsxo_argmax(zr, vocab);
+            if (target_logit) target_logit[r0 + r] = zr[t];
+        }
+    }
+    free(z);
+}
