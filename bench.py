@@ -1,0 +1,443 @@
+"""Benchmark of the B200 decode and readout-validation path.
+
+Headline: decode tok/s of a Qwen3-0.6B-architecture model (random-init bf16,
+seed 7), batch 1, greedy 32 tokens from a 24-token prompt of seeded random ids.
+One bench step is one such generation: 24 prompt tokens and 31 generated tokens
+go through the model one at a time (the reference feeds prompts token by token,
+src/diagnosis.rs:81-99), i.e. 55 decode steps; `value` counts decode steps (tokens
+through the model) per second, device-timed with CUDA events on the library's
+stream.  `e2e` is the same generation through the C ABI call lsx_model_generate
+with host buffers (prompt upload, token and Frame downloads inside the timing).
+
+Second object `readout`: fused readout-margin validation of 4096 RMSNorm'd bf16
+hidden states against lm_head [151936, 1024] with a rank-16 Givens edit; rows/s.
+
+Multi-GPU (torchrun): decode runs as one independent replica per GPU (a batch-1
+stream does not shard); readout validation is row-sharded with a fixed 4096 rows
+per GPU (weak scaling, no data-path collective).  Timing is max over ranks.
+
+--impl reference times the reference's CPU path (the oracle restatement of
+tests/qwen_reference.rs's CPU forward, KV-cached, f64 reductions) on the host
+cores; the reference's Rust crate cannot be built here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+PROMPT, GENERATE = 24, 32
+STEPS_PER_GENERATION = PROMPT + GENERATE - 1
+READOUT_ROWS, VOCAB, HIDDEN, RANK = 4096, 151936, 1024, 16
+METRIC = "decode tok/s (Qwen3-0.6B bs1, % HBM roofline); readout-margin rows/s"
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def decode_bytes_per_step(prompt=PROMPT, generate=GENERATE):
+    """Algorithmic bytes of one decode step averaged over the generation: every
+    bf16 weight once (28 layers x 15,728,640 + lm_head 151936 x 1024) plus the f32
+    KV cache read (positions 0..t) and the new K/V write."""
+    weights = 2 * (28 * 15_728_640 + 151_936 * 1024)
+    steps = prompt + generate - 1
+    kv_read = sum(28 * (t + 1) * 8192 for t in range(steps)) / steps
+    return weights + kv_read + 28 * 8192
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- workload ----
+def build_checkpoint(rank: int) -> Path:
+    from laplacesscissors_b200 import synth
+    d = Path(tempfile.gettempdir()) / f"lsx-bench-qwen3-0.6b-seed7-r{rank}"
+    if not (d / "model.safetensors").exists():
+        synth.make_qwen3_checkpoint(d, synth.qwen3_config(**synth.QWEN3_0_6B), seed=7)
+    return d
+
+
+def readout_inputs():
+    from laplacesscissors_b200 import random_subspace_rotation, synth
+    w = synth.normal_bf16(7, 0, VOCAB * HIDDEN, 0.02)
+    hidden = synth.readout_hidden(7, READOUT_ROWS, HIDDEN)
+    targets = synth.readout_targets(7, READOUT_ROWS, VOCAB)
+    edit = random_subspace_rotation(HIDDEN, RANK, 3.0, seed=7)
+    return w, hidden, targets, edit
+
+
+# ------------------------------------------------------------ CPU legs -----
+def cpu_threads():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def cpu_decode_rate(ckpt: Path, seconds: float = 15.0):
+    """Oracle decode of the same checkpoint and prompt on the host cores."""
+    from laplacesscissors_b200 import synth
+    from oracle import binding as oracle
+    threads = cpu_threads()
+    m = oracle.OracleModel(ckpt, 64, threads=threads)
+    prompt = synth.prompt_tokens(7, PROMPT, VOCAB)
+    m.advance(int(prompt[0]))  # warm-up
+    m.cursor = 0
+    t0 = time.perf_counter()
+    n = 0
+    while n < STEPS_PER_GENERATION and (n < 3 or time.perf_counter() - t0 < seconds):
+        tok = int(prompt[n]) if n < PROMPT else int(np.argmax(z))
+        _, z = m.advance(tok)
+        n += 1
+    dt = time.perf_counter() - t0
+    return n / dt, threads, f"first {n} decode steps of the generation (oracle, f64 reductions)"
+
+
+def cpu_readout_rate(w, hidden, targets, edit, seconds: float = 15.0):
+    from laplacesscissors_b200 import synth
+    from oracle import binding as oracle
+    threads = cpu_threads()
+    rows = 8
+    h = synth.bf16_to_f32(hidden[:rows]).astype(np.float64)
+    edited = np.stack([edit.apply(x) for x in h]).astype(np.float32)
+    t0 = time.perf_counter()
+    done = 0
+    while done == 0 or (time.perf_counter() - t0 < seconds and done < 64):
+        oracle.readout_rows(w, oracle.BF16, None, VOCAB, HIDDEN, edited, targets[:rows], threads)
+        done += rows
+    dt = time.perf_counter() - t0
+    return done / dt, threads, f"{done} rows (oracle readout with the rank-16 edit, f64 accumulation)"
+
+
+# ------------------------------------------------------------ GPU legs -----
+def cuda_timer(gpu):
+    import torch
+    stream = torch.cuda.ExternalStream(gpu.stream())
+
+    def make():
+        e = torch.cuda.Event(enable_timing=True)
+        return e
+    return stream, make
+
+
+def run_decode(gpu, ckpt: Path, steps: int, warmup: int, dist):
+    import ctypes as C
+    import torch
+
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import synth
+    from laplacesscissors_b200._lib import check, lib
+    from laplacesscissors_b200.model import _fp, _up
+    model = lsx.Model.load(ckpt, gpu, 64)
+    assert model.fused
+    prompt = np.ascontiguousarray(synth.prompt_tokens(7, PROMPT, VOCAB), dtype=np.uint32)
+    tokens = np.empty(GENERATE, np.uint32)
+    n = C.c_size_t()
+    stopped = C.c_int()
+
+    def generate(frames_h=None, frames_z=None):
+        check(lib.lsx_model_generate(model.handle, _up(prompt), PROMPT, GENERATE, None, 0, None, _up(tokens),
+                                     C.byref(n), C.byref(stopped), frames_h, frames_z))
+
+    stream, event = cuda_timer(gpu)
+    # Device-timed: the same generation with no frame copies; the graph replays
+    # enqueue back to back and CUDA events bracket K generations.
+    for _ in range(warmup):
+        generate()
+    gpu.synchronize()
+    dist.barrier()
+    start, stop = event(), event()
+    with ClockSampler(gpu.device) as clocks:
+        start.record(stream)
+        for _ in range(steps):
+            generate()
+        stop.record(stream)
+        stop.synchronize()
+    dev_ms = start.elapsed_time(stop)
+    dist.barrier()
+    # End to end through the C ABI with host buffers: prompt in, tokens and the
+    # Frame (hidden + logits) of every generated token out.
+    hid = np.empty((GENERATE, HIDDEN), np.float32)
+    lg = np.empty((GENERATE, VOCAB), np.float32)
+    for _ in range(max(1, warmup)):
+        generate(_fp(hid), _fp(lg))
+    gpu.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        generate(_fp(hid), _fp(lg))
+    e2e_s = time.perf_counter() - t0
+    first_tokens = [int(t) for t in tokens[:8]]
+    return {"dev_ms": dev_ms, "e2e_s": e2e_s, "clocks": clocks.summary(), "tokens": first_tokens,
+            "h2d": prompt.nbytes, "d2h": tokens.nbytes + hid.nbytes + lg.nbytes, "model": model}
+
+
+def run_readout(gpu, inputs, steps: int, warmup: int, dist):
+    import ctypes as C
+    import torch
+
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import DeviceRotation
+    from laplacesscissors_b200._lib import BF16, check, lib
+    w, hidden, targets, edit = inputs
+    weight = gpu.upload_raw(w, BF16)
+    rot = DeviceRotation.upload_edit(gpu, edit, HIDDEN)
+    # Device-resident inputs for the device-timed leg.
+    d_hidden = gpu.upload_raw(hidden, BF16)
+    d_targets = torch.from_numpy(targets.astype(np.int32)).cuda(gpu.device)
+    d_out = torch.empty(READOUT_ROWS * 16, dtype=torch.uint8, device=f"cuda:{gpu.device}")
+    ws_bytes = lib.lsx_readout_workspace_bytes(VOCAB, HIDDEN, READOUT_ROWS, rot.handle)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=f"cuda:{gpu.device}")
+    base = d_out.data_ptr()
+    torch.cuda.synchronize(gpu.device)
+
+    def step():
+        check(lib.lsx_readout_margin_device(gpu.handle, weight.handle, None, VOCAB, HIDDEN,
+                                            C.c_void_p(d_hidden.data_ptr), BF16, READOUT_ROWS,
+                                            C.c_void_p(d_targets.data_ptr()), rot.handle, C.c_void_p(base),
+                                            C.c_void_p(base + READOUT_ROWS * 8), C.c_void_p(base + READOUT_ROWS * 12),
+                                            C.c_void_p(ws.data_ptr()), ws_bytes))
+
+    stream, event = cuda_timer(gpu)
+    for _ in range(warmup):
+        step()
+    gpu.synchronize()
+    dist.barrier()
+    start, stop = event(), event()
+    with ClockSampler(gpu.device) as clocks:
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        stop.record(stream)
+        stop.synchronize()
+    dev_ms = start.elapsed_time(stop)
+    dist.barrier()
+    from laplacesscissors_b200 import diagnosis
+    for _ in range(max(1, warmup)):
+        diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        margin, amax, _ = diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
+    e2e_s = time.perf_counter() - t0
+    return {"dev_ms": dev_ms, "e2e_s": e2e_s, "clocks": clocks.summary(), "h2d": hidden.nbytes + targets.nbytes,
+            "d2h": READOUT_ROWS * 16, "argmax0": int(amax[0])}
+
+
+class Dist:
+    def __init__(self, world: int, local: int):
+        self.world = world
+        self.pg = None
+        if world > 1:
+            import torch
+            import torch.distributed as td
+            from datetime import timedelta
+            torch.cuda.set_device(local)
+            td.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+            self.pg = td
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, local, world = env_rank()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    if args.warmup < 3:
+        args.warmup = 3
+    import laplacesscissors_b200 as lsx
+    dist = Dist(world, local)
+    gpu = lsx.Gpu(local)
+    peaks = measured_peaks()
+    ckpt = build_checkpoint(local)
+    dec = run_decode(gpu, ckpt, args.steps, args.warmup, dist)
+    inputs = readout_inputs()
+    ro = run_readout(gpu, inputs, args.steps, args.warmup, dist)
+    dec_ms = dist.max(dec["dev_ms"]) / args.steps
+    dec_e2e = dist.max(dec["e2e_s"]) / args.steps
+    ro_ms = dist.max(ro["dev_ms"]) / args.steps
+    ro_e2e = dist.max(ro["e2e_s"]) / args.steps
+    if rank == 0:
+        step_s = dec_ms / 1e3 / STEPS_PER_GENERATION
+        bytes_step = decode_bytes_per_step()
+        achieved = bytes_step / step_s / 1e9
+        flops = 2.0 * READOUT_ROWS * VOCAB * HIDDEN
+        tflops = flops / (ro_ms / 1e3) / 1e12
+        line = {
+            "metric": METRIC,
+            "value": world * STEPS_PER_GENERATION / (dec_ms / 1e3),
+            "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dec_ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16 weights, f32 activations and KV (f32 accumulate)",
+            "data": "synthetic: random-init Qwen3-0.6B architecture (seed 7), 24 random prompt ids",
+            "config": {"workload": "Qwen3-0.6B bs1 greedy decode, 24-token prompt + 32 tokens",
+                       "decode_steps_per_step": STEPS_PER_GENERATION, "batch": 1, "kv_cache": "f32",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "weights 1.19 GB per token > 126 MB L2 (no flush needed)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "scope": "whole decode step (2 + 5x28 kernels), algorithmic bytes "
+                                  f"{bytes_step / 1e9:.4f} GB/step, {peaks['source']} peak"},
+            "e2e": {"value": world * STEPS_PER_GENERATION / dec_e2e, "unit": "tok/s",
+                    "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"]},
+            "clocks": dec["clocks"],
+            "gpu_launches": args.steps * STEPS_PER_GENERATION * (2 + 5 * 28) + args.steps * 5,
+            "readout": {
+                "metric": "readout-margin rows/s", "value": world * READOUT_ROWS / (ro_ms / 1e3), "unit": "rows/s",
+                "ms_per_step": ro_ms,
+                "config": {"workload": "4096 RMSNorm'd bf16 hidden x lm_head [151936, 1024] bf16, rank-16 "
+                                       "Givens edit within 3 degrees, target margin + argmax",
+                           "rows_per_gpu": READOUT_ROWS, "scaling": "weak (row shards)",
+                           "l2": "lm_head 311 MB > L2"},
+                "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
+                             "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "traffic": None,
+                             "scope": "whole validation step (edit image + coefficients + tcgen05 GEMM + "
+                                      f"finalize), 2*4096*151936*1024 flops, {peaks['source']} burst peak"},
+                "e2e": {"value": world * READOUT_ROWS / ro_e2e, "unit": "rows/s", "h2d_bytes_per_step": ro["h2d"],
+                        "d2h_bytes_per_step": ro["d2h"]},
+                "clocks": ro["clocks"],
+            },
+        }
+        if not args.no_cpu_baseline and world == 1:
+            v, cores, sample = cpu_decode_rate(ckpt)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+            rv, rcores, rsample = cpu_readout_rate(*inputs)
+            line["readout"]["cpu_baseline"] = {"value": rv, "unit": "rows/s", "cores": rcores, "kind": "port",
+                                               "sample": rsample}
+        print(json.dumps(line))
+    dist.close()
+
+
+def reference_arm(args, rank, world):
+    """The reference's CPU path on the host cores (oracle restatement), rank 0 only."""
+    if rank != 0:
+        return
+    ckpt = build_checkpoint(0)
+    from laplacesscissors_b200 import synth
+    from oracle import binding as oracle
+    threads = cpu_threads()
+    m = oracle.OracleModel(ckpt, 64, threads=threads)
+    prompt = synth.prompt_tokens(7, PROMPT, VOCAB)
+    per_step = 4  # decode steps per bench step: a bounded sample of the generation
+
+    def one(step):
+        m.cursor = 0
+        for i in range(per_step):
+            m.advance(int(prompt[i]))
+
+    for i in range(args.warmup):
+        one(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one(i)
+    dt = time.perf_counter() - t0
+    v = args.steps * per_step / dt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 weights, f32 activations, f64 reductions", "data": "synthetic",
+        "config": {"workload": "Qwen3-0.6B bs1 greedy decode, 24-token prompt + 32 tokens",
+                   "sample": f"{per_step} decode steps per bench step"},
+        "cpu_baseline": {"kind": "port", "cores": threads, "value": v,
+                         "sample": f"{per_step} oracle decode steps per bench step on {threads} threads"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+if __name__ == "__main__":
+    main()

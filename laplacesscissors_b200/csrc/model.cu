@@ -4,6 +4,7 @@
 // odd head sizes), by the per-op kernels in the exact op order of
 // Model::decode.  Both plans run on the GPU; there is no host compute path.
 #include <dirent.h>
+#include <stdlib.h>
 #include <fcntl.h>
 #include <string.h>
 #include <sys/mman.h>
@@ -995,7 +996,10 @@ int lsx_model_load(lsx_ctx* ctx, const char* root, size_t capacity, lsx_model** 
     m->capacity = capacity;
     for (auto& kv : ck.entries) m->parameters += kv.second.count();
     m->tensors = ck.entries.size();
-    m->fused = fusable(g, ck);
+    // LSX_DECODE_PLAN=ops selects the per-op plan for any checkpoint (used to
+    // cross-check the two plans against each other).
+    const char* plan = getenv("LSX_DECODE_PLAN");
+    m->fused = fusable(g, ck) && !(plan && std::string(plan) == "ops");
     try {
         LSX_TRY(bank_take(m.get(), ck, g.embedding, &m->embedding));
         for (auto& S : g.blocks) {

@@ -210,6 +210,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 *abort_flag = 1;
             }
         }
+        __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {  // ---------------- MMA issuer ----------------
             int stage = 0;
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 *abort_flag = 1;
             }
         }
+        __syncwarp();
     } else {  // ---------------- epilogue warps 2..5 ----------------
         const int quarter = warp & 3;  // TMEM lane group this warp may access
         const int row_local = quarter * 32 + lane;
@@ -581,6 +583,9 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
         for (int k0 = 0; k0 < (int)rank; k0 += kc_max) {
             const int kc = std::min(kc_max, (int)rank - k0);
             const size_t smem = (size_t)kc * width * 4;
+            LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                     "edit image smem attribute");
             edit_image_kernel<<<std::min(ctx->sm_count * 8, (V + 7) / 8), 256, smem, s>>>(
                 (const __nv_bfloat16*)weight->data, V, H, dbasis, (int)rank, k0, kc, ext_b, (int)L.ext_k);
             LSX_CUDA(cudaGetLastError(), "edit image");

@@ -372,11 +372,11 @@ def joint_fn(basis, transform):
 
 
 def tiny_decode(out_dir: Path) -> dict:
-    config = synth.qwen3_config(hidden=64, layers=2, heads=4, kv_heads=2, head_dim=16, intermediate=128, vocab=256,
+    config = synth.qwen3_config(hidden=128, layers=2, heads=2, kv_heads=1, head_dim=64, intermediate=192, vocab=512,
                                 tie=True, theta=1e6, eps=1e-6, max_positions=64)
     root = synth.make_qwen3_checkpoint(out_dir / "tiny_qwen3", config, seed=11, std=0.15, gain_std=0.1)
     model = RefModel(load_tensors(root / "model.safetensors"), qwen_graph(config), 32)
-    prompt = [int(t) for t in synth.prompt_tokens(11, 5, 256)]
+    prompt = [int(t) for t in synth.prompt_tokens(11, 5, config["vocab_size"])]
     hiddens, logits, tokens = [], [], []
     frame = None
     for tok in prompt:  # prefill (src/diagnosis.rs:81-99)
@@ -390,12 +390,13 @@ def tiny_decode(out_dir: Path) -> dict:
             break
         frame = model.decode(model.embedding(tok))
     rng = np.random.default_rng(5)
-    u = rng.standard_normal(64)
+    width = config["hidden_size"]
+    u = rng.standard_normal(width)
     u /= np.linalg.norm(u)
-    v = rng.standard_normal(64)
+    v = rng.standard_normal(width)
     v -= (v @ u) * u
     v /= np.linalg.norm(v)
-    q, _ = np.linalg.qr(rng.standard_normal((64, 4)))
+    q, _ = np.linalg.qr(rng.standard_normal((width, 4)))
     basis = q.T.copy()
     th = 0.3
     R = np.eye(4)

@@ -1,0 +1,134 @@
+"""Fused readout-margin validation (tcgen05 kernel) against the oracle:
+margins within tolerance, argmax bit-exact except at near-ties (|margin| < 1e-3),
+over odd shapes, bf16 and f32 hidden states, plane and joint edits, and the
+readout-validation workload at full size on a sample of rows."""
+import numpy as np
+import pytest
+
+import laplacesscissors_b200 as lsx
+from conftest import GOLDEN
+from laplacesscissors_b200 import DeviceRotation, ReadoutRotation, diagnosis, synth
+from laplacesscissors_b200._lib import BF16
+
+pytestmark = pytest.mark.gpu
+
+
+def check_rows(margin, amax, tl, ref, tol=2e-3):
+    m_ref, a_ref, t_ref = ref
+    near = np.abs(m_ref) < 1e-3
+    assert np.all(np.isfinite(margin))
+    assert np.array_equal(amax[~near], a_ref[~near]), np.nonzero(amax != a_ref)[0][:8]
+    assert np.all(np.abs(margin - m_ref) <= tol * (1 + np.abs(m_ref)))
+    assert np.all(np.abs(tl.astype(np.float64) - t_ref) <= tol * (1 + np.abs(t_ref)))
+
+
+def problem(V, H, n, seed=3, std=0.02):
+    w = synth.normal_bf16(seed, 0, V * H, std)
+    hidden = synth.readout_hidden(seed, n, H)
+    targets = synth.readout_targets(seed, n, V)
+    return w, hidden, targets
+
+
+@pytest.mark.parametrize("V,H,n", [(1000, 256, 300), (517, 64, 129), (256, 128, 128), (4099, 1024, 257)])
+def test_margin_small_shapes_bf16(gpu, oracle, V, H, n):
+    w, hidden, targets = problem(V, H, n)
+    weight = gpu.upload_raw(w, BF16)
+    margin, amax, tl = diagnosis.readout_margin(gpu, weight, None, V, H, hidden, targets)
+    ref = oracle.readout_rows(w, oracle.BF16, None, V, H, synth.bf16_to_f32(hidden), targets)
+    check_rows(margin, amax, tl, ref, 1e-5)
+
+
+def test_margin_f32_hidden_and_bias(gpu, oracle):
+    V, H, n = 3001, 512, 200
+    w, _, targets = problem(V, H, n)
+    hidden = synth.normal_f32(5, 9, n * H).reshape(n, H)
+    bias = synth.normal_f32(5, 10, V, 0.5)
+    weight = gpu.upload_raw(w, BF16)
+    margin, amax, tl = diagnosis.readout_margin(gpu, weight, gpu.upload_f32(bias), V, H, hidden, targets)
+    ref = oracle.readout_rows(w, oracle.BF16, bias, V, H, hidden, targets)
+    check_rows(margin, amax, tl, ref, 1e-5)
+
+
+@pytest.mark.parametrize("kind", ["plane", "joint"])
+def test_margin_with_edits(gpu, oracle, kind):
+    V, H, n = 2053, 256, 160
+    w, hidden, targets = problem(V, H, n)
+    h32 = synth.bf16_to_f32(hidden)
+    if kind == "plane":
+        rng = np.random.default_rng(1)
+        u = rng.standard_normal(H)
+        u /= np.linalg.norm(u)
+        v = rng.standard_normal(H)
+        v -= (v @ u) * u
+        v /= np.linalg.norm(v)
+        spec = ReadoutRotation(u, v, 0.35)
+    else:
+        spec = lsx.random_subspace_rotation(H, 16, 3.0, seed=4)
+    edited = np.stack([spec.apply(h) for h in h32.astype(np.float64)]).astype(np.float32)
+    ref = oracle.readout_rows(w, oracle.BF16, None, V, H, edited, targets)
+    weight = gpu.upload_raw(w, BF16)
+    rot = DeviceRotation.upload_edit(gpu, spec, H)
+    for h in (hidden, h32):  # bf16 rows, and the same rows as f32 (hi/lo planes)
+        margin, amax, tl = diagnosis.readout_margin(gpu, weight, None, V, H, h, targets, rot)
+        check_rows(margin, amax, tl, ref, 1e-5)
+
+
+def test_ties_resolve_to_lowest_index(gpu, oracle):
+    """Duplicate vocab rows produce exact ties: first argmax, lowest-index competitor."""
+    V, H, n = 600, 64, 130
+    w, hidden, _ = problem(V, H, n)
+    w = w.reshape(V, H)
+    w[300:600] = w[0:300]  # rows j and j + 300 give equal logits
+    w = w.reshape(-1)
+    ref_in = synth.bf16_to_f32(hidden)
+    targets = np.zeros(n, np.uint32)
+    for i in range(n):
+        z = oracle.matvec(w, oracle.BF16, ref_in[i], None, V, H)
+        targets[i] = int(np.argsort(z)[-3]) % 300 + (300 if i % 2 else 0)
+    weight = gpu.upload_raw(w, BF16)
+    margin, amax, tl = diagnosis.readout_margin(gpu, weight, None, V, H, hidden, targets)
+    m_ref, a_ref, t_ref = oracle.readout_rows(w, oracle.BF16, None, V, H, ref_in, targets)
+    assert np.array_equal(amax, a_ref)
+    assert np.all(amax < 300)
+    assert np.allclose(margin, m_ref, atol=1e-6)
+
+
+def test_rejects_bad_arguments(gpu):
+    weight = gpu.upload_raw(synth.normal_bf16(1, 0, 100 * 64), BF16)
+    with pytest.raises(lsx.LsxError):
+        diagnosis.readout_margin(gpu, weight, None, 100, 64, np.zeros((2, 64), np.float32), np.array([0, 100]))
+    with pytest.raises(lsx.LsxError):
+        diagnosis.readout_margin(gpu, weight, None, 101, 64, np.zeros((2, 64), np.float32), np.array([0, 1]))
+
+
+def test_readout_validation_workload_full_size(gpu, oracle):
+    """4096 RMSNorm'd bf16 hidden states x lm_head [151936, 1024] bf16 with a rank-16
+    Givens edit (angles within 3 degrees); rows sampled for the oracle."""
+    V, H, n = 151936, 1024, 4096
+    w, hidden, targets = problem(V, H, n, seed=7)
+    spec = lsx.random_subspace_rotation(H, 16, 3.0, seed=7)
+    weight = gpu.upload_raw(w, BF16)
+    rot = DeviceRotation.upload_edit(gpu, spec, H)
+    margin, amax, tl = diagnosis.readout_margin(gpu, weight, None, V, H, hidden, targets, rot)
+    sample = np.arange(0, n, 97)
+    h = synth.bf16_to_f32(hidden[sample]).astype(np.float64)
+    edited = np.stack([spec.apply(x) for x in h]).astype(np.float32)
+    ref = oracle.readout_rows(w, oracle.BF16, None, V, H, edited, targets[sample])
+    check_rows(margin[sample], amax[sample], tl[sample], ref, 1e-5)
+
+
+def test_verify_cached_on_tiny_model(gpu, oracle, golden_tiny):
+    """verify_cached: target prefixes through the fused kernel, protected prefixes
+    through Model::readout; acceptance as src/diagnosis.rs:562-563."""
+    model = lsx.Model.load(GOLDEN / "tiny_qwen3", gpu, 32)
+    tokens, _, frames = model.generate(golden_tiny["prompt"], 6, frames=True)
+    path_t = diagnosis.ObservedPath(0, False, [int(t) for t in tokens], frames)
+    path_p = diagnosis.ObservedPath(1, True, [int(t) for t in tokens], frames)
+    spec = lsx.random_subspace_rotation(model.hidden_size, 4, 0.01, seed=2)
+    v = diagnosis.verify_cached(model, gpu, [int(tokens[-1])], spec, [path_t, path_p], margin=-100.0,
+                                tolerance=1.0, deadline=diagnosis.Deadline.after(60))
+    assert v.requested_answers_generated and v.protected_sequences_preserved and v.accepted
+    ref = oracle.OracleModel(GOLDEN / "tiny_qwen3", 32)
+    margins = [oracle.minimum_margin(ref.readout(f.hidden, spec.apply), int(t)) for f, t in zip(frames, tokens)]
+    assert abs(v.target_min_margin - min(margins)) < 1e-4
+    assert v.readout_calls == 2 * len(frames)
