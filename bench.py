@@ -122,11 +122,11 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- workload ----
-def build_checkpoint(rank: int) -> Path:
+def build_checkpoint(rank: int, layers: int = 28) -> Path:
     from laplacesscissors_b200 import synth
-    d = Path(tempfile.gettempdir()) / f"lsx-bench-qwen3-0.6b-seed7-r{rank}"
+    d = Path(tempfile.gettempdir()) / f"lsx-bench-qwen3-0.6b-seed7-l{layers}-r{rank}"
     if not (d / "model.safetensors").exists():
-        synth.make_qwen3_checkpoint(d, synth.qwen3_config(**synth.QWEN3_0_6B), seed=7)
+        synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(synth.QWEN3_0_6B, layers=layers)), seed=7)
     return d
 
 
@@ -190,7 +190,7 @@ def cuda_timer(gpu):
     return stream, make
 
 
-def run_decode(gpu, ckpt: Path, steps: int, warmup: int, dist):
+def run_decode(gpu, ckpt: Path, steps: int, warmup: int, dist, e2e: bool = True):
     import ctypes as C
     import torch
 
@@ -225,24 +225,28 @@ def run_decode(gpu, ckpt: Path, steps: int, warmup: int, dist):
         stop.synchronize()
     dev_ms = start.elapsed_time(stop)
     dist.barrier()
+    info = model.info()
     # End to end through the C ABI with host buffers: prompt in, tokens and the
     # Frame (hidden + logits) of every generated token out.
     hid = np.empty((GENERATE, HIDDEN), np.float32)
     lg = np.empty((GENERATE, VOCAB), np.float32)
-    for _ in range(max(1, warmup)):
-        generate(_fp(hid), _fp(lg))
-    gpu.synchronize()
-    dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        generate(_fp(hid), _fp(lg))
-    e2e_s = time.perf_counter() - t0
+    e2e_s = float("nan")
+    if e2e:
+        for _ in range(max(1, warmup)):
+            generate(_fp(hid), _fp(lg))
+        gpu.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            generate(_fp(hid), _fp(lg))
+        e2e_s = time.perf_counter() - t0
     first_tokens = [int(t) for t in tokens[:8]]
     return {"dev_ms": dev_ms, "e2e_s": e2e_s, "clocks": clocks.summary(), "tokens": first_tokens,
-            "h2d": prompt.nbytes, "d2h": tokens.nbytes + hid.nbytes + lg.nbytes, "model": model}
+            "h2d": prompt.nbytes, "d2h": tokens.nbytes + hid.nbytes + lg.nbytes, "model": model,
+            "graph": int(info.graph), "kernels_per_step": int(info.kernels_per_step)}
 
 
-def run_readout(gpu, inputs, steps: int, warmup: int, dist):
+def run_readout(gpu, inputs, steps: int, warmup: int, dist, e2e: bool = True):
     import ctypes as C
     import torch
 
@@ -283,15 +287,17 @@ def run_readout(gpu, inputs, steps: int, warmup: int, dist):
     dev_ms = start.elapsed_time(stop)
     dist.barrier()
     from laplacesscissors_b200 import diagnosis
-    for _ in range(max(1, warmup)):
-        diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
-    dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        margin, amax, _ = diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
-    e2e_s = time.perf_counter() - t0
+    e2e_s = float("nan")
+    if e2e:
+        for _ in range(max(1, warmup)):
+            diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
+        e2e_s = time.perf_counter() - t0
     return {"dev_ms": dev_ms, "e2e_s": e2e_s, "clocks": clocks.summary(), "h2d": hidden.nbytes + targets.nbytes,
-            "d2h": READOUT_ROWS * 16, "argmax0": int(amax[0])}
+            "d2h": READOUT_ROWS * 16}
 
 
 class Dist:
@@ -330,10 +336,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["all", "decode", "readout"], default="all",
+                    help="profiling aid: run one half only")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling aid: device legs only, no e2e or CPU legs, warm-up as given")
+    ap.add_argument("--layers", type=int, default=28, help="profiling aid: decoder layers of the checkpoint")
     args = ap.parse_args()
     rank, local, world = env_rank()
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.profile:
+        return profile_run(args, local)
     if args.warmup < 3:
         args.warmup = 3
     import laplacesscissors_b200 as lsx
@@ -376,6 +389,7 @@ def main():
             "e2e": {"value": world * STEPS_PER_GENERATION / dec_e2e, "unit": "tok/s",
                     "h2d_bytes_per_step": dec["h2d"], "d2h_bytes_per_step": dec["d2h"]},
             "clocks": dec["clocks"],
+            "decode_graph": dec["graph"],
             "gpu_launches": args.steps * STEPS_PER_GENERATION * (2 + 5 * 28) + args.steps * 5,
             "readout": {
                 "metric": "readout-margin rows/s", "value": world * READOUT_ROWS / (ro_ms / 1e3), "unit": "rows/s",
@@ -401,6 +415,23 @@ def main():
                                                "sample": rsample}
         print(json.dumps(line))
     dist.close()
+
+
+def profile_run(args, local):
+    """Device legs only, for ncu: prints the per-step device times."""
+    import laplacesscissors_b200 as lsx
+    dist = Dist(1, local)
+    gpu = lsx.Gpu(local)
+    out = {"profile": True}
+    if args.workload in ("all", "decode"):
+        dec = run_decode(gpu, build_checkpoint(local, args.layers), args.steps, args.warmup, dist, e2e=False)
+        out["decode_ms_per_generation"] = dec["dev_ms"] / args.steps
+        out["decode_graph"] = dec["graph"]
+        out["kernels_per_step"] = dec["kernels_per_step"]
+    if args.workload in ("all", "readout"):
+        ro = run_readout(gpu, readout_inputs(), args.steps, args.warmup, dist, e2e=False)
+        out["readout_ms_per_step"] = ro["dev_ms"] / args.steps
+    print(json.dumps(out))
 
 
 def reference_arm(args, rank, world):

@@ -138,6 +138,10 @@ typedef struct lsx_model_info {
     uint64_t parameters, tensors;
     uint64_t eos_count;
     uint32_t eos_token_ids[8];
+    uint64_t fused;        /* 1: fused decode engine; 0: per-op kernels */
+    uint64_t graph;        /* 1: the fused step replays a captured CUDA graph */
+    uint64_t kernels_per_step; /* kernel launches of one fused decode step (kernel-chain engine) */
+    uint64_t persistent;   /* 1: one persistent kernel runs each generate/advance call */
 } lsx_model_info;
 
 /* Model::load (src/model.rs:411-529): reads `root`/laplace.graph.json or the HF

@@ -33,7 +33,8 @@ class ModelInfo(C.Structure):
         ("capacity", C.c_uint64), ("position", C.c_uint64), ("query_heads", C.c_uint64),
         ("kv_heads", C.c_uint64), ("head_dim", C.c_uint64), ("intermediate_size", C.c_uint64),
         ("rotary_dim", C.c_uint64), ("parameters", C.c_uint64), ("tensors", C.c_uint64),
-        ("eos_count", C.c_uint64), ("eos_token_ids", C.c_uint32 * 8),
+        ("eos_count", C.c_uint64), ("eos_token_ids", C.c_uint32 * 8), ("fused", C.c_uint64),
+        ("graph", C.c_uint64), ("kernels_per_step", C.c_uint64), ("persistent", C.c_uint64),
     ]
 
 

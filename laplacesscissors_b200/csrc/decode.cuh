@@ -47,6 +47,8 @@ struct DecodeState {
     const float* rot_delta;  // [rank x rank] = R - I
     uint32_t stop[16];
     unsigned int attn_counter[64];
+    unsigned int epoch;  // last publication epoch of the persistent engine's tagged buffers
+    unsigned int pad2;
 };
 
 struct FusedLayer {

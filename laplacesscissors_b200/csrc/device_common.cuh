@@ -74,6 +74,24 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
         : "memory");
 }
 
+// L2 policy for data read exactly once (streamed weights): evict it first so it
+// does not displace small, hot data (norm gains, KV cache, exchange buffers).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// bulk_load with an L2 cache-policy hint.
+__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait until every kernel this one depends on has completed.
 __device__ __forceinline__ void pdl_launch_dependents() {

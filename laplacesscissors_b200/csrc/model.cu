@@ -4,6 +4,7 @@
 // odd head sizes), by the per-op kernels in the exact op order of
 // Model::decode.  Both plans run on the GPU; there is no host compute path.
 #include <dirent.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <fcntl.h>
 #include <string.h>
@@ -22,6 +23,7 @@
 #include <vector>
 
 #include "decode.cuh"
+#include "persistent.cuh"
 #include "device_common.cuh"
 #include "json.h"
 #include "lsx_internal.h"
@@ -544,6 +546,8 @@ struct lsx_model {
     lsx_tensor* embedding = nullptr;
     bool fused = false;
     std::unique_ptr<FusedDecoder> decoder;
+    std::unique_ptr<PersistentDecoder> persistent;  // preferred fused engine when it fits
+    unsigned int epoch = 0;                           // tagged-buffer epoch of the persistent engine
     // Per-op plan work buffers.
     std::vector<lsx_tensor*> work;
     // Host<->device staging for the fused plan.
@@ -566,6 +570,7 @@ lsx_model::~lsx_model() {
         cudaStreamSynchronize(ctx->stream);
     }
     decoder.reset();
+    persistent.reset();
     for (auto& kv : bank) lsx_tensor_free(kv.second);
     for (auto* t : owned) lsx_tensor_free(t);
     for (auto* t : work) lsx_tensor_free(t);
@@ -916,11 +921,18 @@ void fill_rotation(DecodeState* st, const lsx_rotation* r) {
 // state back.
 int run_fused(lsx_model* m, int steps) {
     cudaStream_t s = m->ctx->stream;
-    DecodeState* dev = m->decoder->state();
+    DecodeState* dev = m->persistent ? m->persistent->state() : m->decoder->state();
+    m->host_state->epoch = m->epoch;
     LSX_K(cudaMemcpyAsync(dev, m->host_state, sizeof(DecodeState), cudaMemcpyHostToDevice, s), "state upload");
-    LSX_TRY(m->decoder->enqueue_steps(steps));
+    if (m->persistent) LSX_TRY(m->persistent->run(steps));
+    else LSX_TRY(m->decoder->enqueue_steps(steps));
     LSX_K(cudaMemcpyAsync(m->host_state, dev, sizeof(DecodeState), cudaMemcpyDeviceToHost, s), "state download");
     LSX_K(cudaStreamSynchronize(s), "decode");
+    if (m->persistent) m->epoch = m->host_state->epoch;
+    if (m->host_state->status != 0) {
+        // A failed run may have published epochs it did not report: skip far past them.
+        m->epoch += 1u << 24;
+    }
     if (m->host_state->status != 0)
         return fail(LSX_E_CUDA, "decode kernel reported status " + std::to_string(m->host_state->status));
     return LSX_OK;
@@ -1098,11 +1110,25 @@ int lsx_model_load(lsx_ctx* ctx, const char* root, size_t capacity, lsx_model** 
             c.head_bias = m->head.bias ? (const float*)m->head.bias->data : nullptr;
             c.final_gain = (const float*)m->final_norm.gain->data;
             std::string why;
-            if (FusedDecoder::eligible(c, &why)) {
-                m->decoder.reset(new FusedDecoder);
-                LSX_TRY(m->decoder->build(ctx, c, layers));
-            } else {
-                m->fused = false;
+            const char* engine = getenv("LSX_DECODE_ENGINE");  // "graph" selects the PDL kernel chain
+            const bool want_persistent = !(engine && std::string(engine) == "graph");
+            const bool debug = getenv("LSX_DEBUG") != nullptr;
+            if (want_persistent && PersistentDecoder::eligible(c, ctx, &why)) {
+                m->persistent.reset(new PersistentDecoder);
+                if (m->persistent->build(ctx, c, layers) != LSX_OK) {
+                    if (debug) fprintf(stderr, "[lsx] persistent decode engine not used: %s\n", lsx_last_error());
+                    m->persistent.reset();
+                }
+            } else if (want_persistent && debug) {
+                fprintf(stderr, "[lsx] persistent decode engine not eligible: %s\n", why.c_str());
+            }
+            if (!m->persistent) {
+                if (FusedDecoder::eligible(c, &why)) {
+                    m->decoder.reset(new FusedDecoder);
+                    LSX_TRY(m->decoder->build(ctx, c, layers));
+                } else {
+                    m->fused = false;
+                }
             }
         }
         if (!m->fused) {
@@ -1150,6 +1176,10 @@ int lsx_model_info_get(const lsx_model* m, lsx_model_info* out) {
     out->tensors = m->tensors;
     out->eos_count = std::min<size_t>(8, m->graph.eos.size());
     for (size_t i = 0; i < out->eos_count; ++i) out->eos_token_ids[i] = m->graph.eos[i];
+    out->fused = m->fused ? 1 : 0;
+    out->graph = (m->decoder && m->decoder->supports_graph()) ? 1 : 0;
+    out->kernels_per_step = m->decoder ? (uint64_t)m->decoder->kernels_per_step() : 0;
+    out->persistent = m->persistent ? 1 : 0;
     return LSX_OK;
 }
 

@@ -66,6 +66,12 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// Prefetch a tile of this GPU's memory into L2 (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -176,9 +182,19 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             uint32_t phase = 0;
             int issued = 0;
             bool ok = true;
+            // CTAs that share an lm_head block start it together, so without a
+            // prefetch every K stage of it is a DRAM miss for all of them; warm
+            // L2 one tile ahead instead.
+            if (blockIdx.x < total)
+                for (int kb = 0; kb < p.k_blocks; ++kb)
+                    tma_prefetch_2d(&map_b, kb * RK, (blockIdx.x / p.m_tiles) * RN);
             for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
                 const int m0 = (tile % p.m_tiles) * RM;
                 const int n0 = (tile / p.m_tiles) * RN;
+                const int next = tile + gridDim.x;
+                if (next < total && (next / p.m_tiles) != (tile / p.m_tiles))
+                    for (int kb = 0; kb < p.k_blocks; ++kb)
+                        tma_prefetch_2d(&map_b, kb * RK, (next / p.m_tiles) * RN);
                 for (int kb = 0; kb < k_total; ++kb) {
                     if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
                         ok = false;
@@ -339,7 +355,10 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
 
 // ------------------------------------------------------------ prep kernels --
 // F = W U^T for ranks [k0, k0 + kc), written as split bf16 into the extension
-// block of B: columns [k] = hi(F), [r + k] = hi(F), [2r + k] = lo(F).
+// block of B: columns [k] = hi(F), [r + k] = hi(F), [2r + k] = lo(F).  One lane
+// per vocab row: a warp streams 32 rows chunk by chunk (each 16-byte chunk of a
+// row shares its 128-byte line with the lane's next seven chunks), and every
+// lane reads the same U values, so shared-memory reads are broadcasts.
 __global__ void __launch_bounds__(256) edit_image_kernel(const __nv_bfloat16* __restrict__ W, int V, int H,
                                                          const float* __restrict__ basis, int rank, int k0, int kc,
                                                          __nv_bfloat16* __restrict__ ext_b, int ext_k) {
@@ -347,40 +366,49 @@ __global__ void __launch_bounds__(256) edit_image_kernel(const __nv_bfloat16* __
     for (int i = threadIdx.x; i < kc * H; i += blockDim.x) us[i] = basis[(size_t)k0 * H + i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int j = blockIdx.x * 8 + warp; j < V; j += gridDim.x * 8) {
+    const int warps_total = gridDim.x * (blockDim.x >> 5);
+    for (int base = (blockIdx.x * (blockDim.x >> 5) + warp) * 32; base < V; base += warps_total * 32) {
+        const int j = base + lane;
+        const bool live = j < V;
+        const uint4* row = reinterpret_cast<const uint4*>(W + (size_t)(live ? j : 0) * H);
         float acc[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-        const uint4* row = reinterpret_cast<const uint4*>(W + (size_t)j * H);
-        for (int c = lane; c < H / 8; c += 32) {
-            uint4 w = row[c];
+        for (int c = 0; c < H / 8; ++c) {
+            const uint4 w = __ldg(row + c);
             const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
             float wf[8];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                float2 f = __bfloat1622float2(h2[q]);
+                const float2 f = __bfloat1622float2(h2[q]);
                 wf[2 * q] = f.x;
                 wf[2 * q + 1] = f.y;
             }
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
                 if (k < kc) {
-                    const float* u = us + k * H + c * 8;
+                    const float4 u0 = *reinterpret_cast<const float4*>(us + k * H + c * 8);
+                    const float4 u1 = *reinterpret_cast<const float4*>(us + k * H + c * 8 + 4);
                     float s = acc[k];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) s = fmaf(wf[q], u[q], s);
+                    s = fmaf(wf[0], u0.x, s);
+                    s = fmaf(wf[1], u0.y, s);
+                    s = fmaf(wf[2], u0.z, s);
+                    s = fmaf(wf[3], u0.w, s);
+                    s = fmaf(wf[4], u1.x, s);
+                    s = fmaf(wf[5], u1.y, s);
+                    s = fmaf(wf[6], u1.z, s);
+                    s = fmaf(wf[7], u1.w, s);
                     acc[k] = s;
                 }
             }
         }
+        if (live) {
+            __nv_bfloat16* dst = ext_b + (size_t)j * ext_k;
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            if (k < kc) {
-                float f = warp_allsum(acc[k]);
-                if (lane == 0) {
-                    __nv_bfloat16 hi = __float2bfloat16_rn(f);
-                    __nv_bfloat16 lo = __float2bfloat16_rn(f - __bfloat162float(hi));
-                    __nv_bfloat16* dst = ext_b + (size_t)j * ext_k;
+            for (int k = 0; k < 16; ++k) {
+                if (k < kc) {
+                    const __nv_bfloat16 hi = __float2bfloat16_rn(acc[k]);
+                    const __nv_bfloat16 lo = __float2bfloat16_rn(acc[k] - __bfloat162float(hi));
                     dst[k0 + k] = hi;
                     dst[rank + k0 + k] = hi;
                     dst[2 * rank + k0 + k] = lo;
@@ -586,7 +614,7 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
             LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                      "edit image smem attribute");
-            edit_image_kernel<<<std::min(ctx->sm_count * 8, (V + 7) / 8), 256, smem, s>>>(
+            edit_image_kernel<<<std::min(ctx->sm_count * 2, (V + 255) / 256), 256, smem, s>>>(
                 (const __nv_bfloat16*)weight->data, V, H, dbasis, (int)rank, k0, kc, ext_b, (int)L.ext_k);
             LSX_CUDA(cudaGetLastError(), "edit image");
         }

@@ -27,23 +27,26 @@ def rel_l2(a, b):
 
 
 def load(gpu, root, capacity, plan=None):
-    old = os.environ.get("LSX_DECODE_PLAN")
+    """plan: None (persistent engine), "graph" (PDL kernel chain) or "ops" (per-op kernels)."""
+    keys = {"ops": ("LSX_DECODE_PLAN", "ops"), "graph": ("LSX_DECODE_ENGINE", "graph")}
+    saved = {k: os.environ.get(k) for k in ("LSX_DECODE_PLAN", "LSX_DECODE_ENGINE")}
     if plan:
-        os.environ["LSX_DECODE_PLAN"] = plan
+        os.environ[keys[plan][0]] = keys[plan][1]
     try:
         return lsx.Model.load(root, gpu, capacity)
     finally:
-        if plan:
-            if old is None:
-                del os.environ["LSX_DECODE_PLAN"]
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
             else:
-                os.environ["LSX_DECODE_PLAN"] = old
+                os.environ[k] = v
 
 
-@pytest.mark.parametrize("plan", [None, "ops"])
+@pytest.mark.parametrize("plan", [None, "graph", "ops"])
 def test_tiny_generate_matches_reference_kernels(gpu, golden_tiny, plan):
     model = load(gpu, GOLDEN / "tiny_qwen3", 32, plan)
-    assert model.fused == (plan is None)
+    assert model.fused == (plan != "ops")
+    assert bool(model.info().persistent) == (plan is None)
     tokens, stopped, frames = model.generate(golden_tiny["prompt"], 6, frames=True)
     assert list(map(int, tokens)) == list(map(int, golden_tiny["tokens"]))
     assert not stopped
@@ -64,8 +67,9 @@ def test_tiny_advance_matches_generate_and_oracle(gpu, oracle, golden_tiny):
     assert int(np.argmax(f.logits)) == int(golden_tiny["tokens"][0])
 
 
-def test_fused_and_per_op_plans_agree(gpu):
-    fused = load(gpu, GOLDEN / "tiny_qwen3", 32)
+@pytest.mark.parametrize("engine", [None, "graph"])
+def test_fused_and_per_op_plans_agree(gpu, engine):
+    fused = load(gpu, GOLDEN / "tiny_qwen3", 32, engine)
     ops = load(gpu, GOLDEN / "tiny_qwen3", 32, "ops")
     for t in [3, 77, 500, 12, 9, 9, 1]:
         a = fused.advance(gpu, t)
@@ -98,9 +102,10 @@ def test_edits_leave_hidden_and_match_reference(gpu, golden_tiny):
     close(joint_step.logits, model.readout(gpu, original.hidden, dj), 1e-5)
 
 
-def test_kv_rewind_replays_bit_identically(gpu):
+@pytest.mark.parametrize("engine", [None, "graph"])
+def test_kv_rewind_replays_bit_identically(gpu, engine):
     """tests/model_rotation.rs:273-279."""
-    model = load(gpu, GOLDEN / "tiny_qwen3", 16)
+    model = load(gpu, GOLDEN / "tiny_qwen3", 16, engine)
     model.advance(gpu, 5)
     branch = model.advance(gpu, 7)
     model.rewind(1)
@@ -125,7 +130,7 @@ def test_context_capacity_is_enforced(gpu):
 
 def test_token_path_equals_injected_path(gpu):
     """tests/injection.rs:115-124: feeding the embedding vector reproduces the token path bit-exactly."""
-    for plan in (None, "ops"):
+    for plan in (None, "graph", "ops"):
         model = load(gpu, GOLDEN / "tiny_qwen3", 16, plan)
         vec = model.embedding_vector(gpu, 42)
         a = model.advance(gpu, 42)
@@ -177,7 +182,7 @@ def test_qwen3_0_6b_greedy_tokens_identical_to_oracle(gpu, oracle, qwen06b_dir):
     prompt, 32 greedy tokens; token-identical to the oracle's decode."""
     prompt = synth.prompt_tokens(7, 24, 151936)
     model = lsx.Model.load(qwen06b_dir, gpu, 64)
-    assert model.fused
+    assert model.fused and model.info().persistent
     tokens, _, frames = model.generate(prompt, 32, frames=True)
     ref = oracle.OracleModel(qwen06b_dir, 64)
     ref_tokens, ref_frames = ref.generate(prompt, 32)
@@ -191,3 +196,15 @@ def test_qwen3_0_6b_greedy_tokens_identical_to_oracle(gpu, oracle, qwen06b_dir):
         close(frames[i].logits, ref_frames[i][1], 2e-2)
     else:
         assert list(map(int, tokens)) == ref_tokens
+
+
+def test_qwen3_0_6b_engines_agree(gpu, qwen06b_dir):
+    """The persistent engine and the PDL kernel chain give the same greedy path."""
+    prompt = synth.prompt_tokens(7, 24, 151936)
+    a = load(gpu, qwen06b_dir, 64)
+    b = load(gpu, qwen06b_dir, 64, "graph")
+    ta, _, fa = a.generate(prompt, 8, frames=True)
+    tb, _, fb = b.generate(prompt, 8, frames=True)
+    assert list(ta) == list(tb)
+    for x, y in zip(fa, fb):
+        assert rel_l2(x.logits, y.logits) < 1e-5
