@@ -207,6 +207,21 @@ int lsx_readout_margin_device(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_
                               double* margin_out, uint32_t* argmax_out, float* target_logit_out,
                               void* workspace, size_t workspace_bytes);
 size_t lsx_readout_workspace_bytes(size_t vocab, size_t width, size_t rows, const lsx_rotation* rotation);
+/* The device-pointer readout margin without an edit, for callers that must not
+   allocate device memory (their memory is already fully committed, or an
+   allocation at that point would be illegal or would stall other work).  It has
+   no counterpart in the reference, which allocates per call (src/gpu.rs:204-216).
+   Scratch is a fixed 4 MiB area inside the library's device image, one per device:
+   calls needing more (bf16 hidden: about 12 bytes per row; F32 hidden: a further
+   4 x width bytes per row) fail with LSX_E_ARGUMENT and enqueue nothing.  No
+   scratch word needs to start at zero.  Calls that may overlap on one device share
+   that scratch and race: order them on one stream.  The first call on a device
+   looks the scratch up (which may load the library's device code): make it before
+   any stream capture begins. */
+int lsx_readout_margin_fixed(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias,
+                             size_t vocab, size_t width, const void* hidden, lsx_dtype hidden_kind,
+                             size_t rows, const uint32_t* targets, double* margin_out,
+                             uint32_t* argmax_out, float* target_logit_out);
 
 /* ---------------------------------------------------- synthetic checkpoints -- */
 /* Seeded N(0, std^2) values rounded to `kind` (BF16 or F32): element i of stream

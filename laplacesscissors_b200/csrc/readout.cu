@@ -567,6 +567,11 @@ size_t readout_smem() {
 
 }  // namespace
 
+// Workspace bytes readout_margin_enqueue needs for exactly this hidden dtype.
+size_t readout_workspace_need(size_t vocab, size_t width, size_t rows, size_t rank, bool f32_hidden) {
+    return layout_for(vocab, width, rows, rank, f32_hidden).total;
+}
+
 // Enqueues the whole validation on ctx->stream.  All pointers are device pointers.
 int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
                            const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
