@@ -3,21 +3,31 @@
 // One cooperative launch runs a whole generation (diagnosis::generate_frames,
 // src/diagnosis.rs:106-149: prompt tokens one at a time, then greedy argmax),
 // each step in the op order of Model::decode (src/model.rs:729-853).  One CTA per
-// SM; 8 compute warps and 1 producer warp.
+// SM; 7 compute warps and 1 producer warp.
 //
-// Weights: every GEMV op gives each CTA a fixed contiguous row range.  The
-// producer warp walks the whole sequence of (step, layer, op, chunk) and streams
-// each chunk of those rows into a shared-memory ring with 1-D bulk copies, as far
-// ahead as the ring allows.  Weights never depend on activations, so HBM keeps
-// streaming while the compute warps wait for the previous op's outputs.
+// Weights: every GEMV op gives each CTA a fixed contiguous row range, cut into
+// chunks of a power-of-two number of rows.  The producer warp walks the whole
+// sequence of (step, layer, op, chunk) and streams each chunk into a shared-memory
+// ring with 1-D bulk copies, as far ahead as the ring allows.  Weights never depend
+// on activations, so HBM keeps streaming while the compute warps wait for the
+// previous op's outputs; a chunk typically lands several microseconds before use.
+//
+// Compute: a GEMV op is latency-bound at batch 1 (a CTA holds only tens of rows),
+// so each warp takes NR rows at once: all NR x KCH 16-byte weight loads issue
+// together against x held in registers, and the NR partial sums are reduced across
+// the warp with one transposing butterfly (log2(NR) halving rounds, then plain
+// rounds), which leaves every row's total in 32/NR lanes.  RMSNorm is folded into
+// the register load of x: every warp holds all of x, so each forms the sum of
+// squares itself and no block-wide reduction is needed.
 //
 // Activations: op outputs are published as 64-bit words (epoch << 32 | f32 bits)
 // with single-copy-atomic stores.  A consumer polls the words it needs until every
 // one carries the current epoch, so the data read IS the synchronisation (one L2
 // round trip per op boundary, no separate barrier).  Each residual row is owned by
 // one CTA for the whole generation, so residual updates need no read-back.
-// Every wait is bounded; on timeout the kernel records a status, raises a global
-// abort flag that all other waits observe, drains its copies and returns.
+// Attention runs one query head per CTA (CTAs 0..qheads-1), with QK-norm and RoPE in
+// registers.  Every wait is bounded; on timeout the kernel records a status, raises a
+// global abort flag that all other waits observe, drains its copies and returns.
 #include <math.h>
 
 #include <cmath>
@@ -29,10 +39,26 @@
 namespace lsx {
 namespace {
 
-constexpr int kWarps = 7;                       // compute warps (2 warps per SM sub-partition with the producer)
-constexpr int kThreads = (kWarps + 1) * 32;     // + producer warp
+constexpr int kWarps = 7;                    // compute warps (2 warps per SM sub-partition with the producer)
+constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kCompute = kWarps * 32;
-constexpr long long kSpin = 4000000000ll;        // ~2 s at B200 clocks
+constexpr long long kSpin = 4000000000ll;     // ~2 s at B200 clocks
+
+enum { kOpQkv = 0, kOpO = 1, kOpGu = 2, kOpDown = 3, kOpHead = 4, kOps = 5 };
+
+// This CTA's share of one GEMV op.
+struct OpDesc {
+    int lo, hi;  // rows [lo, hi)
+    int shift;   // rows per chunk = 1 << shift
+    int nch;     // chunks
+    int K;       // row length in elements
+    int win;     // chunks per window (a window is waited for, computed and released together)
+};
+
+// Byte offsets of the shared-memory regions (host-computed).
+struct SmemLayout {
+    int xs, scratch, resid, red, full, empty, flags, ops, layers, total;
+};
 
 struct PArgs {
     int H, V, L, QH, KVH, D, I, rotary, interleaved, act;
@@ -49,11 +75,7 @@ struct PArgs {
     int steps;
     int slots;
     int slot_bytes;
-    int xmax;
-    int scratch;  // floats of attention / edit scratch
-    int rmax;     // residual rows owned per CTA, upper bound
-    int prefetch; // chunks of L2 prefetch ahead of the ring copies
-    int layers_offset;  // byte offset of the layer table in shared memory
+    SmemLayout sm;
 };
 
 // ------------------------------------------------------------ primitives --
@@ -88,9 +110,7 @@ __device__ __forceinline__ bool compute_and(bool v) {
     return r != 0;
 }
 
-__device__ __forceinline__ void raise_abort(DecodeState* st, int code) {
-    atomicCAS(&st->status, 0, code);
-}
+__device__ __forceinline__ void raise_abort(DecodeState* st, int code) { atomicCAS(&st->status, 0, code); }
 __device__ __forceinline__ bool aborted(DecodeState* st) { return ld_relaxed_int(&st->status) != 0; }
 
 // Argmax partial: total-order value (32) | 0x7FFFF - index (19) | epoch (13).
@@ -145,7 +165,7 @@ __device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch
     return ok;
 }
 
-// Three segments polled in one round (q heads, k and v of one KV group).
+// Three segments polled in one round (one query head, the key and the value of its group).
 __device__ bool poll_segments(const unsigned long long* s0, int n0, float* d0, const unsigned long long* s1, int n1,
                               float* d1, const unsigned long long* s2, int n2, float* d2, uint32_t epoch,
                               DecodeState* st) {
@@ -159,10 +179,19 @@ __device__ bool poll_segments(const unsigned long long* s0, int n0, float* d0, c
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int i = base + tid + j * kCompute;
-            if (i < n0) { src[j] = s0 + i; dst[j] = d0 + i; }
-            else if (i < n0 + n1) { src[j] = s1 + (i - n0); dst[j] = d1 + (i - n0); }
-            else if (i < n) { src[j] = s2 + (i - n0 - n1); dst[j] = d2 + (i - n0 - n1); }
-            else { src[j] = nullptr; dst[j] = nullptr; }
+            if (i < n0) {
+                src[j] = s0 + i;
+                dst[j] = d0 + i;
+            } else if (i < n0 + n1) {
+                src[j] = s1 + (i - n0);
+                dst[j] = d1 + (i - n0);
+            } else if (i < n) {
+                src[j] = s2 + (i - n0 - n1);
+                dst[j] = d2 + (i - n0 - n1);
+            } else {
+                src[j] = nullptr;
+                dst[j] = nullptr;
+            }
             v[j] = src[j] ? ld_relaxed(src[j]) : ((unsigned long long)epoch << 32);
         }
         long long start = 0;
@@ -190,83 +219,32 @@ __device__ bool poll_segments(const unsigned long long* s0, int n0, float* d0, c
     return ok;
 }
 
-struct Range {
-    int lo, hi, sr, nch;
-};
-
-__device__ __forceinline__ Range range_of(int n, int unit, int K, int c, int G, int slot_bytes) {
-    Range r;
+// This CTA's rows of an op of n rows in units of `unit` rows, chunked for the ring.
+__device__ OpDesc make_op(int n, int unit, int K, int c, int G, int slot_bytes, int slots) {
+    OpDesc d;
     const int units = n / unit;
-    r.lo = (int)(((long long)c * units) / G) * unit;
-    r.hi = (int)(((long long)(c + 1) * units) / G) * unit;
-    int sr = slot_bytes / (2 * K);
-    sr = (sr / unit) * unit;
-    if (sr < unit) sr = unit;
-    r.sr = sr;
-    r.nch = (r.hi - r.lo + sr - 1) / sr;
-    return r;
+    d.lo = (int)(((long long)c * units) / G) * unit;
+    d.hi = (int)(((long long)(c + 1) * units) / G) * unit;
+    const int fit = slot_bytes / (2 * K);
+    int shift = 0;
+    while ((2 << shift) <= fit) ++shift;
+    while ((1 << shift) < unit) ++shift;
+    d.shift = shift;
+    d.nch = (d.hi - d.lo + (1 << shift) - 1) >> shift;
+    d.K = K;
+    const int half = slots / 2 > 0 ? slots / 2 : 1;
+    d.win = d.nch <= half ? (d.nch > 0 ? d.nch : 1) : half;
+    return d;
 }
 
-// Op table: 0 qkv, 1 o, 2 gate/up, 3 down, 4 head.
-__device__ __forceinline__ void op_shape(const PArgs& a, const FusedLayer* table, int op, int layer,
-                                         const __nv_bfloat16** w, int* n, int* K, int* unit) {
-    const FusedLayer& L = table[layer];
+__device__ __forceinline__ const __nv_bfloat16* op_weight(const PArgs& a, const FusedLayer& L, int op) {
     switch (op) {
-    case 0: *w = L.wqkv; *n = (a.QH + 2 * a.KVH) * a.D; *K = a.H; *unit = 1; break;
-    case 1: *w = L.wo; *n = a.H; *K = a.QH * a.D; *unit = 1; break;
-    case 2: *w = L.wgu; *n = 2 * a.I; *K = a.H; *unit = 2; break;
-    case 3: *w = L.wd; *n = a.H; *K = a.I; *unit = 1; break;
-    default: *w = a.head; *n = a.V; *K = a.H; *unit = 1; break;
+    case kOpQkv: return L.wqkv;
+    case kOpO: return L.wo;
+    case kOpGu: return L.wgu;
+    case kOpDown: return L.wd;
+    default: return a.head;
     }
-}
-
-// Walks this CTA's weight chunks in consumption order: for every step, the four
-// GEMV ops of each layer, then the head.
-struct ChunkCursor {
-    int step = 0, op_i = 0, ch = 0;
-    const __nv_bfloat16* w = nullptr;
-    int K = 0, r0 = 0, nr = 0;
-    Range R{};
-    bool valid = false;
-    // Positions on the first chunk of the current (or next non-empty) op.
-    const FusedLayer* table = nullptr;  // the shared-memory copy of the layer table
-    __device__ void load(const PArgs& a, int c, int G) {
-        valid = false;
-        while (step < a.steps) {
-            const int layer = op_i < 4 * a.L ? op_i / 4 : 0;
-            const int op = op_i < 4 * a.L ? op_i % 4 : 4;
-            int n, unit;
-            op_shape(a, table, op, layer, &w, &n, &K, &unit);
-            R = range_of(n, unit, K, c, G, a.slot_bytes);
-            if (R.nch > 0) {
-                ch = 0;
-                r0 = R.lo;
-                nr = min(R.sr, R.hi - r0);
-                valid = true;
-                return;
-            }
-            if (++op_i > 4 * a.L) {
-                op_i = 0;
-                ++step;
-            }
-        }
-    }
-    __device__ void advance(const PArgs& a, int c, int G) {
-        if (++ch < R.nch) {  // next chunk of the same op: no range arithmetic
-            r0 += R.sr;
-            nr = min(R.sr, R.hi - r0);
-            return;
-        }
-        if (++op_i > 4 * a.L) {
-            op_i = 0;
-            ++step;
-        }
-        load(a, c, G);
-    }
-};
-
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ float activation(float x, int kind) {
@@ -299,6 +277,29 @@ struct Ring {
     int slot_bytes;
 };
 
+// Position of the next chunk in the ring: slot and the parity of its use.
+struct Cursor {
+    int slot = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void at(int ahead, int slots, int* s, uint32_t* p) const {
+        int t = slot + ahead;
+        uint32_t q = phase;
+        if (t >= slots) {
+            t -= slots;
+            q ^= 1u;
+        }
+        *s = t;
+        *p = q;
+    }
+    __device__ __forceinline__ void advance(int n, int slots) {
+        slot += n;
+        if (slot >= slots) {
+            slot -= slots;
+            phase ^= 1u;
+        }
+    }
+};
+
 enum { kEpiStore = 0, kEpiResidual = 1, kEpiGated = 2, kEpiHead = 3 };
 
 struct EpiCtx {
@@ -307,13 +308,13 @@ struct EpiCtx {
     float* resid;             // this CTA's residual rows (shared memory), residual epilogue
     int resid_lo;
     float* logits;            // head
-    unsigned long long best;  // head, per warp (lane 0)
+    unsigned long long best;  // head, per lane
     bool bad;
     int act;
 };
 
 // Partial dot of one 16-byte chunk of bf16 weights with eight f32 values, as two
-// independent FMA chains (shorter dependency chains than one running sum).
+// independent FMA chains.
 __device__ __forceinline__ void dot8_split(uint4 w, float4 x0, float4 x1, float& s0, float& s1) {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
     const float2 p0 = __bfloat1622float2(h[0]);
@@ -330,166 +331,226 @@ __device__ __forceinline__ void dot8_split(uint4 w, float4 x0, float4 x1, float&
     s1 = fmaf(p3.y, x1.w, s1);
 }
 
-// Dot products of two staged rows with x, interleaved for instruction-level
-// parallelism; both results are reduced across the warp together.
+// Sums CNT per-lane partials across the warp.  Each halving round exchanges half
+// of the values with the lane OFF apart, so after log2(CNT) rounds every lane
+// carries one value; the remaining rounds complete the sum.  Lane l ends with
+// the total of value l / (32 / CNT).
+template <int CNT, int OFF>
+struct RowReduce {
+    static __device__ __forceinline__ void run(float* v, int lane) {
+        if constexpr (OFF > 0) {
+            if constexpr (CNT > 1) {
+                constexpr int half = CNT / 2;
+                const bool up = (lane & OFF) != 0;
+#pragma unroll
+                for (int i = 0; i < half; ++i) {
+                    const float keep = up ? v[i + half] : v[i];
+                    const float send = up ? v[i] : v[i + half];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+                }
+                RowReduce<half, OFF / 2>::run(v, lane);
+            } else {
+                v[0] += __shfl_xor_sync(0xffffffffu, v[0], OFF);
+                RowReduce<1, OFF / 2>::run(v, lane);
+            }
+        }
+    }
+};
+
+// x of one GEMV in registers, lane-interleaved as the weight loads use it:
+// lane l holds elements [8 (l + 32 j), 8 (l + 32 j) + 8) for j < KCH.
 template <int KCH>
-__device__ __forceinline__ float2 row_dot2(const uint8_t* ra, const uint8_t* rb, const float4* xr, const float* xs,
-                                           int K, int lane) {
-    const uint4* wa = reinterpret_cast<const uint4*>(ra);
-    const uint4* wb = reinterpret_cast<const uint4*>(rb);
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-    if (KCH > 0) {
+struct XRegs {
+    float4 v[2 * (KCH > 0 ? KCH : 1)];
+    __device__ __forceinline__ void load(const float* xs, int lane) {
+        const float4* x4 = reinterpret_cast<const float4*>(xs);
 #pragma unroll
         for (int j = 0; j < KCH; ++j) {
-            const uint4 ua = wa[lane + 32 * j];
-            const uint4 ub = wb[lane + 32 * j];
-            dot8_split(ua, xr[2 * j], xr[2 * j + 1], a0, a1);
-            dot8_split(ub, xr[2 * j], xr[2 * j + 1], b0, b1);
-        }
-    } else {
-        const float4* x4 = reinterpret_cast<const float4*>(xs);
-        for (int c = lane; c < (K >> 3); c += 32) {
-            const float4 x0 = x4[2 * c], x1 = x4[2 * c + 1];
-            dot8_split(wa[c], x0, x1, a0, a1);
-            dot8_split(wb[c], x0, x1, b0, b1);
+            v[2 * j] = x4[2 * (lane + 32 * j)];
+            v[2 * j + 1] = x4[2 * (lane + 32 * j) + 1];
         }
     }
-    float a = a0 + a1, b = b0 + b1;
+};
+
+// RMSNorm gains in the XRegs layout, fetched before the activations are waited for.
+template <int KCH>
+struct GainX {
+    float g[8 * (KCH > 0 ? KCH : 1)];
+    __device__ __forceinline__ void load(const float* gain, int lane) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        a += __shfl_xor_sync(0xffffffffu, a, o);
-        b += __shfl_xor_sync(0xffffffffu, b, o);
+        for (int j = 0; j < KCH; ++j)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[8 * j + e] = gain ? __ldg(gain + 8 * (lane + 32 * j) + e) : 1.f;
     }
-    return make_float2(a, b);
+};
+
+// RMSNorm (kernels/ops.py:31-45) of the register copy of x: x * rsqrt(mean(x^2) + eps) * gain.
+template <int KCH>
+__device__ __forceinline__ void norm_regs(XRegs<KCH>& x, const GainX<KCH>& g, int n, float eps) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2 * KCH; ++j) {
+        ss = fmaf(x.v[j].x, x.v[j].x, ss);
+        ss = fmaf(x.v[j].y, x.v[j].y, ss);
+        ss = fmaf(x.v[j].z, x.v[j].z, ss);
+        ss = fmaf(x.v[j].w, x.v[j].w, ss);
+    }
+    ss = warp_allsum(ss);
+    const float inverse = rsqrtf(ss / (float)n + eps);
+#pragma unroll
+    for (int j = 0; j < 2 * KCH; ++j) {
+        x.v[j].x = x.v[j].x * inverse * g.g[4 * j + 0];
+        x.v[j].y = x.v[j].y * inverse * g.g[4 * j + 1];
+        x.v[j].z = x.v[j].z * inverse * g.g[4 * j + 2];
+        x.v[j].w = x.v[j].w * inverse * g.g[4 * j + 3];
+    }
 }
 
-__device__ __forceinline__ void epilogue(int EPI, int r, float d, const float* bias, EpiCtx& e) {
-    if (bias) d += bias[r];
-    if (EPI == kEpiStore) {
-        st_relaxed(e.out + r, tagged(e.epoch, d));
-    } else if (EPI == kEpiResidual) {
-        const float v = __fadd_rn(e.resid[r - e.resid_lo], d);
-        e.resid[r - e.resid_lo] = v;
-        st_relaxed(e.out + r, tagged(e.epoch, v));
-    } else {
-        e.logits[r] = d;
-        e.bad |= !isfinite(d);
-        const unsigned long long key = pack_arg(d, (uint32_t)r);
-        e.best = key > e.best ? key : e.best;
-    }
-}
-
-// One GEMV op over this CTA's rows; consumes its chunks from the ring in order
-// and releases them window by window.
-// KCH > 0: K == 256 * KCH and each lane keeps its x chunks in registers;
-// KCH == 0: any K % 8 == 0, x read from shared memory.
-template <int EPI, int KCH>
-__device__ __forceinline__ bool run_gemv(const Ring& ring, unsigned long long& q, const float* bias, int n, int K, int unit,
-                         const float* xs, EpiCtx& e) {
+// One GEMV op over this CTA's rows: consumes its chunks from the ring window by
+// window and releases each window's slots when done.  Each warp takes NR rows per
+// pass.  KCH > 0: K == 256 * KCH and x lives in registers (normalised there when
+// `gain` is given); KCH == 0: any K % 8 == 0, x read from shared memory.
+template <int EPI, int KCH, int NR>
+__device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const OpDesc& op, const float* bias,
+                                         const float* xs, const GainX<KCH>* gain, float eps, EpiCtx& e) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const Range R = range_of(n, unit, K, blockIdx.x, gridDim.x, ring.slot_bytes);
-    float4 xr[KCH > 0 ? 2 * KCH : 1];
+    const int K = op.K;
+    const uint32_t row_bytes = (uint32_t)K * 2u;
+    const int mask = (1 << op.shift) - 1;
+    XRegs<KCH> x;
     if (KCH > 0) {
-        const float4* x4 = reinterpret_cast<const float4*>(xs);
-#pragma unroll
-        for (int j = 0; j < KCH; ++j) {
-            xr[2 * j] = x4[2 * (lane + 32 * j)];
-            xr[2 * j + 1] = x4[2 * (lane + 32 * j) + 1];
-        }
+        x.load(xs, lane);
+        if (gain) norm_regs<KCH>(x, *gain, K, eps);
     }
-    const size_t row_bytes = (size_t)K * 2;
-    // Ops that fit half the ring run as one window; longer ones (the head) stream
-    // in short windows so freed slots are refilled continuously.
-    const int half = ring.slots / 2 > 0 ? ring.slots / 2 : 1;
-    const int win = R.nch <= half ? half : (half >= 4 ? 4 : half);
-    const int slot0 = (int)(q % (unsigned long long)ring.slots);
-    const uint32_t round0 = (uint32_t)(q / (unsigned long long)ring.slots);
+    constexpr int kLanesPerRow = 32 / NR;
+    const int my_row = lane / kLanesPerRow;  // row of the pass this lane ends up holding
+    const bool owner = (lane % kLanesPerRow) == 0;
     bool ok = true;
-    for (int w0 = 0; w0 < R.nch && ok; w0 += win) {
-        const int wn = min(win, R.nch - w0);
-        const int rs = R.lo + w0 * R.sr;
-        const int re = min(R.hi, R.lo + (w0 + wn) * R.sr);
+    for (int w0 = 0; w0 < op.nch && ok; w0 += op.win) {
+        const int wn = min(op.win, op.nch - w0);
+        const int rs = op.lo + (w0 << op.shift);
+        const int re = min(op.hi, op.lo + ((w0 + wn) << op.shift));
         // Wait once for every chunk of the window (immediate when already landed).
         bool landed = true;
-        for (int ch = w0; ch < w0 + wn; ++ch) {
-            const int lin = slot0 + ch;
-            const int slot = lin % ring.slots;
-            const uint32_t parity = (round0 + (uint32_t)(lin / ring.slots)) & 1u;
-            landed &= mbar_wait_bounded(&ring.full[slot], parity);
+        for (int ch = 0; ch < wn; ++ch) {
+            int s;
+            uint32_t p;
+            cur.at(ch, ring.slots, &s, &p);
+            landed &= mbar_wait_bounded(&ring.full[s], p);
         }
         ok = __all_sync(0xffffffffu, landed);
-        auto row_at = [&](int r) -> const uint8_t* {
-            const int local = r - R.lo;
-            const int ch = local / R.sr;
-            const int slot = (slot0 + ch) % ring.slots;
-            return ring.base + (size_t)slot * ring.slot_bytes + (size_t)(local - ch * R.sr) * row_bytes;
-        };
         if (ok) {
-            if (EPI == kEpiGated) {
-                for (int p = warp; p < (re - rs) / 2; p += kWarps) {
-                    const int r = rs + 2 * p;
-                    const uint8_t* g_row = row_at(r);  // even rows per chunk: pairs stay whole
-                    const float2 gu = row_dot2<KCH>(g_row, g_row + row_bytes, xr, xs, K, lane);
-                    if (lane == 0) {
-                        float g = gu.x, u = gu.y;
+            for (int r0 = rs + warp * NR; r0 < re; r0 += kWarps * NR) {
+                const uint8_t* rp[NR];
+#pragma unroll
+                for (int i = 0; i < NR; ++i) {
+                    const int local = min(r0 + i, re - 1) - rs;  // the window starts on a chunk boundary
+                    int s;
+                    uint32_t p;
+                    cur.at(local >> op.shift, ring.slots, &s, &p);
+                    rp[i] = ring.base + (size_t)s * ring.slot_bytes + (uint32_t)(local & mask) * row_bytes;
+                }
+                float acc[NR];
+                {
+                    float a0[NR], a1[NR];
+#pragma unroll
+                    for (int i = 0; i < NR; ++i) a0[i] = a1[i] = 0.f;
+                    if (KCH > 0) {
+#pragma unroll
+                        for (int j = 0; j < KCH; ++j) {
+                            uint4 w[NR];
+#pragma unroll
+                            for (int i = 0; i < NR; ++i) w[i] = reinterpret_cast<const uint4*>(rp[i])[lane + 32 * j];
+#pragma unroll
+                            for (int i = 0; i < NR; ++i) dot8_split(w[i], x.v[2 * j], x.v[2 * j + 1], a0[i], a1[i]);
+                        }
+                    } else {
+                        const float4* x4 = reinterpret_cast<const float4*>(xs);
+                        for (int cc = lane; cc < (K >> 3); cc += 32) {
+                            const float4 x0 = x4[2 * cc], x1 = x4[2 * cc + 1];
+#pragma unroll
+                            for (int i = 0; i < NR; ++i)
+                                dot8_split(reinterpret_cast<const uint4*>(rp[i])[cc], x0, x1, a0[i], a1[i]);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < NR; ++i) acc[i] = a0[i] + a1[i];
+                }
+                RowReduce<NR, 16>::run(acc, lane);
+                float d = acc[0];
+                const int r = r0 + my_row;
+                const bool valid = owner && r < re;
+                if (EPI == kEpiGated) {
+                    // rows come in (gate, up) pairs; the up total sits kLanesPerRow lanes higher
+                    const float u = __shfl_down_sync(0xffffffffu, d, kLanesPerRow);
+                    if (valid && (my_row & 1) == 0) {
+                        float g = d, uu = u;
                         if (bias) {
                             g += bias[r];
-                            u += bias[r + 1];
+                            uu += bias[r + 1];
                         }
-                        st_relaxed(e.out + (r >> 1), tagged(e.epoch, activation(g, e.act) * u));
+                        st_relaxed(e.out + (r >> 1), tagged(e.epoch, activation(g, e.act) * uu));
                     }
-                }
-            } else {
-                for (int r = rs + warp; r < re; r += 2 * kWarps) {
-                    const int r2 = r + kWarps;
-                    const uint8_t* pa = row_at(r);
-                    const uint8_t* pb = r2 < re ? row_at(r2) : pa;
-                    const float2 d = row_dot2<KCH>(pa, pb, xr, xs, K, lane);
-                    if (lane == 0) {
-                        epilogue(EPI, r, d.x, bias, e);
-                        if (r2 < re) epilogue(EPI, r2, d.y, bias, e);
+                } else if (valid) {
+                    if (bias) d += bias[r];
+                    if (EPI == kEpiStore) {
+                        st_relaxed(e.out + r, tagged(e.epoch, d));
+                    } else if (EPI == kEpiResidual) {
+                        const float v = __fadd_rn(e.resid[r - e.resid_lo], d);
+                        e.resid[r - e.resid_lo] = v;
+                        st_relaxed(e.out + r, tagged(e.epoch, v));
+                    } else {
+                        e.logits[r] = d;
+                        e.bad |= !isfinite(d);
+                        const unsigned long long key = pack_arg(d, (uint32_t)r);
+                        e.best = key > e.best ? key : e.best;
                     }
                 }
             }
         }
         ok = compute_and(ok);
         if (tid == 0)
-            for (int ch = w0; ch < w0 + wn; ++ch) mbar_arrive(&ring.empty[(slot0 + ch) % ring.slots]);
+            for (int ch = 0; ch < wn; ++ch) {
+                int s;
+                uint32_t p;
+                cur.at(ch, ring.slots, &s, &p);
+                mbar_arrive(&ring.empty[s]);
+            }
+        cur.advance(wn, ring.slots);
     }
-    q += (unsigned long long)R.nch;
     return ok;
 }
 
-// Attention of KV group g at `pos` (kernels/ops.py:69-101 after QK-norm and RoPE):
-// polls the group's q/k/v, normalises and rotates them, appends k/v to the f32
-// cache, attends over positions 0..pos and publishes the group's output heads.
-template <int RATIO, int DPL>
-__device__ __forceinline__ bool attention_group(const PArgs& a, const FusedLayer& L, int g, int pos, uint32_t e_qkv, uint32_t e_attn,
-                                float* sm) {
+// Attention of query head h at `pos` (kernels/ops.py:69-101 after QK-norm and
+// RoPE): polls the head's q and its group's k and v, normalises and rotates them
+// in registers, appends k/v to the f32 cache (first head of the group), attends
+// over positions 0..pos and publishes the head's output.  Warp w takes positions
+// w, w + kWarps, ... in batches of PB; partial softmax states merge in shared memory.
+template <int DPL, int PB>
+__device__ __forceinline__ bool attention_head(const PArgs& a, const FusedLayer& L, int h, int pos, uint32_t e_qkv,
+                                               uint32_t e_attn, float* sm) {
     constexpr int D = DPL * 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float* raw = sm;                    // (RATIO + 2) * D: q heads, k, v
-    float* qs = raw + (RATIO + 2) * D;  // RATIO * D (normed, rotated)
-    float* ks = qs + RATIO * D;         // D
-    float* merge = ks + D;              // kWarps * RATIO * (D + 2)
+    const int ratio = a.QH / a.KVH, g = h / ratio;
     const int qw = a.QH * D, kw = a.KVH * D;
-    // The cached positions 0..pos-1 do not depend on this step: start loading this
-    // warp's first batch of them before waiting for q, k and v.
-    constexpr int PB = 4;
+    float* raw = sm;                        // 3 D: q, k, v
+    float* merge = raw + 3 * D;             // kWarps * (D + 2)
+    float* rot = merge + kWarps * (D + 2);  // general RoPE path: q, k and the table row (3 D)
+    const bool fast_rope = a.rotary == D && !a.interleaved;
+    // The cached positions 0..pos-1 do not depend on this step: load this warp's
+    // first batch before waiting for q, k and v.
     const float* kbase = L.keys + (size_t)g * D;
     const float* vbase = L.values + (size_t)g * D;
-    float kpre[PB][DPL], vpre[PB][DPL];
+    float kv[PB][DPL], vv[PB][DPL];
 #pragma unroll
     for (int b = 0; b < PB; ++b) {
         const int t = warp + kWarps * b;
 #pragma unroll
         for (int j = 0; j < DPL; ++j) {
-            kpre[b][j] = t < pos ? __ldcg(kbase + (size_t)t * kw + lane + 32 * j) : 0.f;
-            vpre[b][j] = t < pos ? __ldcg(vbase + (size_t)t * kw + lane + 32 * j) : 0.f;
+            kv[b][j] = t < pos ? __ldcg(kbase + (size_t)t * kw + lane + 32 * j) : 0.f;
+            vv[b][j] = t < pos ? __ldcg(vbase + (size_t)t * kw + lane + 32 * j) : 0.f;
         }
     }
-    // Gains and the RoPE row of this position are also independent of the step's
-    // activations: fetch them now.
     float qg[DPL], kg[DPL];
 #pragma unroll
     for (int j = 0; j < DPL; ++j) {
@@ -497,181 +558,178 @@ __device__ __forceinline__ bool attention_group(const PArgs& a, const FusedLayer
         kg[j] = L.k_gain ? __ldg(L.k_gain + lane + 32 * j) : 1.f;
     }
     const int half = a.rotary / 2;
-    constexpr int kRopeRegs = 4;  // rotary pairs up to 4 * kCompute
-    float2 cs_pre[kRopeRegs];
+    float2 cs[DPL / 2 > 0 ? DPL / 2 : 1];
+    if (fast_rope) {
 #pragma unroll
-    for (int j = 0; j < kRopeRegs; ++j) {
-        const int i = tid + j * kCompute;
-        cs_pre[j] = i < half ? a.rope[(size_t)pos * half + i] : make_float2(1.f, 0.f);
+        for (int j = 0; j < DPL / 2; ++j) cs[j] = a.rope[(size_t)pos * half + lane + 32 * j];
     }
-    bool ok = poll_segments(a.t_qkv + (size_t)g * RATIO * D, RATIO * D, raw, a.t_qkv + qw + (size_t)g * D, D,
-                            raw + RATIO * D, a.t_qkv + qw + kw + (size_t)g * D, D, raw + (RATIO + 1) * D, e_qkv,
-                            a.state);
+    bool ok = poll_segments(a.t_qkv + (size_t)h * D, D, raw, a.t_qkv + qw + (size_t)g * D, D, raw + D,
+                            a.t_qkv + qw + kw + (size_t)g * D, D, raw + 2 * D, e_qkv, a.state);
     if (!compute_and(ok)) return false;
-    float* cs_s = merge;  // RoPE row for this position, shared by the heads
+    float q[DPL], k[DPL], v[DPL];
 #pragma unroll
-    for (int j = 0; j < kRopeRegs; ++j) {
-        const int i = tid + j * kCompute;
-        if (i < half) reinterpret_cast<float2*>(cs_s)[i] = cs_pre[j];
+    for (int j = 0; j < DPL; ++j) {
+        q[j] = raw[lane + 32 * j];
+        k[j] = raw[D + lane + 32 * j];
+        v[j] = raw[2 * D + lane + 32 * j];
     }
-    for (int h = warp; h < RATIO + 1; h += kWarps) {  // Qwen3 q_norm / k_norm per head
-        const bool has = h < RATIO ? L.q_gain != nullptr : L.k_gain != nullptr;
-        if (!has) continue;
-        float* row = raw + h * D;
+    // Qwen3 q_norm / k_norm per head (kernels/ops.py:31-45 over head_dim)
+    if (L.q_gain) {
         float ss = 0.f;
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) ss = fmaf(row[lane + 32 * j], row[lane + 32 * j], ss);
-        ss = warp_allsum(ss);
-        const float inverse = rsqrtf(ss / (float)D + a.qk_eps);
+        for (int j = 0; j < DPL; ++j) ss = fmaf(q[j], q[j], ss);
+        const float inverse = rsqrtf(warp_allsum(ss) / (float)D + a.qk_eps);
 #pragma unroll
-        for (int j = 0; j < DPL; ++j)
-            row[lane + 32 * j] = row[lane + 32 * j] * inverse * (h < RATIO ? qg[j] : kg[j]);
+        for (int j = 0; j < DPL; ++j) q[j] = q[j] * inverse * qg[j];
     }
-    compute_sync();
-    for (int i = tid; i < (RATIO + 1) * D; i += kCompute) {  // kernels/ops.py:48-66
-        const int h = i / D, local = i % D;
-        const float x = raw[i];
-        float y = x;
-        if (local < a.rotary) {
-            int pair, other;
-            float sign;
-            if (a.interleaved) {
-                pair = local >> 1;
-                other = (local & 1) ? local - 1 : local + 1;
-                sign = (local & 1) ? 1.f : -1.f;
-            } else {
-                pair = local % half;
-                other = local < half ? local + half : local - half;
-                sign = local < half ? -1.f : 1.f;
-            }
-            const float2 cs = reinterpret_cast<const float2*>(cs_s)[pair];
-            y = x * cs.x + sign * raw[h * D + other] * cs.y;
+    if (L.k_gain) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) ss = fmaf(k[j], k[j], ss);
+        const float inverse = rsqrtf(warp_allsum(ss) / (float)D + a.qk_eps);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) k[j] = k[j] * inverse * kg[j];
+    }
+    // RoPE (kernels/ops.py:48-66).  Full-width rotate-half pairs d with d + D/2,
+    // i.e. register j with register j + DPL/2 of the same lane.
+    if (fast_rope) {
+#pragma unroll
+        for (int j = 0; j < DPL / 2; ++j) {
+            const float q1 = q[j], q2 = q[j + DPL / 2], k1 = k[j], k2 = k[j + DPL / 2];
+            q[j] = q1 * cs[j].x + -1.f * q2 * cs[j].y;
+            q[j + DPL / 2] = q2 * cs[j].x + 1.f * q1 * cs[j].y;
+            k[j] = k1 * cs[j].x + -1.f * k2 * cs[j].y;
+            k[j + DPL / 2] = k2 * cs[j].x + 1.f * k1 * cs[j].y;
         }
-        if (h < RATIO) qs[i] = y;
-        else ks[local] = y;
-    }
-    compute_sync();
-    const float* vs = raw + (RATIO + 1) * D;
-    float* kd = L.keys + (size_t)pos * kw + (size_t)g * D;
-    float* vd = L.values + (size_t)pos * kw + (size_t)g * D;
-    for (int i = tid; i < D; i += kCompute) {  // kernels/ops.py:69-73
-        kd[i] = ks[i];
-        vd[i] = vs[i];
-    }
-    float q[RATIO][DPL], acc[RATIO][DPL], m[RATIO], l[RATIO];
-#pragma unroll
-    for (int h = 0; h < RATIO; ++h) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-            q[h][j] = qs[h * D + lane + 32 * j];
-            acc[h][j] = 0.f;
-        }
-    }
-    // Scores of a batch of positions are formed and reduced together, then one
-    // online-softmax update folds the whole batch in (kernels/ops.py:88-99).
-    auto attend_batch = [&](const float (*kv)[DPL], const float (*vv)[DPL], int nb) {
-        float sc[PB][RATIO];
-#pragma unroll
-        for (int b = 0; b < PB; ++b)
-#pragma unroll
-            for (int h = 0; h < RATIO; ++h) {
-                float t = 0.f;
-#pragma unroll
-                for (int j = 0; j < DPL; ++j) t = fmaf(q[h][j], kv[b][j], t);
-                sc[b][h] = t;
-            }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int b = 0; b < PB; ++b)
-#pragma unroll
-                for (int h = 0; h < RATIO; ++h) sc[b][h] += __shfl_xor_sync(0xffffffffu, sc[b][h], o);
-#pragma unroll
-        for (int h = 0; h < RATIO; ++h) {
-            float mn = m[h];
-#pragma unroll
-            for (int b = 0; b < PB; ++b) {
-                sc[b][h] = b < nb ? sc[b][h] * a.scale : -INFINITY;
-                mn = fmaxf(mn, sc[b][h]);
-            }
-            const float carry = expf(m[h] - mn);
-            float pr[PB], psum = 0.f;
-#pragma unroll
-            for (int b = 0; b < PB; ++b) {
-                pr[b] = b < nb ? expf(sc[b][h] - mn) : 0.f;
-                psum += pr[b];
-            }
-            l[h] = l[h] * carry + psum;
+    } else if (a.rotary > 0) {
+        float* qn = rot;
+        float* kn = rot + D;
+        float2* cs_s = reinterpret_cast<float2*>(rot + 2 * D);
+        if (warp == 0) {
 #pragma unroll
             for (int j = 0; j < DPL; ++j) {
-                float v = acc[h][j] * carry;
-#pragma unroll
-                for (int b = 0; b < PB; ++b) v = fmaf(pr[b], vv[b][j], v);
-                acc[h][j] = v;
+                qn[lane + 32 * j] = q[j];
+                kn[lane + 32 * j] = k[j];
             }
-            m[h] = mn;
         }
-    };
-    // Cached positions in batches of PB per warp, every batch's loads issued together.
-    for (int i0 = 0; warp + kWarps * i0 < pos; i0 += PB) {
+        for (int i = tid; i < half; i += kCompute) cs_s[i] = a.rope[(size_t)pos * half + i];
+        compute_sync();
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            const int local = lane + 32 * j;
+            if (local < a.rotary) {
+                int pair, other;
+                float sign;
+                if (a.interleaved) {
+                    pair = local >> 1;
+                    other = (local & 1) ? local - 1 : local + 1;
+                    sign = (local & 1) ? 1.f : -1.f;
+                } else {
+                    pair = local % half;
+                    other = local < half ? local + half : local - half;
+                    sign = local < half ? -1.f : 1.f;
+                }
+                const float2 c2 = cs_s[pair];
+                q[j] = qn[local] * c2.x + sign * qn[other] * c2.y;
+                k[j] = kn[local] * c2.x + sign * kn[other] * c2.y;
+            }
+        }
+    }
+    if (h % ratio == 0 && warp == 0) {  // kernels/ops.py:69-73: append this position's k, v
+        float* kd = L.keys + (size_t)pos * kw + (size_t)g * D;
+        float* vd = L.values + (size_t)pos * kw + (size_t)g * D;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            kd[lane + 32 * j] = k[j];
+            vd[lane + 32 * j] = v[j];
+        }
+    }
+    // Online softmax over this warp's positions, a batch of PB at a time
+    // (kernels/ops.py:88-99): the batch's scores are reduced together.
+    constexpr int kLanesPerPos = 32 / PB;
+    const int my_b = lane / kLanesPerPos;
+    float m = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+    for (int i0 = 0; warp + kWarps * i0 <= pos; i0 += PB) {
         if (i0 > 0) {
 #pragma unroll
             for (int b = 0; b < PB; ++b) {
                 const int t = warp + kWarps * (i0 + b);
 #pragma unroll
                 for (int j = 0; j < DPL; ++j) {
-                    kpre[b][j] = t < pos ? __ldcg(kbase + (size_t)t * kw + lane + 32 * j) : 0.f;
-                    vpre[b][j] = t < pos ? __ldcg(vbase + (size_t)t * kw + lane + 32 * j) : 0.f;
+                    kv[b][j] = t < pos ? __ldcg(kbase + (size_t)t * kw + lane + 32 * j) : 0.f;
+                    vv[b][j] = t < pos ? __ldcg(vbase + (size_t)t * kw + lane + 32 * j) : 0.f;
                 }
             }
         }
-        int nb = 0;
+        float sc[PB];
 #pragma unroll
-        for (int b = 0; b < PB; ++b) nb += warp + kWarps * (i0 + b) < pos ? 1 : 0;
-        attend_batch(kpre, vpre, nb);
-    }
-    if (warp == 0) {  // the current position, from shared memory
+        for (int b = 0; b < PB; ++b) {
+            const int t = warp + kWarps * (i0 + b);
+            if (t == pos) {  // the current position, from registers
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-            kpre[0][j] = ks[lane + 32 * j];
-            vpre[0][j] = vs[lane + 32 * j];
+                for (int j = 0; j < DPL; ++j) {
+                    kv[b][j] = k[j];
+                    vv[b][j] = v[j];
+                }
+            }
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) s = fmaf(q[j], kv[b][j], s);
+            sc[b] = s;
         }
-        attend_batch(kpre, vpre, 1);
+        RowReduce<PB, 16>::run(sc, lane);
+        const bool valid = warp + kWarps * (i0 + my_b) <= pos;
+        const float s = valid ? sc[0] * a.scale : -INFINITY;
+        float mb = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float mn = fmaxf(m, mb);
+        const float carry = expf(m - mn);
+        const float p = valid ? expf(s - mn) : 0.f;
+        const float psum = warp_allsum(lane % kLanesPerPos == 0 ? p : 0.f);
+        l = l * carry + psum;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] *= carry;
+#pragma unroll
+        for (int b = 0; b < PB; ++b) {
+            const float pb = __shfl_sync(0xffffffffu, p, b * kLanesPerPos);
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[j] = fmaf(pb, vv[b][j], acc[j]);
+        }
+        m = mn;
     }
     const int stride = D + 2;
-#pragma unroll
-    for (int h = 0; h < RATIO; ++h) {
-        float* slot = merge + (size_t)(warp * RATIO + h) * stride;
-        if (lane == 0) {
-            slot[0] = m[h];
-            slot[1] = l[h];
-        }
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) slot[2 + lane + 32 * j] = acc[h][j];
+    float* slot = merge + (size_t)warp * stride;
+    if (lane == 0) {
+        slot[0] = m;
+        slot[1] = l;
     }
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) slot[2 + lane + 32 * j] = acc[j];
     compute_sync();
-    for (int i = tid; i < RATIO * D; i += kCompute) {
-        const int h = i / D, d = i % D;
+    for (int d = tid; d < D; d += kCompute) {
         float M = -INFINITY;
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, merge[(w * RATIO + h) * stride]);
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, merge[w * stride]);
         float Lsum = 0.f, O = 0.f;
+#pragma unroll
         for (int w = 0; w < kWarps; ++w) {
-            const float* sl = merge + (size_t)(w * RATIO + h) * stride;
+            const float* sl = merge + (size_t)w * stride;
             if (sl[0] == -INFINITY) continue;
             const float ex = expf(sl[0] - M);
             Lsum = fmaf(sl[1], ex, Lsum);
             O = fmaf(sl[2 + d], ex, O);
         }
-        st_relaxed(a.t_attn + (size_t)(g * RATIO + h) * D + d, tagged(e_attn, O / Lsum));
+        st_relaxed(a.t_attn + (size_t)h * D + d, tagged(e_attn, O / Lsum));
     }
-    compute_sync();
+    // The merge area is rewritten only after later block-wide barriers.
     return true;
 }
 
-// Norm gains of one width, fetched into registers before the activations they
-// scale are waited for (hides the load behind the poll).
+// Norm gains of one width in a strided layout (i = tid + j * kCompute), for the
+// shared-memory RMSNorm used by the generic widths and the final norm.
 constexpr int kGainRegs = 24;  // widths up to 24 * kCompute
 struct GainRegs {
     float g[kGainRegs];
@@ -679,7 +737,7 @@ struct GainRegs {
 #pragma unroll
         for (int j = 0; j < kGainRegs; ++j) {
             const int i = threadIdx.x + j * kCompute;
-            g[j] = i < n ? __ldg(gain + i) : 0.f;
+            g[j] = i < n ? (gain ? __ldg(gain + i) : 1.f) : 0.f;
         }
     }
 };
@@ -702,26 +760,35 @@ __device__ void rms_norm_inplace(float* xs, int n, const GainRegs& gain, float e
     compute_sync();
 }
 
+// Rows per warp pass for a register-resident x of KCH chunks (0: x in shared memory).
+constexpr int rows_for(int kch) { return kch == 0 ? 2 : (kch <= 4 ? 4 : (kch <= 8 ? 2 : 1)); }
+
 // KH, KQ, KI: 16-byte chunks per lane of x for the hidden, query and
-// intermediate widths (0: x stays in shared memory).
-template <int KH, int KQ, int KI, int RATIO, int DPL>
+// intermediate widths (0: x stays in shared memory).  DPL: head_dim / 32.
+template <int KH, int KQ, int KI, int DPL>
 __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int NRH = rows_for(KH);               // qkv and head
+    constexpr int NRG = KH > 0 && KH <= 4 ? 8 : 2;  // gate/up: whole (gate, up) pairs
+    constexpr int NRQ = KQ > 4 ? 1 : rows_for(KQ);  // o
+    constexpr int NRI = KI > 4 ? 1 : rows_for(KI);  // down
+    constexpr int PB = DPL >= 8 ? 4 : 8;            // attention positions per warp batch
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;
     Ring ring;
     ring.base = smem;
     ring.slots = a.slots;
     ring.slot_bytes = a.slot_bytes;
-    float* xs = reinterpret_cast<float*>(smem + (size_t)a.slots * a.slot_bytes);
-    float* scratch = xs + a.xmax;
-    float* resid = scratch + a.scratch;
-    float* red = resid + a.rmax;
-    ring.full = reinterpret_cast<uint64_t*>(red + 64);
-    ring.empty = ring.full + a.slots;
-    volatile int* s_stop = reinterpret_cast<volatile int*>(ring.empty + a.slots);
-    int* s_issued = const_cast<int*>(s_stop) + 1;
-    FusedLayer* layers = reinterpret_cast<FusedLayer*>(smem + a.layers_offset);
+    float* xs = reinterpret_cast<float*>(smem + a.sm.xs);
+    float* scratch = reinterpret_cast<float*>(smem + a.sm.scratch);
+    float* resid = reinterpret_cast<float*>(smem + a.sm.resid);
+    float* red = reinterpret_cast<float*>(smem + a.sm.red);
+    ring.full = reinterpret_cast<uint64_t*>(smem + a.sm.full);
+    ring.empty = reinterpret_cast<uint64_t*>(smem + a.sm.empty);
+    volatile int* s_stop = reinterpret_cast<volatile int*>(smem + a.sm.flags);
+    long long* s_issued = reinterpret_cast<long long*>(smem + a.sm.flags + 8);
+    OpDesc* ops = reinterpret_cast<OpDesc*>(smem + a.sm.ops);
+    FusedLayer* layers = reinterpret_cast<FusedLayer*>(smem + a.sm.layers);
     DecodeState* st = a.state;
     // The per-layer pointer table lives in shared memory: reading it from global
     // memory would miss L2 (the weight stream evicts it) on every op.
@@ -735,6 +802,12 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
         }
         *s_stop = 0;
         *s_issued = 0;
+        const int qkv_rows = (a.QH + 2 * a.KVH) * a.D;
+        ops[kOpQkv] = make_op(qkv_rows, 1, a.H, c, G, a.slot_bytes, a.slots);
+        ops[kOpO] = make_op(a.H, 1, a.QH * a.D, c, G, a.slot_bytes, a.slots);
+        ops[kOpGu] = make_op(2 * a.I, 2, a.H, c, G, a.slot_bytes, a.slots);
+        ops[kOpDown] = make_op(a.H, 1, a.I, c, G, a.slot_bytes, a.slots);
+        ops[kOpHead] = make_op(a.V, 1, a.H, c, G, a.slot_bytes, a.slots);
         fence_barrier_init();
     }
     __syncthreads();
@@ -746,58 +819,59 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
 
     if (warp == kWarps) {  // ---------------------------------- producer warp
         if (lane == 0) {
-            unsigned long long q = 0;
-            bool go = true;
-            // Copies into the ring follow `cur`; L2 prefetches run `a.prefetch` chunks
-            // ahead of it so HBM reads start about a layer before the ring can hold them.
             const uint64_t policy = l2_evict_first_policy();
-            ChunkCursor cur, pre;
-            cur.table = layers;
-            pre.table = layers;
-            cur.load(a, c, G);
-            pre.load(a, c, G);
-            for (int i = 0; i < a.prefetch && pre.valid; ++i) {
-                prefetch_l2(pre.w + (size_t)pre.r0 * pre.K, (uint32_t)((size_t)pre.nr * pre.K * 2));
-                pre.advance(a, c, G);
-            }
-            for (; cur.valid && go; ++q) {
-                const int slot = (int)(q % (unsigned long long)a.slots);
-                const unsigned long long round = q / (unsigned long long)a.slots;
-                if (round > 0) {
-                    // wait until the consumers released this slot's previous chunk
-                    const uint32_t addr = smem_u32(&ring.empty[slot]);
-                    const uint32_t parity = (uint32_t)((round - 1) & 1ull);
-                    long long start = 0;
-                    while (!mbar_try_wait(addr, parity)) {
-                        if (*s_stop) {
-                            go = false;
-                            break;
+            int slot = 0;
+            uint32_t phase = 0;
+            bool wrapped = false, go = true;
+            long long issued = 0;
+            for (int step = 0; step < a.steps && go; ++step) {
+                for (int oi = 0; oi <= 4 * a.L && go; ++oi) {
+                    const int op = oi < 4 * a.L ? (oi & 3) : kOpHead;
+                    const OpDesc d = ops[op];
+                    const __nv_bfloat16* w = op_weight(a, layers[oi < 4 * a.L ? oi >> 2 : 0], op);
+                    for (int ch = 0; ch < d.nch; ++ch) {
+                        if (wrapped) {
+                            // wait until the consumers released this slot's previous chunk
+                            const uint32_t addr = smem_u32(&ring.empty[slot]);
+                            long long start = 0;
+                            while (!mbar_try_wait(addr, phase ^ 1u)) {
+                                if (*s_stop) {
+                                    go = false;
+                                    break;
+                                }
+                                if (start == 0) {
+                                    start = clock64();
+                                } else if (clock64() - start > kSpin) {
+                                    raise_abort(st, kDeviceTimeoutWeights);
+                                    go = false;
+                                    break;
+                                }
+                            }
+                            if (!go) break;
                         }
-                        if (start == 0) start = clock64();
-                        else if (clock64() - start > kSpin) {
-                            raise_abort(st, kDeviceTimeoutWeights);
-                            go = false;
-                            break;
+                        const int r0 = d.lo + (ch << d.shift);
+                        const int nr = min(1 << d.shift, d.hi - r0);
+                        const uint32_t bytes = (uint32_t)nr * (uint32_t)d.K * 2u;
+                        mbar_expect_tx(&ring.full[slot], bytes);
+                        bulk_load_hint(ring.base + (size_t)slot * a.slot_bytes, w + (size_t)r0 * d.K, bytes,
+                                       &ring.full[slot], policy);
+                        ++issued;
+                        if (++slot == a.slots) {
+                            slot = 0;
+                            phase ^= 1u;
+                            wrapped = true;
                         }
                     }
-                    if (!go) break;
-                }
-                const uint32_t bytes = (uint32_t)((size_t)cur.nr * cur.K * 2);
-                mbar_expect_tx(&ring.full[slot], bytes);
-                bulk_load_hint(ring.base + (size_t)slot * a.slot_bytes, cur.w + (size_t)cur.r0 * cur.K, bytes,
-                               &ring.full[slot], policy);
-                cur.advance(a, c, G);
-                if (pre.valid) {
-                    prefetch_l2(pre.w + (size_t)pre.r0 * pre.K, (uint32_t)((size_t)pre.nr * pre.K * 2));
-                    pre.advance(a, c, G);
                 }
             }
-            *s_issued = (int)q;
+            *s_issued = issued;
         }
         __syncwarp();
     } else {  // ------------------------------------------------ compute warps
-        unsigned long long q = 0;
-        const Range RH = range_of(a.H, 1, a.H, c, G, a.slot_bytes);  // residual rows owned by this CTA
+        Cursor cur;
+        const OpDesc op_qkv = ops[kOpQkv], op_o = ops[kOpO], op_gu = ops[kOpGu], op_down = ops[kOpDown],
+                     op_head = ops[kOpHead];
+        const int r_lo = op_o.lo, r_hi = op_o.hi;  // residual rows owned by this CTA
         bool ok = true;
         int steps_done = 0;
         uint32_t token = 0, next_token = 0;
@@ -823,26 +897,31 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 xs[i] = v;
             }
             compute_sync();
-            for (int i = tid; i < RH.hi - RH.lo; i += kCompute) resid[i] = xs[RH.lo + i];
+            for (int i = tid; i < r_hi - r_lo; i += kCompute) resid[i] = xs[r_lo + i];
             for (int layer = 0; layer < a.L && ok; ++layer) {
                 const FusedLayer& Lr = layers[layer];
                 const uint32_t e_qkv = e0 + 5u * layer + 1u, e_attn = e_qkv + 1u, e_o = e_qkv + 2u,
                                e_gu = e_qkv + 3u, e_down = e_qkv + 4u;
-                // qkv: RMSNorm(residual) -> [q; k; v]
-                GainRegs gain;
-                gain.load(Lr.input_gain, a.H);
-                if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st));
-                if (!ok) break;
-                rms_norm_inplace(xs, a.H, gain, a.eps, red);
                 EpiCtx e{};
-                e.out = a.t_qkv;
-                e.epoch = e_qkv;
                 e.act = a.act;
-                ok = run_gemv<kEpiStore, KH>(ring, q, Lr.bqkv, (a.QH + 2 * a.KVH) * a.D, a.H, 1, xs, e);
-                if (!ok) break;
-                // attention: KV groups on CTAs 0..KVH-1
-                if (c < a.KVH) {
-                    ok = attention_group<RATIO, DPL>(a, Lr, c, pos, e_qkv, e_attn, scratch);
+                // qkv: RMSNorm(residual) -> [q; k; v]
+                {
+                    GainX<KH> gx;
+                    GainRegs gs;
+                    if (KH > 0) gx.load(Lr.input_gain, lane);
+                    else gs.load(Lr.input_gain, a.H);
+                    if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st));
+                    if (!ok) break;
+                    if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
+                    e.out = a.t_qkv;
+                    e.epoch = e_qkv;
+                    ok = run_gemv<kEpiStore, KH, NRH>(ring, cur, op_qkv, Lr.bqkv, xs, KH > 0 ? &gx : nullptr,
+                                                      a.eps, e);
+                    if (!ok) break;
+                }
+                // attention: one query head per CTA
+                if (c < a.QH) {
+                    ok = attention_head<DPL, PB>(a, Lr, c, pos, e_qkv, e_attn, scratch);
                     if (!ok) break;
                 }
                 // o: residual += Wo attn
@@ -851,24 +930,30 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 e.out = a.t_resid;
                 e.epoch = e_o;
                 e.resid = resid;
-                e.resid_lo = RH.lo;
-                ok = run_gemv<kEpiResidual, KQ>(ring, q, Lr.bo, a.H, a.QH * a.D, 1, xs, e);
+                e.resid_lo = r_lo;
+                ok = run_gemv<kEpiResidual, KQ, NRQ>(ring, cur, op_o, Lr.bo, xs, nullptr, a.eps, e);
                 if (!ok) break;
                 // gate/up: RMSNorm(residual) -> act(gate) * up
-                gain.load(Lr.post_gain, a.H);
-                ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st));
-                if (!ok) break;
-                rms_norm_inplace(xs, a.H, gain, a.eps, red);
-                e.out = a.t_feat;
-                e.epoch = e_gu;
-                ok = run_gemv<kEpiGated, KH>(ring, q, Lr.bgu, 2 * a.I, a.H, 2, xs, e);
-                if (!ok) break;
+                {
+                    GainX<KH> gx;
+                    GainRegs gs;
+                    if (KH > 0) gx.load(Lr.post_gain, lane);
+                    else gs.load(Lr.post_gain, a.H);
+                    ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st));
+                    if (!ok) break;
+                    if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
+                    e.out = a.t_feat;
+                    e.epoch = e_gu;
+                    ok = run_gemv<kEpiGated, KH, NRG>(ring, cur, op_gu, Lr.bgu, xs, KH > 0 ? &gx : nullptr,
+                                                      a.eps, e);
+                    if (!ok) break;
+                }
                 // down: residual += Wd feature
                 ok = compute_and(poll_vector(a.t_feat, a.I, e_gu, xs, st));
                 if (!ok) break;
                 e.out = a.t_resid;
                 e.epoch = e_down;
-                ok = run_gemv<kEpiResidual, KI>(ring, q, Lr.bd, a.H, a.I, 1, xs, e);
+                ok = run_gemv<kEpiResidual, KI, NRI>(ring, cur, op_down, Lr.bd, xs, nullptr, a.eps, e);
             }
             if (!ok) break;
             // ---- head: final RMSNorm, optional edit, logits and first argmax
@@ -931,10 +1016,11 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             EpiCtx e{};
             e.logits = logits;
             e.best = 0ull;
-            ok = run_gemv<kEpiHead, KH>(ring, q, a.head_bias, a.V, a.H, 1, xs, e);
+            ok = run_gemv<kEpiHead, KH, NRH>(ring, cur, op_head, a.head_bias, xs, nullptr, a.eps, e);
             if (!ok) break;
             unsigned long long* rb = reinterpret_cast<unsigned long long*>(red);
-            if (lane == 0) rb[warp] = e.best;
+            const unsigned long long wbest = warp_max_u64(e.best);
+            if (lane == 0) rb[warp] = wbest;
             if (!compute_and(!e.bad) && tid == 0) atomicOr(&st->nonfinite, 1);
             if (tid == 0) {
                 unsigned long long b = 0ull;
@@ -1002,17 +1088,59 @@ using PKernel = void (*)(const PArgs);
 
 PKernel kernel_for(const FusedConfig& c) {
     const int qw = c.qheads * c.head_dim;
-    const int ratio = c.qheads / c.kvheads, dpl = c.head_dim / 32;
-    // Register-resident x needs compile-time widths; attention shapes likewise.
-    if (c.hidden == 1024 && qw == 2048 && c.intermediate == 3072 && ratio == 2 && dpl == 4)
-        return persistent_decode_kernel<4, 8, 12, 2, 4>;  // Qwen3-0.6B
-    if (c.hidden == 2560 && ratio == 4 && dpl == 4) return persistent_decode_kernel<10, 0, 0, 4, 4>;  // Qwen3-4B
-    if (ratio == 4 && dpl == 4) return persistent_decode_kernel<0, 0, 0, 4, 4>;  // Qwen3-8B and others
-    if (ratio == 2 && dpl == 4) return persistent_decode_kernel<0, 0, 0, 2, 4>;
-    if (ratio == 2 && dpl == 2) return persistent_decode_kernel<0, 0, 0, 2, 2>;
-    if (ratio == 1 && dpl == 4) return persistent_decode_kernel<0, 0, 0, 1, 4>;
-    if (ratio == 8 && dpl == 4) return persistent_decode_kernel<0, 0, 0, 8, 4>;
+    const int dpl = c.head_dim / 32;
+    // Register-resident x needs compile-time widths; attention likewise.
+    if (c.hidden == 1024 && qw == 2048 && c.intermediate == 3072 && dpl == 4)
+        return persistent_decode_kernel<4, 8, 12, 4>;  // Qwen3-0.6B
+    if (c.hidden == 2560 && dpl == 4) return persistent_decode_kernel<10, 0, 0, 4>;  // Qwen3-4B
+    if (dpl == 4) return persistent_decode_kernel<0, 0, 0, 4>;
+    if (dpl == 2) return persistent_decode_kernel<0, 0, 0, 2>;
+    if (dpl == 8) return persistent_decode_kernel<0, 0, 0, 8>;
     return nullptr;
+}
+
+int scratch_floats(const FusedConfig& c) {
+    const int D = c.head_dim;
+    const int attention = 3 * D + kWarps * (D + 2) + 3 * D;
+    return (std::max(attention, 512 + 2 * 256) + 3) & ~3;
+}
+
+// Shared-memory layout for `slots` ring slots.
+SmemLayout layout_for(const FusedConfig& c, int slots, int slot_bytes, int grid, size_t layers) {
+    const int qw = c.qheads * c.head_dim;
+    const int xmax = (std::max(std::max(c.hidden, qw), c.intermediate) + 3) & ~3;
+    const int rmax = ((c.hidden + grid - 1) / grid + 1 + 3) & ~3;
+    SmemLayout s{};
+    size_t at = (size_t)slots * slot_bytes;
+    s.xs = (int)at;
+    at += (size_t)xmax * 4;
+    s.scratch = (int)at;
+    at += (size_t)scratch_floats(c) * 4;
+    s.resid = (int)at;
+    at += (size_t)rmax * 4;
+    s.red = (int)at;
+    at += 64 * 4;
+    s.full = (int)at;
+    at += (size_t)slots * 8;
+    s.empty = (int)at;
+    at += (size_t)slots * 8;
+    s.flags = (int)at;
+    at += 16;
+    s.ops = (int)at;
+    at += (kOps * sizeof(OpDesc) + 15) & ~(size_t)15;
+    s.layers = (int)at;
+    at += layers * sizeof(FusedLayer);
+    s.total = (int)at;
+    return s;
+}
+
+int slot_bytes_for(const FusedConfig& c) {
+    const int qw = c.qheads * c.head_dim;
+    int slot_bytes = 16384;
+    const int ks[4] = {c.hidden, qw, c.hidden, c.intermediate};
+    const int units[4] = {1, 1, 2, 1};
+    for (int i = 0; i < 4; ++i) slot_bytes = std::max(slot_bytes, units[i] * ks[i] * 2);
+    return (slot_bytes + 127) & ~127;
 }
 
 }  // namespace
@@ -1024,20 +1152,19 @@ PersistentDecoder::~PersistentDecoder() {
 bool PersistentDecoder::eligible(const FusedConfig& c, const lsx_ctx* ctx, std::string* why) {
     if (!FusedDecoder::eligible(c, why)) return false;
     if (!kernel_for(c)) {
-        if (why) *why = "no persistent kernel instantiation for this GQA ratio / head_dim";
-        return false;
-    }
-    const int ratio = c.qheads / c.kvheads;
-    if (ratio == 8 && c.head_dim == 256) {
-        if (why) *why = "GQA ratio 8 with head_dim 256";
+        if (why) *why = "no persistent kernel instantiation for this head_dim";
         return false;
     }
     if (c.vocab > 0x7FFFF) {
         if (why) *why = "vocabulary above 524287";
         return false;
     }
-    if (c.kvheads > ctx->sm_count) {
-        if (why) *why = "more KV heads than SMs";
+    if (c.qheads > ctx->sm_count) {
+        if (why) *why = "more query heads than SMs";
+        return false;
+    }
+    if (c.hidden > kGainRegs * kCompute) {
+        if (why) *why = "hidden width above the register-gain limit";
         return false;
     }
     return true;
@@ -1077,22 +1204,19 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
         LSX_CUDA(cudaMemcpy(rope_, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice),
                  "rope table upload");
     }
-    // Shared memory: ring slots, x buffer, attention/edit scratch, owned residual rows.
-    int slot_bytes = 16384;
-    const int ks[4] = {c.hidden, qw, c.hidden, c.intermediate};
-    const int units[4] = {1, 1, 2, 1};
-    for (int i = 0; i < 4; ++i) slot_bytes = std::max(slot_bytes, units[i] * ks[i] * 2);
-    slot_bytes = (slot_bytes + 127) & ~127;
-    const int ratio = c.qheads / c.kvheads;
-    const int xmax = (std::max(std::max(c.hidden, qw), c.intermediate) + 3) & ~3;
-    const int scratch = (std::max((2 * ratio + 3) * c.head_dim + 8 * ratio * (c.head_dim + 2), 512) + 3) & ~3;
-    const int rmax = ((c.hidden + grid_ - 1) / grid_ + 1 + 3) & ~3;
-    const size_t fixed = (size_t)(xmax + scratch + rmax + 64) * 4 + 16 + 16 + layers.size() * sizeof(FusedLayer);
+    // Shared memory: ring slots first, then x, scratch, owned residual rows,
+    // barriers and the tables.  As many slots as fit, at most 16.
+    const int slot_bytes = slot_bytes_for(c);
     const size_t limit = ctx->smem_optin;
-    if (fixed + 2 * (size_t)slot_bytes + 32 > limit) return fail(LSX_E_UNSUPPORTED, "persistent decode plan: smem");
-    slots_ = (int)((limit - fixed - 64) / ((size_t)slot_bytes + 16));
-    if (slots_ > 16) slots_ = 16;
-    smem_ = (size_t)slots_ * slot_bytes + fixed + (size_t)slots_ * 16 + 16;
+    slots_ = 0;
+    for (int s = 16; s >= 2; --s)
+        if ((size_t)layout_for(c, s, slot_bytes, grid_, layers.size()).total <= limit) {
+            slots_ = s;
+            break;
+        }
+    if (slots_ == 0) return fail(LSX_E_UNSUPPORTED, "persistent decode plan: shared memory");
+    layer_count_ = (int)layers.size();
+    smem_ = (size_t)layout_for(c, slots_, slot_bytes, grid_, layers.size()).total;
     PKernel k = kernel_for(c);
     LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_),
              "persistent smem attribute");
@@ -1134,27 +1258,8 @@ int PersistentDecoder::run(int steps) {
     a.state = state_;
     a.steps = steps;
     a.slots = slots_;
-    const int qw = c.qheads * c.head_dim;
-    int slot_bytes = 16384;
-    const int ks[4] = {c.hidden, qw, c.hidden, c.intermediate};
-    const int units[4] = {1, 1, 2, 1};
-    for (int i = 0; i < 4; ++i) slot_bytes = std::max(slot_bytes, units[i] * ks[i] * 2);
-    a.slot_bytes = (slot_bytes + 127) & ~127;
-    const int ratio = c.qheads / c.kvheads;
-    a.xmax = (std::max(std::max(c.hidden, qw), c.intermediate) + 3) & ~3;
-    a.scratch = (std::max((2 * ratio + 3) * c.head_dim + 8 * ratio * (c.head_dim + 2), 512) + 3) & ~3;
-    a.rmax = ((c.hidden + grid_ - 1) / grid_ + 1 + 3) & ~3;
-    // About one layer of this CTA's chunks: 4 GEMV ops of roughly 16 KB chunks.
-    {
-        const size_t layer_bytes = (size_t)2 * c.hidden * ((size_t)(c.qheads + 2 * c.kvheads) * c.head_dim + 2 * c.intermediate) +
-                                   (size_t)2 * c.hidden * ((size_t)c.qheads * c.head_dim + c.intermediate);
-        const size_t per_cta = layer_bytes / grid_;
-        (void)per_cta;
-        a.prefetch = 0;  // measured: L2 prefetch through the bulk-copy engine slows the stream
-    }
-    // Layer table after the barriers and flags, 8-byte aligned.
-    a.layers_offset = (int)(((size_t)a.slots * a.slot_bytes + (size_t)(a.xmax + a.scratch + a.rmax + 64) * 4 +
-                             (size_t)a.slots * 16 + 16 + 15) & ~(size_t)15);
+    a.slot_bytes = slot_bytes_for(c);
+    a.sm = layout_for(c, slots_, a.slot_bytes, grid_, (size_t)layer_count_);
     void* args[] = {&a};
     LSX_CUDA(cudaLaunchCooperativeKernel((const void*)kernel_for(c), dim3(grid_), dim3(kThreads), args, smem_,
                                          ctx_->stream),

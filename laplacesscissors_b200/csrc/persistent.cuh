@@ -33,6 +33,7 @@ private:
     size_t smem_ = 0;
     int slots_ = 0;
     int grid_ = 0;
+    int layer_count_ = 0;
     std::vector<void*> owned_;
 };
 
