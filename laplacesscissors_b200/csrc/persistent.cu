@@ -384,26 +384,52 @@ struct GainX {
     }
 };
 
-// RMSNorm (kernels/ops.py:31-45) of the register copy of x: x * rsqrt(mean(x^2) + eps) * gain.
+// RMSNorm (kernels/ops.py:31-45) split for latency: x * gain feeds the dot
+// products at once, and rsqrt(mean(x^2) + eps) (four independent chains, then one
+// warp reduction) multiplies each row total in the epilogue, off the critical path.
 template <int KCH>
-__device__ __forceinline__ void norm_regs(XRegs<KCH>& x, const GainX<KCH>& g, int n, float eps) {
-    float ss = 0.f;
+__device__ __forceinline__ float gain_regs_rms(XRegs<KCH>& x, const GainX<KCH>& g, int n, float eps) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
     for (int j = 0; j < 2 * KCH; ++j) {
-        ss = fmaf(x.v[j].x, x.v[j].x, ss);
-        ss = fmaf(x.v[j].y, x.v[j].y, ss);
-        ss = fmaf(x.v[j].z, x.v[j].z, ss);
-        ss = fmaf(x.v[j].w, x.v[j].w, ss);
+        s0 = fmaf(x.v[j].x, x.v[j].x, s0);
+        s1 = fmaf(x.v[j].y, x.v[j].y, s1);
+        s2 = fmaf(x.v[j].z, x.v[j].z, s2);
+        s3 = fmaf(x.v[j].w, x.v[j].w, s3);
+        x.v[j].x *= g.g[4 * j + 0];
+        x.v[j].y *= g.g[4 * j + 1];
+        x.v[j].z *= g.g[4 * j + 2];
+        x.v[j].w *= g.g[4 * j + 3];
     }
-    ss = warp_allsum(ss);
-    const float inverse = rsqrtf(ss / (float)n + eps);
-#pragma unroll
-    for (int j = 0; j < 2 * KCH; ++j) {
-        x.v[j].x = x.v[j].x * inverse * g.g[4 * j + 0];
-        x.v[j].y = x.v[j].y * inverse * g.g[4 * j + 1];
-        x.v[j].z = x.v[j].z * inverse * g.g[4 * j + 2];
-        x.v[j].w = x.v[j].w * inverse * g.g[4 * j + 3];
+    const float ss = warp_allsum((s0 + s1) + (s2 + s3));
+    return rsqrtf(ss / (float)n + eps);
+}
+
+// Waits for the chunks of the window starting at the cursor: one pass of
+// independent tests, then bounded waits only if some chunk has not landed.
+__device__ __forceinline__ bool window_landed(const Ring& ring, const Cursor& cur, int wn) {
+    bool all = true;
+    for (int ch = 0; ch < wn; ++ch) {
+        int s;
+        uint32_t p;
+        cur.at(ch, ring.slots, &s, &p);
+        all &= mbar_try_wait(smem_u32(&ring.full[s]), p);
     }
+    if (!all) {
+        all = true;
+        for (int ch = 0; ch < wn; ++ch) {
+            int s;
+            uint32_t p;
+            cur.at(ch, ring.slots, &s, &p);
+            all &= mbar_wait_bounded(&ring.full[s], p);
+        }
+    }
+    return __all_sync(0xffffffffu, all);
+}
+
+// The first window of an op, waited for ahead of the activations it multiplies.
+__device__ __forceinline__ bool first_window_landed(const Ring& ring, const Cursor& cur, const OpDesc& op) {
+    return op.nch == 0 || window_landed(ring, cur, min(op.win, op.nch));
 }
 
 // One GEMV op over this CTA's rows: consumes its chunks from the ring window by
@@ -412,15 +438,17 @@ __device__ __forceinline__ void norm_regs(XRegs<KCH>& x, const GainX<KCH>& g, in
 // `gain` is given); KCH == 0: any K % 8 == 0, x read from shared memory.
 template <int EPI, int KCH, int NR>
 __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const OpDesc& op, const float* bias,
-                                         const float* xs, const GainX<KCH>* gain, float eps, EpiCtx& e) {
+                                         const float* xs, const GainX<KCH>* gain, float eps, EpiCtx& e,
+                                         bool first_ready) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = op.K;
     const uint32_t row_bytes = (uint32_t)K * 2u;
     const int mask = (1 << op.shift) - 1;
     XRegs<KCH> x;
+    float inverse = 1.f;
     if (KCH > 0) {
         x.load(xs, lane);
-        if (gain) norm_regs<KCH>(x, *gain, K, eps);
+        if (gain) inverse = gain_regs_rms<KCH>(x, *gain, K, eps);
     }
     constexpr int kLanesPerRow = 32 / NR;
     const int my_row = lane / kLanesPerRow;  // row of the pass this lane ends up holding
@@ -430,15 +458,9 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
         const int wn = min(op.win, op.nch - w0);
         const int rs = op.lo + (w0 << op.shift);
         const int re = min(op.hi, op.lo + ((w0 + wn) << op.shift));
-        // Wait once for every chunk of the window (immediate when already landed).
-        bool landed = true;
-        for (int ch = 0; ch < wn; ++ch) {
-            int s;
-            uint32_t p;
-            cur.at(ch, ring.slots, &s, &p);
-            landed &= mbar_wait_bounded(&ring.full[s], p);
-        }
-        ok = __all_sync(0xffffffffu, landed);
+        // Wait once for every chunk of the window (the first one usually before the
+        // activations were polled).
+        ok = (w0 == 0 && first_ready) || window_landed(ring, cur, wn);
         if (ok) {
             for (int r0 = rs + warp * NR; r0 < re; r0 += kWarps * NR) {
                 const uint8_t* rp[NR];
@@ -477,7 +499,7 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                     for (int i = 0; i < NR; ++i) acc[i] = a0[i] + a1[i];
                 }
                 RowReduce<NR, 16>::run(acc, lane);
-                float d = acc[0];
+                float d = gain ? acc[0] * inverse : acc[0];
                 const int r = r0 + my_row;
                 const bool valid = owner && r < re;
                 if (EPI == kEpiGated) {
@@ -910,13 +932,14 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     GainRegs gs;
                     if (KH > 0) gx.load(Lr.input_gain, lane);
                     else gs.load(Lr.input_gain, a.H);
+                    const bool ready = first_window_landed(ring, cur, op_qkv);
                     if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st));
                     if (!ok) break;
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
                     e.out = a.t_qkv;
                     e.epoch = e_qkv;
                     ok = run_gemv<kEpiStore, KH, NRH>(ring, cur, op_qkv, Lr.bqkv, xs, KH > 0 ? &gx : nullptr,
-                                                      a.eps, e);
+                                                      a.eps, e, ready);
                     if (!ok) break;
                 }
                 // attention: one query head per CTA
@@ -925,13 +948,14 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     if (!ok) break;
                 }
                 // o: residual += Wo attn
+                bool ready = first_window_landed(ring, cur, op_o);
                 ok = compute_and(poll_vector(a.t_attn, a.QH * a.D, e_attn, xs, st));
                 if (!ok) break;
                 e.out = a.t_resid;
                 e.epoch = e_o;
                 e.resid = resid;
                 e.resid_lo = r_lo;
-                ok = run_gemv<kEpiResidual, KQ, NRQ>(ring, cur, op_o, Lr.bo, xs, nullptr, a.eps, e);
+                ok = run_gemv<kEpiResidual, KQ, NRQ>(ring, cur, op_o, Lr.bo, xs, nullptr, a.eps, e, ready);
                 if (!ok) break;
                 // gate/up: RMSNorm(residual) -> act(gate) * up
                 {
@@ -939,21 +963,23 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     GainRegs gs;
                     if (KH > 0) gx.load(Lr.post_gain, lane);
                     else gs.load(Lr.post_gain, a.H);
+                    ready = first_window_landed(ring, cur, op_gu);
                     ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st));
                     if (!ok) break;
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
                     e.out = a.t_feat;
                     e.epoch = e_gu;
                     ok = run_gemv<kEpiGated, KH, NRG>(ring, cur, op_gu, Lr.bgu, xs, KH > 0 ? &gx : nullptr,
-                                                      a.eps, e);
+                                                      a.eps, e, ready);
                     if (!ok) break;
                 }
                 // down: residual += Wd feature
+                ready = first_window_landed(ring, cur, op_down);
                 ok = compute_and(poll_vector(a.t_feat, a.I, e_gu, xs, st));
                 if (!ok) break;
                 e.out = a.t_resid;
                 e.epoch = e_down;
-                ok = run_gemv<kEpiResidual, KI, NRI>(ring, cur, op_down, Lr.bd, xs, nullptr, a.eps, e);
+                ok = run_gemv<kEpiResidual, KI, NRI>(ring, cur, op_down, Lr.bd, xs, nullptr, a.eps, e, ready);
             }
             if (!ok) break;
             // ---- head: final RMSNorm, optional edit, logits and first argmax
@@ -1016,7 +1042,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             EpiCtx e{};
             e.logits = logits;
             e.best = 0ull;
-            ok = run_gemv<kEpiHead, KH, NRH>(ring, cur, op_head, a.head_bias, xs, nullptr, a.eps, e);
+            ok = run_gemv<kEpiHead, KH, NRH>(ring, cur, op_head, a.head_bias, xs, nullptr, a.eps, e, false);
             if (!ok) break;
             unsigned long long* rb = reinterpret_cast<unsigned long long*>(red);
             const unsigned long long wbest = warp_max_u64(e.best);
