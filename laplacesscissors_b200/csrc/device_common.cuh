@@ -64,6 +64,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+// Orders this thread's (and, after a block barrier, the block's) earlier generic
+// accesses to shared memory before its later async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // 1-D bulk copy global -> shared completing on `bar` (bytes % 16 == 0, both
 // addresses 16-byte aligned).  The source is this GPU's own memory.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {

@@ -36,6 +36,17 @@
 #include "device_common.cuh"
 #include "persistent.cuh"
 
+// Phase marks for timing builds; empty in the library.
+#ifndef LSX_PHASE_MARK
+#define LSX_PHASE_MARK(k)
+#endif
+#ifndef LSX_HEAD_MARK
+#define LSX_HEAD_MARK(k)
+#endif
+#ifndef LSX_WINDOW_MARK
+#define LSX_WINDOW_MARK(k)
+#endif
+
 namespace lsx {
 namespace {
 
@@ -281,6 +292,7 @@ struct Ring {
 struct Cursor {
     int slot = 0;
     uint32_t phase = 0;
+    long long consumed = 0;  // chunks consumed so far
     __device__ __forceinline__ void at(int ahead, int slots, int* s, uint32_t* p) const {
         int t = slot + ahead;
         uint32_t q = phase;
@@ -292,6 +304,7 @@ struct Cursor {
         *p = q;
     }
     __device__ __forceinline__ void advance(int n, int slots) {
+        consumed += n;
         slot += n;
         if (slot >= slots) {
             slot -= slots;
@@ -460,7 +473,9 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
         const int re = min(op.hi, op.lo + ((w0 + wn) << op.shift));
         // Wait once for every chunk of the window (the first one usually before the
         // activations were polled).
+        LSX_WINDOW_MARK(0);
         ok = (w0 == 0 && first_ready) || window_landed(ring, cur, wn);
+        LSX_WINDOW_MARK(1);
         if (ok) {
             for (int r0 = rs + warp * NR; r0 < re; r0 += kWarps * NR) {
                 const uint8_t* rp[NR];
@@ -530,7 +545,9 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                 }
             }
         }
+        LSX_WINDOW_MARK(4);
         ok = compute_and(ok);
+        LSX_WINDOW_MARK(2);
         if (tid == 0)
             for (int ch = 0; ch < wn; ++ch) {
                 int s;
@@ -926,6 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                                e_gu = e_qkv + 3u, e_down = e_qkv + 4u;
                 EpiCtx e{};
                 e.act = a.act;
+                LSX_PHASE_MARK(0);
                 // qkv: RMSNorm(residual) -> [q; k; v]
                 {
                     GainX<KH> gx;
@@ -935,28 +953,33 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     const bool ready = first_window_landed(ring, cur, op_qkv);
                     if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st));
                     if (!ok) break;
+                    LSX_PHASE_MARK(1);
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
                     e.out = a.t_qkv;
                     e.epoch = e_qkv;
                     ok = run_gemv<kEpiStore, KH, NRH>(ring, cur, op_qkv, Lr.bqkv, xs, KH > 0 ? &gx : nullptr,
                                                       a.eps, e, ready);
                     if (!ok) break;
+                    LSX_PHASE_MARK(3);
                 }
                 // attention: one query head per CTA
                 if (c < a.QH) {
                     ok = attention_head<DPL, PB>(a, Lr, c, pos, e_qkv, e_attn, scratch);
                     if (!ok) break;
                 }
+                LSX_PHASE_MARK(4);
                 // o: residual += Wo attn
                 bool ready = first_window_landed(ring, cur, op_o);
                 ok = compute_and(poll_vector(a.t_attn, a.QH * a.D, e_attn, xs, st));
                 if (!ok) break;
+                LSX_PHASE_MARK(5);
                 e.out = a.t_resid;
                 e.epoch = e_o;
                 e.resid = resid;
                 e.resid_lo = r_lo;
                 ok = run_gemv<kEpiResidual, KQ, NRQ>(ring, cur, op_o, Lr.bo, xs, nullptr, a.eps, e, ready);
                 if (!ok) break;
+                LSX_PHASE_MARK(6);
                 // gate/up: RMSNorm(residual) -> act(gate) * up
                 {
                     GainX<KH> gx;
@@ -966,28 +989,34 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     ready = first_window_landed(ring, cur, op_gu);
                     ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st));
                     if (!ok) break;
+                    LSX_PHASE_MARK(7);
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
                     e.out = a.t_feat;
                     e.epoch = e_gu;
                     ok = run_gemv<kEpiGated, KH, NRG>(ring, cur, op_gu, Lr.bgu, xs, KH > 0 ? &gx : nullptr,
                                                       a.eps, e, ready);
                     if (!ok) break;
+                    LSX_PHASE_MARK(9);
                 }
                 // down: residual += Wd feature
                 ready = first_window_landed(ring, cur, op_down);
                 ok = compute_and(poll_vector(a.t_feat, a.I, e_gu, xs, st));
                 if (!ok) break;
+                LSX_PHASE_MARK(10);
                 e.out = a.t_resid;
                 e.epoch = e_down;
                 ok = run_gemv<kEpiResidual, KI, NRI>(ring, cur, op_down, Lr.bd, xs, nullptr, a.eps, e, ready);
+                LSX_PHASE_MARK(11);
             }
             if (!ok) break;
             // ---- head: final RMSNorm, optional edit, logits and first argmax
             const uint32_t e_last = e0 + 5u * (uint32_t)a.L, e_head = e_last + 1u;
             GainRegs fgain;
             fgain.load(a.final_gain, a.H);
+            LSX_HEAD_MARK(0);
             ok = compute_and(poll_vector(a.t_resid, a.H, e_last, xs, st));
             if (!ok) break;
+            LSX_HEAD_MARK(1);
             rms_norm_inplace(xs, a.H, fgain, a.eps, red);
             const int slot_idx = step - (P - 1);
             const bool framed = frames && slot_idx >= 0;
@@ -1042,8 +1071,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             EpiCtx e{};
             e.logits = logits;
             e.best = 0ull;
+            LSX_HEAD_MARK(2);
             ok = run_gemv<kEpiHead, KH, NRH>(ring, cur, op_head, a.head_bias, xs, nullptr, a.eps, e, false);
             if (!ok) break;
+            LSX_HEAD_MARK(3);
             unsigned long long* rb = reinterpret_cast<unsigned long long*>(red);
             const unsigned long long wbest = warp_max_u64(e.best);
             if (lane == 0) rb[warp] = wbest;
@@ -1070,6 +1101,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 gathered[tid] = v;
             }
             ok = compute_and(ok);
+            LSX_HEAD_MARK(4);
             if (!ok) {
                 raise_abort(st, kDeviceTimeoutEpilogue);
                 break;
