@@ -55,7 +55,13 @@ struct ReadoutParams {
     unsigned long long* other_key;  // [M] packed (value, index) of the best non-target
     float* target_logit;            // [M]
     int* status;                    // [0] device error code, [1] non-finite flag
+    // image mode: the extension block [V, image_stride] receives F = W U^T for
+    // ranks [image_k0, image_k0 + M / 2) of `image_rank` as [F_hi | F_hi | F_lo]
+    __nv_bfloat16* image;
+    int image_stride, image_rank, image_k0;
 };
+
+enum { kModeMargin = 0, kModeImage = 1 };
 
 // ---------------------------------------------------------------- PTX ------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -132,7 +138,10 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     return true;
 }
 
-template <int PLANES, int STAGES>
+// MODE kModeMargin: the margin epilogue above.  MODE kModeImage: A holds the
+// edit basis as interleaved (hi, lo) bf16 rows and the epilogue writes the edit
+// image F = W U^T (each rank's two TMEM lanes summed) into the B extension.
+template <int PLANES, int STAGES, int MODE>
 __global__ void __launch_bounds__(kReadoutThreads, 1)
     readout_margin_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                           const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_ea,
@@ -297,6 +306,40 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 break;
             }
             tc_fence_after();
+            if (MODE == kModeImage) {
+                // TMEM lane 2k + 0/1: rank k's hi/lo part; lanes of one rank are adjacent.
+                const int kl = row_local >> 1;
+                const bool writer = (lane & 1) == 0 && 2 * kl < p.M;
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
+                const int k = p.image_k0 + kl;
+#pragma unroll 1
+                for (int c = 0; c < RN / 32; ++c) {
+                    uint32_t r[32];
+                    tc_ld32(taddr + (uint32_t)(c * 32), r);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float v = __uint_as_float(r[i]);
+                        const float f = v + __shfl_down_sync(0xffffffffu, v, 1);
+                        const int n = n0 + c * 32 + i;
+                        if (writer && n < p.V) {
+                            const __nv_bfloat16 hi = __float2bfloat16_rn(f);
+                            const __nv_bfloat16 lo = __float2bfloat16_rn(f - __bfloat162float(hi));
+                            __nv_bfloat16* dst = p.image + (size_t)n * p.image_stride;
+                            dst[k] = hi;
+                            dst[p.image_rank + k] = hi;
+                            dst[2 * p.image_rank + k] = lo;
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&tmem_empty[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                continue;
+            }
             const int row = m0 + row_local;
             const bool live = row < p.M;
             const int tcol = live ? (int)p.targets[row] - n0 : -1;
@@ -354,67 +397,17 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
 }
 
 // ------------------------------------------------------------ prep kernels --
-// F = W U^T for ranks [k0, k0 + kc), written as split bf16 into the extension
-// block of B: columns [k] = hi(F), [r + k] = hi(F), [2r + k] = lo(F).  One lane
-// per vocab row: a warp streams 32 rows chunk by chunk (each 16-byte chunk of a
-// row shares its 128-byte line with the lane's next seven chunks), and every
-// lane reads the same U values, so shared-memory reads are broadcasts.
-__global__ void __launch_bounds__(256) edit_image_kernel(const __nv_bfloat16* __restrict__ W, int V, int H,
-                                                         const float* __restrict__ basis, int rank, int k0, int kc,
-                                                         __nv_bfloat16* __restrict__ ext_b, int ext_k) {
-    extern __shared__ float us[];  // kc x H
-    for (int i = threadIdx.x; i < kc * H; i += blockDim.x) us[i] = basis[(size_t)k0 * H + i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int warps_total = gridDim.x * (blockDim.x >> 5);
-    for (int base = (blockIdx.x * (blockDim.x >> 5) + warp) * 32; base < V; base += warps_total * 32) {
-        const int j = base + lane;
-        const bool live = j < V;
-        const uint4* row = reinterpret_cast<const uint4*>(W + (size_t)(live ? j : 0) * H);
-        float acc[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-        for (int c = 0; c < H / 8; ++c) {
-            const uint4 w = __ldg(row + c);
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
-            float wf[8];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float2 f = __bfloat1622float2(h2[q]);
-                wf[2 * q] = f.x;
-                wf[2 * q + 1] = f.y;
-            }
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                if (k < kc) {
-                    const float4 u0 = *reinterpret_cast<const float4*>(us + k * H + c * 8);
-                    const float4 u1 = *reinterpret_cast<const float4*>(us + k * H + c * 8 + 4);
-                    float s = acc[k];
-                    s = fmaf(wf[0], u0.x, s);
-                    s = fmaf(wf[1], u0.y, s);
-                    s = fmaf(wf[2], u0.z, s);
-                    s = fmaf(wf[3], u0.w, s);
-                    s = fmaf(wf[4], u1.x, s);
-                    s = fmaf(wf[5], u1.y, s);
-                    s = fmaf(wf[6], u1.z, s);
-                    s = fmaf(wf[7], u1.w, s);
-                    acc[k] = s;
-                }
-            }
-        }
-        if (live) {
-            __nv_bfloat16* dst = ext_b + (size_t)j * ext_k;
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                if (k < kc) {
-                    const __nv_bfloat16 hi = __float2bfloat16_rn(acc[k]);
-                    const __nv_bfloat16 lo = __float2bfloat16_rn(acc[k] - __bfloat162float(hi));
-                    dst[k0 + k] = hi;
-                    dst[rank + k0 + k] = hi;
-                    dst[2 * rank + k0 + k] = lo;
-                }
-            }
-        }
+// The edit basis U [rank, H] f32 as the A operand of the image GEMM: rows 2k and
+// 2k + 1 hold bf16 hi and lo of U's row k0 + k.
+__global__ void basis_split_kernel(const float* __restrict__ basis, int H, int k0, int kc,
+                                   __nv_bfloat16* __restrict__ out) {
+    const int total = kc * H;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int k = i / H, j = i - k * H;
+        const float u = basis[(size_t)(k0 + k) * H + j];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(u);
+        out[(size_t)(2 * k) * H + j] = hi;
+        out[(size_t)(2 * k + 1) * H + j] = __float2bfloat16_rn(u - __bfloat162float(hi));
     }
 }
 
@@ -530,9 +523,11 @@ int make_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, u
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+constexpr int kImageRanks = RM / 2;  // ranks per image pass (two A rows each)
+
 struct Layout {
-    size_t ext_k, planes_off, planes_bytes, ext_a_off, ext_b_off, basis_off, delta_off, key_off, tlog_off,
-        status_off, total;
+    size_t ext_k, planes_off, planes_bytes, ext_a_off, ext_b_off, basis_off, delta_off, image_a_off, key_off,
+        tlog_off, status_off, total;
 };
 
 Layout layout_for(size_t vocab, size_t width, size_t rows, size_t rank, bool f32_hidden) {
@@ -550,6 +545,8 @@ Layout layout_for(size_t vocab, size_t width, size_t rows, size_t rank, bool f32
     at = align256(at + rank * width * 4);
     L.delta_off = at;
     at = align256(at + rank * rank * 4);
+    L.image_a_off = at;
+    at = align256(at + 2 * std::min(rank, (size_t)kImageRanks) * width * 2);
     L.key_off = at;
     at = align256(at + rows * 8);
     L.tlog_off = at;
@@ -612,15 +609,35 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
         LSX_CUDA(cudaMemcpyAsync(ddelta, d.data(), d.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
         LSX_CUDA(cudaStreamSynchronize(s), "edit upload");  // host vectors go out of scope
         LSX_CUDA(cudaMemsetAsync(ext_b, 0, vocab * L.ext_k * 2, s), "extension clear");
-        const int kc_max = std::max(1, std::min(16, (int)(65536 / (width * 4))));
-        for (int k0 = 0; k0 < (int)rank; k0 += kc_max) {
-            const int kc = std::min(kc_max, (int)rank - k0);
-            const size_t smem = (size_t)kc * width * 4;
-            LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                     "edit image smem attribute");
-            edit_image_kernel<<<std::min(ctx->sm_count * 2, (V + 255) / 256), 256, smem, s>>>(
-                (const __nv_bfloat16*)weight->data, V, H, dbasis, (int)rank, k0, kc, ext_b, (int)L.ext_k);
+        // F = W U^T on the tensor cores, up to kImageRanks ranks per pass.
+        __nv_bfloat16* image_a = (__nv_bfloat16*)(ws + L.image_a_off);
+        CUtensorMap mw;
+        LSX_TRY(make_map(&mw, weight->data, width, vocab, width * 2, RN));
+        auto ik = readout_margin_kernel<1, 4, kModeImage>;
+        const size_t ismem = readout_smem<1, 4>();
+        LSX_CUDA(cudaFuncSetAttribute((const void*)ik, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem),
+                 "edit image smem attribute");
+        for (int k0 = 0; k0 < (int)rank; k0 += kImageRanks) {
+            const int kc = std::min(kImageRanks, (int)rank - k0);
+            basis_split_kernel<<<std::min(ctx->sm_count, (kc * H + 255) / 256), 256, 0, s>>>(dbasis, H, k0, kc,
+                                                                                           image_a);
+            LSX_CUDA(cudaGetLastError(), "edit basis split");
+            CUtensorMap mu;
+            LSX_TRY(make_map(&mu, image_a, width, 2 * (size_t)kc, width * 2, RM));
+            ReadoutParams q{};
+            q.M = 2 * kc;
+            q.V = V;
+            q.H = H;
+            q.k_blocks = (H + RK - 1) / RK;
+            q.ext_blocks = 0;
+            q.m_tiles = 1;
+            q.n_tiles = (V + RN - 1) / RN;
+            q.status = status;
+            q.image = ext_b;
+            q.image_stride = (int)L.ext_k;
+            q.image_rank = (int)rank;
+            q.image_k0 = k0;
+            ik<<<std::min(q.n_tiles, ctx->sm_count), kReadoutThreads, ismem, s>>>(mu, mu, mw, mu, mw, q);
             LSX_CUDA(cudaGetLastError(), "edit image");
         }
         edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, dbasis, ddelta, (int)rank,
@@ -660,13 +677,13 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
     const int total = p.m_tiles * p.n_tiles;
     const int grid = std::min(total, ctx->sm_count);
     if (f32_hidden) {
-        auto k = readout_margin_kernel<2, 3>;
+        auto k = readout_margin_kernel<2, 3, kModeMargin>;
         size_t smem = readout_smem<2, 3>();
         LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                  "readout smem attribute");
         k<<<grid, kReadoutThreads, smem, s>>>(ma, ma2, mb, mea, meb, p);
     } else {
-        auto k = readout_margin_kernel<1, 4>;
+        auto k = readout_margin_kernel<1, 4, kModeMargin>;
         size_t smem = readout_smem<1, 4>();
         LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                  "readout smem attribute");
