@@ -32,6 +32,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <vector>
 
@@ -127,6 +128,81 @@ constexpr uint32_t kIdesc = (1u << 4)            // D format f32
                             | ((RN >> 3) << 17)  // N
                             | ((RM >> 4) << 24); // M
 
+// Waits for this thread's tcgen05.ld results; the registers are tied to the wait
+// so no use of them can be scheduled before it.
+__device__ __forceinline__ void tc_wait_ld_regs(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// Running margin state of one hidden row over one tile.
+struct RowScan {
+    float best = -INFINITY;  // best non-target logit so far
+    int best_col = -1;       // its tile column (lowest on ties)
+    float tval = 0.f;        // the target's logit when it lies in this tile
+    float probe = 0.f;       // becomes NaN once any logit is non-finite (z * 0)
+};
+
+// Folds 32 accumulator columns [c0, c0 + 32) of one row into the scan: the target
+// column is set aside, the rest reduce by a max tree, and the (rare) chunk that
+// beats the running best is searched for its first maximal column.
+template <bool BIAS, bool TAIL>
+__device__ __forceinline__ void scan_chunk(const uint32_t (&r)[32], int c0, int tcol, int n0, const ReadoutParams& p,
+                                           RowScan& st) {
+    float z[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        float v = __uint_as_float(r[i]);
+        if (BIAS) v += __ldg(&p.bias[min(n0 + c0 + i, p.V - 1)]);
+        if (TAIL && n0 + c0 + i >= p.V) v = -INFINITY;
+        else st.probe = fmaf(v, 0.f, st.probe);
+        if (c0 + i == tcol) {
+            st.tval = v;
+            v = -INFINITY;
+        }
+        z[i] = v;
+    }
+    float m[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = fmaxf(fmaxf(z[4 * j], z[4 * j + 1]), fmaxf(z[4 * j + 2], z[4 * j + 3]));
+    const float mx = fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+    if (mx > st.best) {
+        int idx = 31;
+#pragma unroll
+        for (int i = 30; i >= 0; --i) idx = z[i] == mx ? i : idx;
+        st.best = mx;
+        st.best_col = c0 + idx;
+    }
+}
+
+// One row's pass over a 256-column accumulator: TMEM loads run one 32-column
+// chunk ahead of the scan.
+__device__ __forceinline__ void scan_tile(uint32_t taddr, int tcol, int n0, const ReadoutParams& p, RowScan& st) {
+    uint32_t ra[32], rb[32];
+    const bool bias = p.bias != nullptr, tail = n0 + RN > p.V;
+    tc_ld32(taddr, ra);
+    tc_wait_ld_regs(ra);
+#pragma unroll 1
+    for (int c = 0; c < RN / 32; c += 2) {
+        tc_ld32(taddr + (uint32_t)((c + 1) * 32), rb);
+        if (bias) scan_chunk<true, true>(ra, c * 32, tcol, n0, p, st);
+        else if (tail) scan_chunk<false, true>(ra, c * 32, tcol, n0, p, st);
+        else scan_chunk<false, false>(ra, c * 32, tcol, n0, p, st);
+        tc_wait_ld_regs(rb);
+        if (c + 2 < RN / 32) tc_ld32(taddr + (uint32_t)((c + 2) * 32), ra);
+        if (bias) scan_chunk<true, true>(rb, (c + 1) * 32, tcol, n0, p, st);
+        else if (tail) scan_chunk<false, true>(rb, (c + 1) * 32, tcol, n0, p, st);
+        else scan_chunk<false, false>(rb, (c + 1) * 32, tcol, n0, p, st);
+        if (c + 2 < RN / 32) tc_wait_ld_regs(ra);
+    }
+}
+
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
@@ -204,7 +280,12 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 if (next < total && (next / p.m_tiles) != (tile / p.m_tiles))
                     for (int kb = 0; kb < p.k_blocks; ++kb)
                         tma_prefetch_2d(&map_b, kb * RK, (next / p.m_tiles) * RN);
-                for (int kb = 0; kb < k_total; ++kb) {
+                // Tiles that share an operand block run side by side; each starts its
+                // K sweep at a different block so they do not all request the same
+                // lines at once.
+                const int rot = tile % k_total;
+                for (int kq = 0; kq < k_total; ++kq) {
+                    const int kb = kq + rot < k_total ? kq + rot : kq + rot - k_total;
                     if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
                         ok = false;
                         break;
@@ -250,7 +331,9 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * RN);
-                for (int kb = 0; kb < k_total; ++kb) {
+                const int rot = tile % k_total;  // the producer's K order
+                for (int kq = 0; kq < k_total; ++kq) {
+                    const int kb = kq + rot < k_total ? kq + rot : kq + rot - k_total;
                     if (!wait_or_abort(&full[stage], phase, abort_flag)) {
                         ok = false;
                         break;
@@ -265,7 +348,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
 #pragma unroll
                         for (int k = 0; k < RK / 16; ++k) {
                             // +32 bytes along K inside the swizzle atom per 16-element step
-                            const uint32_t accumulate = (kb | pl | k) != 0;
+                            const uint32_t accumulate = (kq | pl | k) != 0;
                             tc_mma(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc, accumulate);
                         }
                     }
@@ -343,29 +426,12 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             const int row = m0 + row_local;
             const bool live = row < p.M;
             const int tcol = live ? (int)p.targets[row] - n0 : -1;
-            float best = -INFINITY, tval = 0.f;
-            int best_col = -1;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
-#pragma unroll 1
-            for (int c = 0; c < RN / 32; ++c) {
-                uint32_t r[32];
-                tc_ld32(taddr + (uint32_t)(c * 32), r);
-                tc_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = c * 32 + i;
-                    if (n0 + col < p.V) {
-                        float z = __uint_as_float(r[i]);
-                        if (p.bias) z += __ldg(&p.bias[n0 + col]);
-                        nonfinite |= !isfinite(z);
-                        if (col == tcol) tval = z;
-                        else if (z > best) {
-                            best = z;
-                            best_col = col;
-                        }
-                    }
-                }
-            }
+            RowScan scan;
+            scan_tile(taddr, tcol, n0, p, scan);
+            nonfinite |= scan.probe != 0.f;  // NaN (non-finite logit) or never 0 otherwise
+            const float best = scan.best, tval = scan.tval;
+            const int best_col = scan.best_col;
             tc_fence_before();
             mbar_arrive(&tmem_empty[acc]);
             if (live) {
@@ -394,6 +460,275 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
     }
     tc_fence_after();
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
+}
+
+// ------------------------------------------------- CTA-pair margin kernel --
+// The same margin GEMM on CTA pairs (a cluster of 2, tcgen05 cta_group::2, M = 256
+// per MMA): each CTA of the pair loads its own 128 hidden rows and its half (128
+// rows) of the 256-row lm_head block, and the pair's MMA reads both halves, so each
+// CTA moves 32 KB per K block instead of 48 KB for the same 128 x 256 outputs.
+// The margin path is bound by operand traffic out of L2, so this is the lever.
+// Protocol (the one CUTLASS's 2-SM pipelines use):
+//   - both CTAs allocate TMEM with cta_group::2; the even CTA (leader) issues MMAs;
+//   - each producer waits for its own stage to be released, the leader expects the
+//     pair's bytes on its own `full` barrier and both producers' TMA loads (never
+//     multicast; sources are this GPU's memory) complete on that barrier;
+//   - the leader's commits arrive on both CTAs' `empty` / `tmem_full` barriers;
+//   - both CTAs' epilogue warps release an accumulator on the leader's `tmem_empty`;
+//   - cluster barriers after initialisation and before TMEM is freed.
+constexpr int kPairRows = 2 * RM;       // rows per pair tile
+constexpr int kHalfN = RN / 2;          // lm_head rows loaded by each CTA
+constexpr int kHalfBytesB = kHalfN * RK * 2;  // 16 KB
+constexpr uint32_t kIdescPair = (1u << 4) | (1u << 7) | (1u << 10) | ((RN >> 3) << 17) | ((kPairRows >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory object in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA 2-D load into this CTA's shared memory, completing on a barrier of the pair
+// (given as a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(map), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+// Arrive (once, when the issued MMAs complete) on `bar` in both CTAs of the pair.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+template <int PLANES, int STAGES>
+__global__ void __launch_bounds__(kReadoutThreads, 1)
+    readout_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
+                        const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_ea,
+                        const __grid_constant__ CUtensorMap map_eb, const ReadoutParams p) {
+    constexpr int kStageBytes = PLANES * kTileBytesA + kHalfBytesB;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tmem_full = empty + STAGES;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued_count = const_cast<int*>(abort_flag) + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();  // 0: leader
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const int m_pairs = (p.M + kPairRows - 1) / kPairRows;
+    const int total = m_pairs * p.n_tiles;
+    const int k_total = p.k_blocks + p.ext_blocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);   // the leader's expect_tx arrival (+ the pair's bytes)
+            mbar_init(&empty[s], 1);  // the leader's MMA commit
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);   // the leader's commit after a tile's MMAs
+            mbar_init(&tmem_empty[a], 8);  // the 4 epilogue warps of both CTAs (leader's copy)
+        }
+        *abort_flag = 0;
+        *issued_count = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before either signals the other
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---------------- TMA producer (both CTAs) ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            const uint32_t full0 = map_to_rank(smem_u32(&full[0]), 0);
+            for (int tile = pair; tile < total && ok; tile += pairs) {
+                const int m0 = (tile % m_pairs) * kPairRows + (int)rank * RM;
+                const int n0 = (tile / m_pairs) * RN + (int)rank * kHalfN;
+                for (int kb = 0; kb < k_total; ++kb) {
+                    if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = smem + stage * kStageBytes;
+                    uint8_t* sb = sa + PLANES * kTileBytesA;
+                    const uint32_t fb = full0 + (uint32_t)(stage * 8);
+                    if (kb < p.k_blocks) {
+                        if (rank == 0) mbar_expect_tx(&full[stage], 2 * kStageBytes);
+                        tma_load_2d_pair(sa, &map_a, kb * RK, m0, fb);
+                        if (PLANES == 2) tma_load_2d_pair(sa + kTileBytesA, &map_a2, kb * RK, m0, fb);
+                        tma_load_2d_pair(sb, &map_b, kb * RK, n0, fb);
+                    } else {
+                        const int e = kb - p.k_blocks;
+                        if (rank == 0) mbar_expect_tx(&full[stage], 2 * (kTileBytesA + kHalfBytesB));
+                        tma_load_2d_pair(sa, &map_ea, e * RK, m0, fb);
+                        tma_load_2d_pair(sb, &map_eb, e * RK, n0, fb);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            *issued_count = issued;
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {  // ---------------- MMA issuer (leader) ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < total && ok; tile += pairs) {
+                if (!wait_or_abort(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * RN);
+                for (int kb = 0; kb < k_total; ++kb) {
+                    if (!wait_or_abort(&full[stage], phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+                    const uint32_t sb = sa + PLANES * kTileBytesA;
+                    const uint64_t bdesc = smem_desc_sw128(sb);
+                    const int planes = kb < p.k_blocks ? PLANES : 1;
+                    for (int pl = 0; pl < planes; ++pl) {
+                        const uint64_t adesc = smem_desc_sw128(sa + pl * kTileBytesA);
+#pragma unroll
+                        for (int k = 0; k < RK / 16; ++k) {
+                            const uint32_t accumulate = (kb | pl | k) != 0;
+                            tc_mma_pair(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdescPair,
+                                        accumulate);
+                        }
+                    }
+                    tc_commit_pair(&empty[stage]);  // frees the stage in both CTAs
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else {  // ---------------- epilogue warps 2..5 (both CTAs) ----------------
+        const int quarter = warp & 3;
+        const int row_local = quarter * 32 + lane;
+        const uint32_t tmem_empty0 = map_to_rank(smem_u32(&tmem_empty[0]), 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool nonfinite = false;
+        for (int tile = pair; tile < total; tile += pairs) {
+            const int m0 = (tile % m_pairs) * kPairRows + (int)rank * RM;
+            const int n0 = (tile / m_pairs) * RN;
+            const bool ok = wait_or_abort(&tmem_full[acc], acc_phase, abort_flag);
+            if (__any_sync(0xffffffffu, !ok)) {
+                if (lane == 0) {
+                    atomicExch(&p.status[0], kDeviceTimeoutEpilogue);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int row = m0 + row_local;
+            const bool live = row < p.M;
+            const int tcol = live ? (int)p.targets[row] - n0 : -1;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
+            RowScan scan;
+            scan_tile(taddr, tcol, n0, p, scan);
+            nonfinite |= scan.probe != 0.f;  // NaN (non-finite logit) or never 0 otherwise
+            const float best = scan.best, tval = scan.tval;
+            const int best_col = scan.best_col;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tmem_empty0 + (uint32_t)(acc * 8));
+            if (live) {
+                if (best_col >= 0) atomicMax(&p.other_key[row], pack_arg(best, (uint32_t)(n0 + best_col)));
+                if (tcol >= 0 && tcol < RN && n0 + tcol < p.V) p.target_logit[row] = tval;
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (__any_sync(0xffffffffu, nonfinite) && lane == 0) atomicOr(&p.status[1], 1);
+    }
+
+    __syncthreads();
+    if (*abort_flag) {
+        // Leave nothing in flight: wait (bounded) for every TMA stage this CTA issued
+        // whose completion the leader's barrier would show.
+        if (threadIdx.x == 0 && rank == 0) {
+            const int issued = *issued_count;
+            for (int s = 0; s < STAGES && s < issued; ++s) {
+                const int last = issued - 1 - ((issued - 1 - s) % STAGES);
+                mbar_wait_bounded(&full[s], (uint32_t)((last / STAGES) & 1));
+            }
+        }
+        __syncthreads();
+    }
+    tc_fence_before();
+    cluster_sync();  // the pair's MMAs and epilogues are done with both CTAs' memory
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
 }
 
 // ------------------------------------------------------------ prep kernels --
@@ -562,6 +897,37 @@ size_t readout_smem() {
     return (size_t)STAGES * (PLANES * kTileBytesA + kTileBytesB) + 1024 + (2 * STAGES + 4) * 8 + 16;
 }
 
+template <int PLANES, int STAGES>
+size_t pair_smem() {
+    return (size_t)STAGES * (PLANES * kTileBytesA + kHalfBytesB) + 1024 + (2 * STAGES + 4) * 8 + 16;
+}
+
+// Launches the CTA-pair margin kernel as clusters of 2.
+template <int PLANES, int STAGES>
+cudaError_t launch_pair(lsx_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb,
+                        const CUtensorMap& mea, const CUtensorMap& meb, const ReadoutParams& p) {
+    auto k = readout_pair_kernel<PLANES, STAGES>;
+    const size_t smem = pair_smem<PLANES, STAGES>();
+    cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const int m_pairs = (p.M + kPairRows - 1) / kPairRows;
+    const int total = m_pairs * p.n_tiles;
+    const int pairs = std::max(1, std::min(total, ctx->sm_count / 2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kReadoutThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, ma, ma2, mb, mea, meb, p);
+}
+
 }  // namespace
 
 // Workspace bytes readout_margin_enqueue needs for exactly this hidden dtype.
@@ -676,13 +1042,23 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
     p.status = status;
     const int total = p.m_tiles * p.n_tiles;
     const int grid = std::min(total, ctx->sm_count);
-    if (f32_hidden) {
+    // CTA pairs (cta_group::2) unless LSX_READOUT_SINGLE=1 asks for one CTA per tile.
+    const char* single = getenv("LSX_READOUT_SINGLE");
+    if (!(single && single[0] == '1') && ctx->sm_count >= 2) {
+        CUtensorMap mbh, mebh;
+        LSX_TRY(make_map(&mbh, weight->data, width, vocab, width * 2, kHalfN));
+        if (rank > 0) LSX_TRY(make_map(&mebh, ext_b, L.ext_k, vocab, L.ext_k * 2, kHalfN));
+        else mebh = mbh;
+        cudaError_t e = f32_hidden ? launch_pair<2, 4>(ctx, ma, ma2, mbh, mea, mebh, p)
+                                   : launch_pair<1, 6>(ctx, ma, ma2, mbh, mea, mebh, p);
+        LSX_CUDA(e, "readout margin launch");
+    } else if (f32_hidden) {
         auto k = readout_margin_kernel<2, 3, kModeMargin>;
         size_t smem = readout_smem<2, 3>();
         LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                  "readout smem attribute");
         k<<<grid, kReadoutThreads, smem, s>>>(ma, ma2, mb, mea, meb, p);
-    } else {
+    } else {  // single CTA per tile
         auto k = readout_margin_kernel<1, 4, kModeMargin>;
         size_t smem = readout_smem<1, 4>();
         LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
