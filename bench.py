@@ -42,6 +42,12 @@ PROMPT, GENERATE = 24, 32
 STEPS_PER_GENERATION = PROMPT + GENERATE - 1
 READOUT_ROWS, VOCAB, HIDDEN, RANK = 4096, 151936, 1024, 16
 METRIC = "decode tok/s (Qwen3-0.6B bs1, % HBM roofline); readout-margin rows/s"
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
+# dominant kernel of each leg on this workload, from ncu captures of this script
+# (--profile): persistent_decode_kernel per 55-step generation, and
+# readout_pair_kernel per 4096-row validation.
+DECODE_TRAFFIC_PER_LAUNCH = 65_563_098_000 + 40_558_336
+READOUT_TRAFFIC_PER_LAUNCH = 339_733_248 + 4_837_888
 
 
 def env_rank():
@@ -388,7 +394,9 @@ def main():
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "l2": "weights 1.19 GB per token > 126 MB L2 (no flush needed)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                         "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": DECODE_TRAFFIC_PER_LAUNCH if dec["persistent"] else None,
+                         "traffic_unit": "bytes per launch (one generation of 55 decode steps)",
                          "scope": ("one cooperative decode kernel per generation" if dec["persistent"] else
                                    f"{dec['kernels_per_step']} kernels per decode step") +
                                   f", algorithmic bytes {bytes_step / 1e9:.4f} GB per decode step, "
@@ -406,9 +414,12 @@ def main():
                            "rows_per_gpu": READOUT_ROWS, "scaling": "weak (row shards)",
                            "l2": "lm_head 311 MB > L2"},
                 "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
-                             "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "traffic": None,
-                             "scope": "whole validation step (edit image + coefficients + tcgen05 GEMM + "
-                                      f"finalize), 2*4096*151936*1024 flops, {peaks['source']} burst peak"},
+                             "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
+                             "traffic": READOUT_TRAFFIC_PER_LAUNCH,
+                             "traffic_unit": "bytes per launch of the margin GEMM (lm_head read once)",
+                             "scope": "whole validation step (tcgen05 edit image + coefficients + tcgen05 "
+                                      "CTA-pair margin GEMM + finalize), 2*4096*151936*1024 flops, "
+                                      f"{peaks['source']} burst peak"},
                 "e2e": {"value": world * READOUT_ROWS / ro_e2e, "unit": "rows/s", "h2d_bytes_per_step": ro["h2d"],
                         "d2h_bytes_per_step": ro["d2h"]},
                 "clocks": ro["clocks"],
