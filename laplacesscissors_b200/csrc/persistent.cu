@@ -132,11 +132,19 @@ __device__ __forceinline__ unsigned long long arg_word(unsigned long long key, u
            (unsigned long long)(epoch & 0x1FFFu);
 }
 
-// Polls n tagged words until each carries `epoch`; values land in dst[0..n).
+// Activation layout in shared memory for the GEMVs: element i of an n-vector is
+// stored at xperm(i, n) so that the two 16-byte halves of every lane's 8-element
+// slice sit in two arrays of consecutive slices, and each warp-wide 16-byte load
+// of x reads 512 contiguous bytes (one conflict-free pass).
+__device__ __forceinline__ int xperm(int i, int n) { return ((i & 4) ? (n >> 1) : 0) + ((i >> 3) << 2) + (i & 3); }
+
+// Polls n tagged words until each carries `epoch`; values land in dst[0..n)
+// (at xperm positions when `perm`).
 // Every stale word of a thread is re-read in the same round, so a poll costs one
 // L2 round trip per round rather than one per word.  Called by all compute
 // threads; false on timeout or abort.
-__device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch, float* dst, DecodeState* st) {
+__device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch, float* dst, DecodeState* st,
+                            bool perm = false) {
     const int tid = threadIdx.x;
     constexpr int kBatch = 16;
     bool ok = true;
@@ -169,7 +177,7 @@ __device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
             const int i = base + tid + j * kCompute;
-            if (i < n) dst[i] = __uint_as_float((uint32_t)v[j]);
+            if (i < n) dst[perm ? xperm(i, n) : i] = __uint_as_float((uint32_t)v[j]);
         }
     }
     if (!ok) raise_abort(st, kDeviceTimeoutEpilogue);
@@ -375,12 +383,14 @@ struct RowReduce {
 template <int KCH>
 struct XRegs {
     float4 v[2 * (KCH > 0 ? KCH : 1)];
-    __device__ __forceinline__ void load(const float* xs, int lane) {
+    // perm: xs holds x at xperm positions (K = 256 KCH); otherwise in natural order.
+    __device__ __forceinline__ void load(const float* xs, int lane, bool perm) {
         const float4* x4 = reinterpret_cast<const float4*>(xs);
 #pragma unroll
         for (int j = 0; j < KCH; ++j) {
-            v[2 * j] = x4[2 * (lane + 32 * j)];
-            v[2 * j + 1] = x4[2 * (lane + 32 * j) + 1];
+            const int c = lane + 32 * j;
+            v[2 * j] = perm ? x4[c] : x4[2 * c];
+            v[2 * j + 1] = perm ? x4[KCH * 32 + c] : x4[2 * c + 1];
         }
     }
 };
@@ -452,7 +462,7 @@ __device__ __forceinline__ bool first_window_landed(const Ring& ring, const Curs
 template <int EPI, int KCH, int NR>
 __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const OpDesc& op, const float* bias,
                                          const float* xs, const GainX<KCH>* gain, float eps, EpiCtx& e,
-                                         bool first_ready) {
+                                         bool first_ready, bool perm) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = op.K;
     const uint32_t row_bytes = (uint32_t)K * 2u;
@@ -460,7 +470,7 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
     XRegs<KCH> x;
     float inverse = 1.f;
     if (KCH > 0) {
-        x.load(xs, lane);
+        x.load(xs, lane, perm);
         if (gain) inverse = gain_regs_rms<KCH>(x, *gain, K, eps);
     }
     constexpr int kLanesPerRow = 32 / NR;
@@ -504,7 +514,8 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                     } else {
                         const float4* x4 = reinterpret_cast<const float4*>(xs);
                         for (int cc = lane; cc < (K >> 3); cc += 32) {
-                            const float4 x0 = x4[2 * cc], x1 = x4[2 * cc + 1];
+                            const float4 x0 = perm ? x4[cc] : x4[2 * cc];
+                            const float4 x1 = perm ? x4[(K >> 3) + cc] : x4[2 * cc + 1];
 #pragma unroll
                             for (int i = 0; i < NR; ++i)
                                 dot8_split(reinterpret_cast<const uint4*>(rp[i])[cc], x0, x1, a0[i], a1[i]);
@@ -782,19 +793,25 @@ struct GainRegs {
 };
 
 // RMSNorm of xs in place (kernels/ops.py:31-45): x * rsqrt(mean(x^2) + eps) * gain.
-__device__ void rms_norm_inplace(float* xs, int n, const GainRegs& gain, float eps, float* red) {
+__device__ void rms_norm_inplace(float* xs, int n, const GainRegs& gain, float eps, float* red, bool perm = false) {
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < kGainRegs; ++j) {
         const int i = threadIdx.x + j * kCompute;
-        if (i < n) ss = fmaf(xs[i], xs[i], ss);
+        if (i < n) {
+            const float x = xs[perm ? xperm(i, n) : i];
+            ss = fmaf(x, x, ss);
+        }
     }
     ss = compute_allsum(ss, red);
     const float inverse = rsqrtf(ss / (float)n + eps);
 #pragma unroll
     for (int j = 0; j < kGainRegs; ++j) {
         const int i = threadIdx.x + j * kCompute;
-        if (i < n) xs[i] = xs[i] * inverse * gain.g[j];
+        if (i < n) {
+            const int k = perm ? xperm(i, n) : i;
+            xs[k] = xs[k] * inverse * gain.g[j];
+        }
     }
     compute_sync();
 }
@@ -933,10 +950,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     else v = __half2float(((const __half*)a.embedding)[off]);
                     if (a.emb_scale != 1.f) v = __fadd_rn(v, __fmul_rn(a.emb_scale - 1.f, v));
                 }
-                xs[i] = v;
+                xs[xperm(i, a.H)] = v;
             }
             compute_sync();
-            for (int i = tid; i < r_hi - r_lo; i += kCompute) resid[i] = xs[r_lo + i];
+            for (int i = tid; i < r_hi - r_lo; i += kCompute) resid[i] = xs[xperm(r_lo + i, a.H)];
             for (int layer = 0; layer < a.L && ok; ++layer) {
                 const FusedLayer& Lr = layers[layer];
                 const uint32_t e_qkv = e0 + 5u * layer + 1u, e_attn = e_qkv + 1u, e_o = e_qkv + 2u,
@@ -951,14 +968,14 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     if (KH > 0) gx.load(Lr.input_gain, lane);
                     else gs.load(Lr.input_gain, a.H);
                     const bool ready = first_window_landed(ring, cur, op_qkv);
-                    if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st));
+                    if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st, true));
                     if (!ok) break;
                     LSX_PHASE_MARK(1);
-                    if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
+                    if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red, true);
                     e.out = a.t_qkv;
                     e.epoch = e_qkv;
                     ok = run_gemv<kEpiStore, KH, NRH>(ring, cur, op_qkv, Lr.bqkv, xs, KH > 0 ? &gx : nullptr,
-                                                      a.eps, e, ready);
+                                                      a.eps, e, ready, true);
                     if (!ok) break;
                     LSX_PHASE_MARK(3);
                 }
@@ -970,14 +987,14 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 LSX_PHASE_MARK(4);
                 // o: residual += Wo attn
                 bool ready = first_window_landed(ring, cur, op_o);
-                ok = compute_and(poll_vector(a.t_attn, a.QH * a.D, e_attn, xs, st));
+                ok = compute_and(poll_vector(a.t_attn, a.QH * a.D, e_attn, xs, st, true));
                 if (!ok) break;
                 LSX_PHASE_MARK(5);
                 e.out = a.t_resid;
                 e.epoch = e_o;
                 e.resid = resid;
                 e.resid_lo = r_lo;
-                ok = run_gemv<kEpiResidual, KQ, NRQ>(ring, cur, op_o, Lr.bo, xs, nullptr, a.eps, e, ready);
+                ok = run_gemv<kEpiResidual, KQ, NRQ>(ring, cur, op_o, Lr.bo, xs, nullptr, a.eps, e, ready, true);
                 if (!ok) break;
                 LSX_PHASE_MARK(6);
                 // gate/up: RMSNorm(residual) -> act(gate) * up
@@ -987,25 +1004,25 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     if (KH > 0) gx.load(Lr.post_gain, lane);
                     else gs.load(Lr.post_gain, a.H);
                     ready = first_window_landed(ring, cur, op_gu);
-                    ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st));
+                    ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st, true));
                     if (!ok) break;
                     LSX_PHASE_MARK(7);
-                    if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red);
+                    if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red, true);
                     e.out = a.t_feat;
                     e.epoch = e_gu;
                     ok = run_gemv<kEpiGated, KH, NRG>(ring, cur, op_gu, Lr.bgu, xs, KH > 0 ? &gx : nullptr,
-                                                      a.eps, e, ready);
+                                                      a.eps, e, ready, true);
                     if (!ok) break;
                     LSX_PHASE_MARK(9);
                 }
                 // down: residual += Wd feature
                 ready = first_window_landed(ring, cur, op_down);
-                ok = compute_and(poll_vector(a.t_feat, a.I, e_gu, xs, st));
+                ok = compute_and(poll_vector(a.t_feat, a.I, e_gu, xs, st, true));
                 if (!ok) break;
                 LSX_PHASE_MARK(10);
                 e.out = a.t_resid;
                 e.epoch = e_down;
-                ok = run_gemv<kEpiResidual, KI, NRI>(ring, cur, op_down, Lr.bd, xs, nullptr, a.eps, e, ready);
+                ok = run_gemv<kEpiResidual, KI, NRI>(ring, cur, op_down, Lr.bd, xs, nullptr, a.eps, e, ready, true);
                 LSX_PHASE_MARK(11);
             }
             if (!ok) break;
@@ -1072,7 +1089,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             e.logits = logits;
             e.best = 0ull;
             LSX_HEAD_MARK(2);
-            ok = run_gemv<kEpiHead, KH, NRH>(ring, cur, op_head, a.head_bias, xs, nullptr, a.eps, e, false);
+            ok = run_gemv<kEpiHead, KH, NRH>(ring, cur, op_head, a.head_bias, xs, nullptr, a.eps, e, false, false);
             if (!ok) break;
             LSX_HEAD_MARK(3);
             unsigned long long* rb = reinterpret_cast<unsigned long long*>(red);
