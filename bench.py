@@ -136,11 +136,16 @@ def build_checkpoint(rank: int, layers: int = 28) -> Path:
     return d
 
 
-def readout_inputs():
+def readout_inputs(rank: int = 0, world: int = 1):
+    """This rank's row shard of the validation set: READOUT_ROWS rows per rank out
+    of a seeded global set of READOUT_ROWS x world rows (weak scaling); the lm_head
+    and the edit are shared."""
     from laplacesscissors_b200 import random_subspace_rotation, synth
+    from laplacesscissors_b200.sharding import row_shard
     w = synth.normal_bf16(7, 0, VOCAB * HIDDEN, 0.02)
-    hidden = synth.readout_hidden(7, READOUT_ROWS, HIDDEN)
-    targets = synth.readout_targets(7, READOUT_ROWS, VOCAB)
+    lo, hi = row_shard(READOUT_ROWS * world, world, rank)
+    hidden = synth.readout_hidden(7, hi - lo, HIDDEN, first=lo)
+    targets = synth.readout_targets(7, hi - lo, VOCAB, first=lo)
     edit = random_subspace_rotation(HIDDEN, RANK, 3.0, seed=7)
     return w, hidden, targets, edit
 
@@ -362,7 +367,7 @@ def main():
     peaks = measured_peaks()
     ckpt = build_checkpoint(local)
     dec = run_decode(gpu, ckpt, args.steps, args.warmup, dist)
-    inputs = readout_inputs()
+    inputs = readout_inputs(rank, world)
     ro = run_readout(gpu, inputs, args.steps, args.warmup, dist)
     # Kernels of ours per timed generation: one cooperative launch (persistent
     # engine) or the graph's per-step chain; readout: init, edit image, edit

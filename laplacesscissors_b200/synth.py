@@ -170,16 +170,18 @@ def prompt_tokens(seed: int, length: int, vocab: int) -> np.ndarray:
     return uniform_u32(seed, STREAM_PROMPT, length, vocab)
 
 
-def readout_hidden(seed: int, rows: int, width: int, eps: float = 1e-6) -> np.ndarray:
+def readout_hidden(seed: int, rows: int, width: int, eps: float = 1e-6, first: int = 0) -> np.ndarray:
     """Hidden states of the readout-validation workload: N(0, 1) rows, RMSNorm'd
-    (gain 1) in f64, rounded to bf16.  Returns bf16 bit patterns [rows, width]."""
-    x = normal_f32(seed, STREAM_HIDDEN, rows * width).astype(np.float64).reshape(rows, width)
+    (gain 1) in f64, rounded to bf16.  Returns bf16 bit patterns [rows, width] of
+    rows first .. first + rows - 1 of the seed's row sequence (any shard of the
+    global set is generated independently)."""
+    x = normal_f32(seed, STREAM_HIDDEN, rows * width, offset=first * width).astype(np.float64).reshape(rows, width)
     x = x / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + eps)
     return f32_to_bf16(x.astype(np.float32))
 
 
-def readout_targets(seed: int, rows: int, vocab: int) -> np.ndarray:
-    return uniform_u32(seed, STREAM_TARGETS, rows, vocab)
+def readout_targets(seed: int, rows: int, vocab: int, first: int = 0) -> np.ndarray:
+    return uniform_u32(seed, STREAM_TARGETS, rows, vocab, offset=first)
 
 
 __all__ = [
