@@ -258,6 +258,60 @@ def run_decode(gpu, ckpt: Path, steps: int, warmup: int, dist, e2e: bool = True)
             "persistent": int(info.persistent)}
 
 
+GEMV_SHAPES = [(2048, 1024), (6144, 1024), (1024, 3072), (151936, 1024), (12288, 4096)]
+
+
+def run_gemv(gpu, iters: int = 20):
+    """The bf16 GEMV microbenchmark: y = W x through lsx_linear_into (the drop-in
+    for Gpu::linear / kernels/ops.py matvec), W [N, K] bf16 N(0, 0.02), x f32 from
+    bf16 N(0, 1), y f32.  Launches over enough weight copies to exceed L2 (>= 256 MB
+    per pass) are captured once in a CUDA graph so launch gaps do not count;
+    CUDA events time `iters` replays.  bytes = 2NK + 4K + 4N per GEMV."""
+    import ctypes as C
+    from cuda.bindings import runtime as rt
+
+    from laplacesscissors_b200 import synth
+    from laplacesscissors_b200._lib import BF16
+    stream = gpu.stream()
+    out = {}
+    for n, k in GEMV_SHAPES:
+        w_host = synth.normal_bf16(7, 100 + n, n * k, 0.02)
+        copies = max(2, min(64, -(-256_000_000 // (2 * n * k))))
+        ws = [gpu.upload_raw(w_host, BF16) for _ in range(copies)]
+        x = gpu.upload_f32(synth.bf16_to_f32(synth.normal_bf16(7, 200 + k, k)))
+        y = gpu.zeros(n)
+        gpu.synchronize()
+
+        def ok(r):
+            err = r[0] if isinstance(r, tuple) else r
+            if err != rt.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cuda runtime: {err}")
+            return r[1] if isinstance(r, tuple) and len(r) > 1 else None
+
+        ok(rt.cudaStreamBeginCapture(stream, rt.cudaStreamCaptureMode.cudaStreamCaptureModeRelaxed))
+        for w in ws:
+            gpu.linear_into(x, w, None, n, k, y)
+        graph = ok(rt.cudaStreamEndCapture(stream))
+        exe = ok(rt.cudaGraphInstantiate(graph, 0))
+        for _ in range(3):
+            ok(rt.cudaGraphLaunch(exe, stream))
+        start, stop = ok(rt.cudaEventCreate()), ok(rt.cudaEventCreate())
+        ok(rt.cudaEventRecord(start, stream))
+        for _ in range(iters):
+            ok(rt.cudaGraphLaunch(exe, stream))
+        ok(rt.cudaEventRecord(stop, stream))
+        ok(rt.cudaEventSynchronize(stop))
+        ms = ok(rt.cudaEventElapsedTime(start, stop)) / (iters * copies)
+        nbytes = 2 * n * k + 4 * k + 4 * n
+        out[f"{n}x{k}"] = {"us": ms * 1e3, "GB/s": nbytes / (ms * 1e-3) / 1e9, "weight_copies": copies}
+        ok(rt.cudaGraphExecDestroy(exe))
+        ok(rt.cudaGraphDestroy(graph))
+        ok(rt.cudaEventDestroy(start))
+        ok(rt.cudaEventDestroy(stop))
+        del ws
+    return out
+
+
 def run_readout(gpu, inputs, steps: int, warmup: int, dist, e2e: bool = True):
     import ctypes as C
     import torch
@@ -348,7 +402,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["all", "decode", "readout"], default="all",
+    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv"], default="all",
                     help="profiling aid: run one half only")
     ap.add_argument("--profile", action="store_true",
                     help="profiling aid: device legs only, no e2e or CPU legs, warm-up as given")
@@ -369,6 +423,7 @@ def main():
     dec = run_decode(gpu, ckpt, args.steps, args.warmup, dist)
     inputs = readout_inputs(rank, world)
     ro = run_readout(gpu, inputs, args.steps, args.warmup, dist)
+    gemv = run_gemv(gpu) if rank == 0 else None
     # Kernels of ours per timed generation: one cooperative launch (persistent
     # engine) or the graph's per-step chain; readout: init, edit image, edit
     # coefficients, tcgen05 margin, finalize.
@@ -430,6 +485,14 @@ def main():
                 "clocks": ro["clocks"],
             },
         }
+        line["gemv"] = {
+            "metric": "bf16 GEMV y = W x achieved HBM GB/s (lsx_linear_into, the Gpu::linear drop-in)",
+            "unit": "GB/s", "peak": peaks["hbm_gbs"],
+            "config": {"shapes": [f"{n}x{k}" for n, k in GEMV_SHAPES], "x": "f32", "y": "f32",
+                       "l2": "weight copies rotated so each pass reads >= 256 MB",
+                       "timing": "CUDA graph of the launches, CUDA events, rank 0"},
+            "results": gemv,
+        }
         if not args.no_cpu_baseline and world == 1:
             v, cores, sample = cpu_decode_rate(ckpt)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
@@ -454,6 +517,8 @@ def profile_run(args, local):
     if args.workload in ("all", "readout"):
         ro = run_readout(gpu, readout_inputs(), args.steps, args.warmup, dist, e2e=False)
         out["readout_ms_per_step"] = ro["dev_ms"] / args.steps
+    if args.workload in ("all", "gemv"):
+        out["gemv"] = run_gemv(gpu)
     print(json.dumps(out))
 
 

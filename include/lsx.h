@@ -97,6 +97,11 @@ int lsx_embedding(lsx_ctx* ctx, const lsx_tensor* weight, size_t row, size_t wid
 /* Gpu::linear (src/gpu.rs:378-405), kernels/ops.py:14-28.  bias may be NULL. */
 int lsx_linear(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* w, const lsx_tensor* bias,
                size_t rows, size_t cols, lsx_tensor** out);
+/* Gpu::linear into a caller-provided F32 tensor `out` of `rows` elements (no
+   allocation and no synchronisation; the reference always returns a new tensor).
+   Enqueued on the context's stream, so it can be captured into a CUDA graph. */
+int lsx_linear_into(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* w, const lsx_tensor* bias,
+                    size_t rows, size_t cols, lsx_tensor* out);
 /* Gpu::norm (src/gpu.rs:406-431), kernels/ops.py:31-45.  center != 0 is LayerNorm. */
 int lsx_norm(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* gain, const lsx_tensor* bias,
              size_t groups, size_t width, float epsilon, int center, lsx_tensor** out);

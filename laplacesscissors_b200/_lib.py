@@ -71,6 +71,7 @@ SIGNATURES = {
     "lsx_tensor_wrap": (I, [P, P, SZ, I, PP]),
     "lsx_embedding": (I, [P, P, SZ, SZ, PP]),
     "lsx_linear": (I, [P, P, P, P, SZ, SZ, PP]),
+    "lsx_linear_into": (I, [P, P, P, P, SZ, SZ, P]),
     "lsx_norm": (I, [P, P, P, P, SZ, SZ, F, I, PP]),
     "lsx_rope": (I, [P, P, SZ, SZ, SZ, F, SZ, I, PP]),
     "lsx_attention": (I, [P, P, P, P, P, P, SZ, SZ, SZ, SZ, F, PP]),

@@ -546,6 +546,20 @@ int lsx_embedding(lsx_ctx* ctx, const lsx_tensor* weight, size_t row, size_t wid
                   out, "take_row");
 }
 
+int lsx_linear_into(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* w, const lsx_tensor* bias, size_t rows,
+                    size_t cols, lsx_tensor* out) {
+    LSX_ENSURE(ctx && x && w && out, "invalid argument");
+    LSX_ENSURE(is_f32(x) && (!bias || is_f32(bias)) && is_f32(out), "linear inputs, bias and output are F32 tensors");
+    LSX_ENSURE(rows > 0 && cols > 0 && x->count == cols && w->count / rows == cols && w->count % rows == 0 &&
+                   (!bias || bias->count == rows) && out->count == rows,
+               "check the dimensions of the linear op");
+    cudaSetDevice(ctx->device);
+    LSX_CUDA(launch_matvec(ctx->stream, ctx->sm_count, w->data, w->kind, (const float*)x->data,
+                           bias ? (const float*)bias->data : nullptr, rows, cols, (float*)out->data),
+             "matvec");
+    return LSX_OK;
+}
+
 int lsx_linear(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* w, const lsx_tensor* bias, size_t rows,
                size_t cols, lsx_tensor** out) {
     LSX_ENSURE(ctx && x && w && out, "invalid argument");

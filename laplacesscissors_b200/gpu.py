@@ -178,6 +178,11 @@ class Gpu:
                              C.byref(h)))
         return self._tensor(h)
 
+    def linear_into(self, x: Tensor, w: Tensor, bias: Tensor | None, rows: int, cols: int, out: Tensor) -> None:
+        """linear() into an existing F32 tensor (no allocation, enqueue only)."""
+        check(lib.lsx_linear_into(self._h, x.handle, w.handle, bias.handle if bias else None, int(rows), int(cols),
+                                  out.handle))
+
     def norm(self, x: Tensor, gain: Tensor, bias: Tensor | None, config: NormConfig) -> Tensor:
         h = C.c_void_p()
         check(lib.lsx_norm(self._h, x.handle, gain.handle, bias.handle if bias else None, config.groups,
