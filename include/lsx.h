@@ -190,6 +190,19 @@ int lsx_model_generate(lsx_model* model, const uint32_t* prompt, size_t prompt_l
                        uint32_t* tokens_out, size_t* generated, int* stopped,
                        float* hidden_frames, float* logits_frames);
 
+/* Teacher-forced case scoring (src/scaling.rs:181-216): prefill `prompt` token by
+   token, then for each of the `count` targets score the Frame that predicts it and
+   advance with the target.  Per scored position k: nll_out[k] = attribution::loss
+   (src/attribution.rs:49-60) of the Frame's logits for targets[k] (f64),
+   argmax_out[k] = the logits' first argmax.  With `rotation` the logits are the
+   edited readout of the unedited hidden state (the reference's "after" scores:
+   Model::readout with the edit); hidden states and the advance are unchanged.
+   hidden_frames [count x hidden] and logits_frames [count x vocab] may be NULL, as
+   may nll_out and argmax_out.  The cursor ends at prompt_length + count - 1. */
+int lsx_model_score(lsx_model* model, const uint32_t* prompt, size_t prompt_length, const uint32_t* targets,
+                    size_t count, const lsx_rotation* rotation, double* nll_out, uint32_t* argmax_out,
+                    float* hidden_frames, float* logits_frames);
+
 /* ------------------------------------------------------ readout validation -- */
 /* Fused readout margin over many hidden states (verify_cached's target rows,
    src/diagnosis.rs:512-537 with minimum_margin src/diagnosis.rs:490-492 and argmax

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(kGemvThreads) fused_gemv_kernel(const GemvArgs
     __syncthreads();
     float* logits = nullptr;
     if (PRO == kNormRotate) {
-        const int slot = st->step - (st->prompt_length - 1);
+        const int slot = st->step - (st->prompt_length - 1 - st->frame_back);
         const bool framed = st->frames && slot >= 0;
         float* hid = framed ? st->hidden_frames + (size_t)slot * K : st->hidden_scratch;
         logits = framed ? st->logits_frames + (size_t)slot * a.n : st->logits_scratch;
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kGemvThreads) fused_gemv_kernel(const GemvArgs
                 const uint32_t token = packed_index(b);
                 st->argmax = token;
                 st->head_counter = 0u;
-                const int index = st->step - (st->prompt_length - 1);
+                const int index = st->step - (st->prompt_length - 1 - st->frame_back);
                 if (index >= 0) {
                     st->tokens_out[index] = token;
                     st->generated = index + 1;

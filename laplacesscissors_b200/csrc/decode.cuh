@@ -28,7 +28,7 @@ struct DecodeState {
     int n_stop;
     int rot_kind;  // 0 none, 1 plane, 2 joint
     int rot_rank;
-    int pad0;
+    int frame_back;     // frames start this many steps before the last prompt step (teacher forcing)
     uint32_t argmax;  // argmax of the latest logits
     uint32_t token;   // token consumed by the latest step
     unsigned int head_counter;

@@ -509,6 +509,33 @@ __global__ void argmax_kernel(const float* z, int n, unsigned long long* out, in
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(nonfinite, 1);
 }
 
+// Teacher-forced loss of one scored position per block: attribution::loss
+// (src/attribution.rs:49-60), top + ln(sum_j exp(z_j - top)) - z[target], in f64.
+__global__ void __launch_bounds__(1024) frame_nll_kernel(const float* __restrict__ logits, int vocab,
+                                                         const uint32_t* __restrict__ targets, double* nll) {
+    __shared__ double red[32];
+    const float* z = logits + (size_t)blockIdx.x * vocab;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    double top = -INFINITY;
+    for (int j = tid; j < vocab; j += blockDim.x) top = fmax(top, (double)z[j]);
+    for (int o = 16; o > 0; o >>= 1) top = fmax(top, __shfl_xor_sync(0xffffffffu, top, o));
+    if (lane == 0) red[warp] = top;
+    __syncthreads();
+    top = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) top = fmax(top, red[w]);
+    __syncthreads();
+    double sum = 0.0;
+    for (int j = tid; j < vocab; j += blockDim.x) sum += exp((double)z[j] - top);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        double total = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total += red[w];
+        nll[blockIdx.x] = top + log(total) - (double)z[targets[blockIdx.x]];
+    }
+}
+
 }  // namespace lsx
 
 using namespace lsx;
@@ -1364,6 +1391,89 @@ int lsx_model_generate(lsx_model* m, const uint32_t* prompt, size_t prompt_lengt
     }
     *generated = n;
     if (stopped) *stopped = stop ? 1 : 0;
+    return LSX_OK;
+}
+
+// Teacher-forced scoring of one case (src/scaling.rs:181-216): prefill the prompt,
+// then for each target score the frame that predicts it and advance with the target.
+int lsx_model_score(lsx_model* m, const uint32_t* prompt, size_t prompt_length, const uint32_t* targets,
+                    size_t count, const lsx_rotation* rotation, double* nll_out, uint32_t* argmax_out,
+                    float* hidden_frames, float* logits_frames) {
+    LSX_ENSURE(m && prompt && targets, "invalid argument");
+    LSX_ENSURE(prompt_length > 0 && count > 0 && prompt_length + count - 1 <= m->capacity,
+               "give a context that fits the prompt and the continuation");
+    for (size_t i = 0; i < prompt_length; ++i) LSX_ENSURE(prompt[i] < m->graph.vocab, "check the token range");
+    for (size_t i = 0; i < count; ++i) LSX_ENSURE(targets[i] < m->graph.vocab, "check the target range");
+    LSX_TRY(check_rotation(m, rotation));
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    m->cursor = 0;
+    const size_t H = m->graph.hidden, V = m->graph.vocab;
+    const size_t forced = prompt_length + count - 1;  // prompt, then every target but the last
+    if (m->fused) {
+        LSX_TRY(ensure_frames(m, count));
+        std::vector<uint32_t> seq(forced);
+        memcpy(seq.data(), prompt, prompt_length * 4);
+        if (count > 1) memcpy(seq.data() + prompt_length, targets, (count - 1) * 4);
+        void* block = nullptr;
+        LSX_TRY(device_alloc(m->ctx, count * 12 + 16, &block));
+        uint32_t* d_targets = (uint32_t*)block;
+        double* d_nll = (double*)((uint8_t*)block + ((count * 4 + 15) & ~(size_t)15));
+        int rc = LSX_OK;
+        cudaError_t e = cudaMemcpyAsync(m->d_prompt, seq.data(), forced * 4, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d_targets, targets, count * 4, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("score upload", e));
+        if (rc == LSX_OK) {
+            base_state(m, rotation);
+            DecodeState* st = m->host_state;
+            st->prompt_length = (int)forced;
+            st->maximum = (int)count;
+            st->frame_back = (int)count - 1;
+            st->frames = 1;
+            st->hidden_frames = m->d_frames;
+            st->logits_frames = m->d_frames + count * H;
+            rc = run_fused(m, (int)forced);
+        }
+        if (rc == LSX_OK) {
+            frame_nll_kernel<<<(int)count, 1024, 0, s>>>(m->d_frames + count * H, (int)V, d_targets, d_nll);
+            e = cudaGetLastError();
+            if (e == cudaSuccess && nll_out) e = cudaMemcpyAsync(nll_out, d_nll, count * 8, cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess && argmax_out)
+                e = cudaMemcpyAsync(argmax_out, m->d_tokens, count * 4, cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess && hidden_frames)
+                e = cudaMemcpyAsync(hidden_frames, m->d_frames, count * H * 4, cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess && logits_frames)
+                e = cudaMemcpyAsync(logits_frames, m->d_frames + count * H, count * V * 4, cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("score", e));
+        }
+        device_release(m->ctx, block);
+        if (rc != LSX_OK) return rc;
+        if (m->host_state->nonfinite) return fail(LSX_E_NONFINITE, "check the finiteness of the model outputs");
+        m->cursor = (size_t)m->host_state->position;
+        return LSX_OK;
+    }
+    // Per-op plan: the reference's host loop, loss on the host in f64.
+    std::vector<float> hid(H), logits(V);
+    uint32_t next = 0;
+    for (size_t i = 0; i < prompt_length; ++i) {
+        OpBuffers b = buffers_of(m);
+        LSX_TRY(embedding_into(m, prompt[i], b.residual));
+        LSX_TRY(step_ops(m, rotation, hid.data(), i + 1 == prompt_length ? logits.data() : nullptr, &next));
+    }
+    for (size_t k = 0; k < count; ++k) {
+        double top = -INFINITY, sum = 0.0;
+        for (size_t j = 0; j < V; ++j) top = std::max(top, (double)logits[j]);
+        for (size_t j = 0; j < V; ++j) sum += std::exp((double)logits[j] - top);
+        if (nll_out) nll_out[k] = top + std::log(sum) - (double)logits[targets[k]];
+        if (argmax_out) argmax_out[k] = next;
+        if (hidden_frames) memcpy(hidden_frames + k * H, hid.data(), H * 4);
+        if (logits_frames) memcpy(logits_frames + k * V, logits.data(), V * 4);
+        if (k + 1 == count) break;
+        OpBuffers b = buffers_of(m);
+        LSX_TRY(embedding_into(m, targets[k], b.residual));
+        LSX_TRY(step_ops(m, rotation, hid.data(), logits.data(), &next));
+    }
     return LSX_OK;
 }
 

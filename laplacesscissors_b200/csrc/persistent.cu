@@ -869,6 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
     __syncthreads();
 
     const int P = st->prompt_length, maximum = st->maximum, mode = st->mode;
+    const int first_frame = P - 1 - st->frame_back;  // step of the first recorded frame
     const int pos0 = st->position;
     const uint32_t base = st->epoch;
     const uint32_t per_step = 5u * (uint32_t)a.L + 1u;
@@ -1035,7 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             if (!ok) break;
             LSX_HEAD_MARK(1);
             rms_norm_inplace(xs, a.H, fgain, a.eps, red);
-            const int slot_idx = step - (P - 1);
+            const int slot_idx = step - first_frame;
             const bool framed = frames && slot_idx >= 0;
             float* hid = framed ? st->hidden_frames + (size_t)slot_idx * a.H : st->hidden_scratch;
             float* logits = framed ? st->logits_frames + (size_t)slot_idx * a.V : st->logits_scratch;

@@ -247,3 +247,56 @@ __all__ = [
     "argmax", "other", "minimum_margin", "prefill", "generate_frames", "generate", "Generation", "ObservedPath",
     "Verification", "verify_cached", "CompactReadout", "readout_margin", "Deadline", "BudgetExpired",
 ]
+
+
+@dataclass
+class ScoredCase:  # one case record of scaling::evaluate (src/scaling.rs:198-211)
+    case: int
+    prompt_tokens: list[int]
+    target_tokens: list[int]
+    sequence_nll_before: float
+    sequence_nll_after: float
+    canonical_path_before: bool
+    canonical_path_after: bool
+
+
+@dataclass
+class Evaluation:  # the aggregates of scaling::evaluate (src/scaling.rs:178-216)
+    loss_before: float
+    loss_after: float
+    correct_before: int
+    correct_after: int
+    cases: list[ScoredCase]
+
+
+def evaluate_cases(model: Model, cases, rotation: DeviceRotation | None = None,
+                   deadline: Deadline | None = None) -> Evaluation:
+    """Teacher-forced scoring of many cases (src/scaling.rs:181-216).  `cases` holds
+    (prompt token ids, target token ids, answer byte length) per case; the
+    tokenizer (Text::target) is the caller's.  Per case the before scores use the
+    unedited readout and the after scores the edited one; a case's weight is
+    1 / (cases x max(answer bytes, 1)), as the reference's."""
+    n_cases = len(cases)
+    before = after = 0.0
+    correct_before = correct_after = 0
+    records = []
+    for i, (prompt, targets, answer_bytes) in enumerate(cases):
+        if deadline:
+            deadline.check()
+        targets = [int(t) for t in targets]
+        weight = 1.0 / (n_cases * max(int(answer_bytes), 1))
+        nll_b, amax_b, _ = model.score(prompt, targets)
+        if rotation is not None:
+            nll_a, amax_a, _ = model.score(prompt, targets, rotation)
+        else:
+            nll_a, amax_a = nll_b, amax_b
+        case_before, case_after = float(np.sum(nll_b)), float(np.sum(nll_a))
+        path_before = bool(np.all(amax_b == np.asarray(targets, dtype=np.uint32)))
+        path_after = bool(np.all(amax_a == np.asarray(targets, dtype=np.uint32)))
+        before += case_before * weight
+        after += case_after * weight
+        correct_before += int(path_before)
+        correct_after += int(path_after)
+        records.append(ScoredCase(i, [int(x) for x in prompt], targets, case_before, case_after, path_before,
+                                  path_after))
+    return Evaluation(before, after, correct_before, correct_after, records)

@@ -222,4 +222,23 @@ class Model:
         return tokens[:k].copy(), bool(stopped.value), fr
 
 
+    def score(self, prompt, targets, rotation: DeviceRotation | None = None, frames: bool = False):
+        """Teacher-forced scoring of one case (lsx_model_score; the per-case loop of
+        src/scaling.rs:181-216): per continuation position the loss
+        (attribution::loss, src/attribution.rs:49-60) of its target and the argmax of
+        the frame's logits.  Returns (nll f64 [n], argmax u32 [n], frames or None)."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        t = np.ascontiguousarray(targets, dtype=np.uint32)
+        n = t.size
+        nll = np.empty(n, dtype=np.float64)
+        amax = np.empty(n, dtype=np.uint32)
+        H, V = self.hidden_size, self.vocab_size()
+        hid = np.empty((n, H), dtype=np.float32) if frames else None
+        lg = np.empty((n, V), dtype=np.float32) if frames else None
+        check(lib.lsx_model_score(self._h, _up(p), p.size, _up(t), n, _rot(rotation), _dp(nll), _up(amax),
+                                  _fp(hid) if frames else None, _fp(lg) if frames else None))
+        fr = [Frame(hid[i].copy(), lg[i].copy()) for i in range(n)] if frames else None
+        return nll, amax, fr
+
+
 __all__ = ["Model", "DeviceRotation", "Frame"]
