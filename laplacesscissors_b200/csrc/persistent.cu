@@ -31,6 +31,7 @@
 #include <math.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <string>
 
 #include "device_common.cuh"
@@ -86,6 +87,7 @@ struct PArgs {
     int steps;
     int slots;
     int slot_bytes;
+    int inflight;  // chunks the producer keeps in flight at most (0: every free slot)
     SmemLayout sm;
 };
 
@@ -456,10 +458,12 @@ __device__ __forceinline__ bool first_window_landed(const Ring& ring, const Curs
 }
 
 // One GEMV op over this CTA's rows: consumes its chunks from the ring window by
-// window and releases each window's slots when done.  Each warp takes NR rows per
-// pass.  KCH > 0: K == 256 * KCH and x lives in registers (normalised there when
-// `gain` is given); KCH == 0: any K % 8 == 0, x read from shared memory.
-template <int EPI, int KCH, int NR>
+// window and releases each window's slots when done.  Each warp takes NV <= NR rows
+// per pass (NR, a power of two, is the width of the cross-lane reduction; NV < NR
+// evens out a CTA's rows over its warps).  KCH > 0: K == 256 * KCH and x lives in
+// registers (normalised there when `gain` is given); KCH == 0: any K % 8 == 0, x
+// read from shared memory.
+template <int EPI, int KCH, int NR, int NV = NR>
 __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const OpDesc& op, const float* bias,
                                          const float* xs, const GainX<KCH>* gain, float eps, EpiCtx& e,
                                          bool first_ready, bool perm) {
@@ -487,10 +491,10 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
         ok = (w0 == 0 && first_ready) || window_landed(ring, cur, wn);
         LSX_WINDOW_MARK(1);
         if (ok) {
-            for (int r0 = rs + warp * NR; r0 < re; r0 += kWarps * NR) {
-                const uint8_t* rp[NR];
+            for (int r0 = rs + warp * NV; r0 < re; r0 += kWarps * NV) {
+                const uint8_t* rp[NV];
 #pragma unroll
-                for (int i = 0; i < NR; ++i) {
+                for (int i = 0; i < NV; ++i) {
                     const int local = min(r0 + i, re - 1) - rs;  // the window starts on a chunk boundary
                     int s;
                     uint32_t p;
@@ -505,11 +509,11 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                     if (KCH > 0) {
 #pragma unroll
                         for (int j = 0; j < KCH; ++j) {
-                            uint4 w[NR];
+                            uint4 w[NV];
 #pragma unroll
-                            for (int i = 0; i < NR; ++i) w[i] = reinterpret_cast<const uint4*>(rp[i])[lane + 32 * j];
+                            for (int i = 0; i < NV; ++i) w[i] = reinterpret_cast<const uint4*>(rp[i])[lane + 32 * j];
 #pragma unroll
-                            for (int i = 0; i < NR; ++i) dot8_split(w[i], x.v[2 * j], x.v[2 * j + 1], a0[i], a1[i]);
+                            for (int i = 0; i < NV; ++i) dot8_split(w[i], x.v[2 * j], x.v[2 * j + 1], a0[i], a1[i]);
                         }
                     } else {
                         const float4* x4 = reinterpret_cast<const float4*>(xs);
@@ -517,7 +521,7 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                             const float4 x0 = perm ? x4[cc] : x4[2 * cc];
                             const float4 x1 = perm ? x4[(K >> 3) + cc] : x4[2 * cc + 1];
 #pragma unroll
-                            for (int i = 0; i < NR; ++i)
+                            for (int i = 0; i < NV; ++i)
                                 dot8_split(reinterpret_cast<const uint4*>(rp[i])[cc], x0, x1, a0[i], a1[i]);
                         }
                     }
@@ -527,7 +531,7 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                 RowReduce<NR, 16>::run(acc, lane);
                 float d = gain ? acc[0] * inverse : acc[0];
                 const int r = r0 + my_row;
-                const bool valid = owner && r < re;
+                const bool valid = owner && my_row < NV && r < re;
                 if (EPI == kEpiGated) {
                     // rows come in (gate, up) pairs; the up total sits kLanesPerRow lanes higher
                     const float u = __shfl_down_sync(0xffffffffu, d, kLanesPerRow);
@@ -825,7 +829,9 @@ template <int KH, int KQ, int KI, int DPL>
 __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int NRH = rows_for(KH);               // qkv and head
-    constexpr int NRG = KH > 0 && KH <= 4 ? 8 : 2;  // gate/up: whole (gate, up) pairs
+    // gate/up: whole (gate, up) pairs; at H = 1024 a CTA holds 40-42 rows, six per warp
+    constexpr int NRG = KH > 0 && KH <= 4 ? 8 : 2;
+    constexpr int NVG = KH > 0 && KH <= 4 ? 6 : 2;
     constexpr int NRQ = KQ > 4 ? 1 : rows_for(KQ);  // o
     constexpr int NRI = KI > 4 ? 1 : rows_for(KI);  // down
     constexpr int PB = DPL >= 8 ? 4 : 8;            // attention positions per warp batch
@@ -881,6 +887,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             uint32_t phase = 0;
             bool wrapped = false, go = true;
             long long issued = 0;
+            // the oldest chunk that may still be in flight
+            int lslot = 0;
+            uint32_t lphase = 0;
+            long long landed = 0;
             for (int step = 0; step < a.steps && go; ++step) {
                 for (int oi = 0; oi <= 4 * a.L && go; ++oi) {
                     const int op = oi < 4 * a.L ? (oi & 3) : kOpHead;
@@ -906,6 +916,21 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                             }
                             if (!go) break;
                         }
+                        // bound the bytes in flight per SM: a deep queue of bulk copies
+                        // delays the small exchange loads behind it
+                        while (a.inflight > 0 && issued - landed >= a.inflight && go) {
+                            if (!mbar_wait_bounded(&ring.full[lslot], lphase)) {
+                                raise_abort(st, kDeviceTimeoutWeights);
+                                go = false;
+                                break;
+                            }
+                            ++landed;
+                            if (++lslot == a.slots) {
+                                lslot = 0;
+                                lphase ^= 1u;
+                            }
+                        }
+                        if (!go) break;
                         const int r0 = d.lo + (ch << d.shift);
                         const int nr = min(1 << d.shift, d.hi - r0);
                         const uint32_t bytes = (uint32_t)nr * (uint32_t)d.K * 2u;
@@ -1011,7 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red, true);
                     e.out = a.t_feat;
                     e.epoch = e_gu;
-                    ok = run_gemv<kEpiGated, KH, NRG>(ring, cur, op_gu, Lr.bgu, xs, KH > 0 ? &gx : nullptr,
+                    ok = run_gemv<kEpiGated, KH, NRG, NVG>(ring, cur, op_gu, Lr.bgu, xs, KH > 0 ? &gx : nullptr,
                                                       a.eps, e, ready, true);
                     if (!ok) break;
                     LSX_PHASE_MARK(9);
@@ -1291,6 +1316,12 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
             break;
         }
     if (slots_ == 0) return fail(LSX_E_UNSUPPORTED, "persistent decode plan: shared memory");
+    // Weight chunks each SM keeps in flight.  Six 16 KB chunks per SM (14 MB over the
+    // GPU) still saturate HBM, and the shorter queue lets the exchange loads through
+    // sooner than a full ring of copies does.  LSX_DECODE_INFLIGHT overrides (0: every
+    // free slot).
+    inflight_ = std::min(6, slots_ - 1);
+    if (const char* v = std::getenv("LSX_DECODE_INFLIGHT")) inflight_ = std::max(0, std::min(std::atoi(v), slots_ - 1));
     layer_count_ = (int)layers.size();
     smem_ = (size_t)layout_for(c, slots_, slot_bytes, grid_, layers.size()).total;
     PKernel k = kernel_for(c);
@@ -1335,6 +1366,7 @@ int PersistentDecoder::run(int steps) {
     a.steps = steps;
     a.slots = slots_;
     a.slot_bytes = slot_bytes_for(c);
+    a.inflight = inflight_;
     a.sm = layout_for(c, slots_, a.slot_bytes, grid_, (size_t)layer_count_);
     void* args[] = {&a};
     LSX_CUDA(cudaLaunchCooperativeKernel((const void*)kernel_for(c), dim3(grid_), dim3(kThreads), args, smem_,

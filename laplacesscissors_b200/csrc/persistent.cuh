@@ -32,6 +32,7 @@ private:
                        *t_arg_ = nullptr;
     size_t smem_ = 0;
     int slots_ = 0;
+    int inflight_ = 0;
     int grid_ = 0;
     int layer_count_ = 0;
     std::vector<void*> owned_;
