@@ -402,8 +402,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv"], default="all",
-                    help="profiling aid: run one half only")
+    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "score8b"], default="all",
+                    help="all: the headline line; decode/readout/gemv: one leg only (with --profile); "
+                         "long4b: Qwen3-4B decode after a long prompt; score8b: Qwen3-8B teacher-forced scoring")
+    ap.add_argument("--prompt", type=int, default=4096, help="long4b: prompt length")
+    ap.add_argument("--cases", type=int, default=8, help="score8b: cases timed (of the 1024-case job)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling aid: device legs only, no e2e or CPU legs, warm-up as given")
     ap.add_argument("--layers", type=int, default=28, help="profiling aid: decoder layers of the checkpoint")
@@ -411,6 +414,10 @@ def main():
     rank, local, world = env_rank()
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.workload == "long4b":
+        return long_decode(args, local)
+    if args.workload == "score8b":
+        return scoring(args, local)
     if args.profile:
         return profile_run(args, local)
     if args.warmup < 3:
@@ -520,6 +527,129 @@ def profile_run(args, local):
     if args.workload in ("all", "gemv"):
         out["gemv"] = run_gemv(gpu)
     print(json.dumps(out))
+
+
+def model_checkpoint(shape: str, **overrides) -> Path:
+    from laplacesscissors_b200 import synth
+    cfg = dict(getattr(synth, shape), **overrides)
+    tag = "-".join(f"{k}{v}" for k, v in sorted(overrides.items()))
+    d = Path(tempfile.gettempdir()) / f"lsx-bench-{shape.lower()}-seed7{'-' + tag if tag else ''}"
+    if not (d / "model.safetensors").exists():
+        synth.make_qwen3_checkpoint(d, synth.qwen3_config(**cfg), seed=7)
+    return d
+
+
+def weight_bytes_per_step(cfg: dict) -> int:
+    """bf16 weight bytes one decode step reads: every block matrix and norm, the
+    final norm and the lm_head (one embedding row is not counted)."""
+    H, I, D = cfg["hidden"], cfg["intermediate"], cfg["head_dim"]
+    q, kv = cfg["heads"] * D, cfg["kv_heads"] * D
+    block = H * (q + 2 * kv) + q * H + 3 * H * I + 2 * H + 2 * D
+    return 2 * (cfg["layers"] * block + H + cfg["vocab"] * H)
+
+
+def long_decode(args, local):
+    """Qwen3-4B (36 layers, hidden 2560, 32/8 heads, I 9728, tied), batch 1: a
+    seeded random prompt of --prompt ids fed token by token (one persistent
+    launch), then --steps greedy decode steps timed one lsx_model_advance call
+    each (CUDA events on the library stream).  Bytes per decode step: the bf16
+    weights plus the f32 K and V of every cached position."""
+    import torch
+
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import synth
+    gpu = lsx.Gpu(local)
+    cfg = synth.QWEN3_4B
+    P = args.prompt
+    model = lsx.Model.load(model_checkpoint("QWEN3_4B"), gpu, P + args.warmup + args.steps + 8)
+    prompt = synth.prompt_tokens(7, P, cfg["vocab"])
+    stream, event = cuda_timer(gpu)
+    t0 = time.perf_counter()
+    tokens, _, _ = model.generate(prompt, 1)
+    prefill_s = time.perf_counter() - t0
+    token = int(tokens[0])
+    for _ in range(args.warmup):
+        token = model.advance_token(token)
+    start, stop = event(), event()
+    pos0 = model.position()
+    with ClockSampler(gpu.device) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            token = model.advance_token(token)
+        stop.record(stream)
+        stop.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    kv = 2 * cfg["layers"] * cfg["kv_heads"] * cfg["head_dim"] * 4
+    mean_ctx = pos0 + (args.steps + 1) / 2
+    step_bytes = weight_bytes_per_step(cfg) + kv * mean_ctx
+    peaks = measured_peaks()
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "decode tok/s (Qwen3-4B bs1 after a long prompt)", "value": 1e3 / ms, "unit": "tok/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16 weights, f32 activations and KV (f32 accumulate)",
+        "data": f"synthetic: random-init Qwen3-4B architecture (seed 7), {P} random prompt ids",
+        "config": {"workload": f"Qwen3-4B bs1 greedy decode at context {pos0}..{pos0 + args.steps}",
+                   "prompt": P, "kv_cache": "f32", "timing": "one lsx_model_advance per step, CUDA events"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"],
+                     "scope": f"{step_bytes / 1e9:.3f} GB per step (weights + f32 KV at the mean context)"},
+        "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s,
+                    "note": "token by token in one persistent launch (as the reference prefills), wall clock"},
+        "clocks": clocks.summary(),
+    }))
+
+
+def scoring(args, local):
+    """Qwen3-8B (36 layers, hidden 4096, 32/8 heads, I 12288, untied lm_head)
+    teacher-forced case scoring: cases of 64 random prompt ids and 8 random
+    answer ids + EOS, each scored by lsx_model_score (prefill, then per target the
+    frame's loss and argmax, advancing with the target).  --cases of the 1024-case
+    job are timed end to end (host arrays in, losses and argmaxes out)."""
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import synth
+    gpu = lsx.Gpu(local)
+    cfg = synth.QWEN3_8B
+    eos = 151645
+    model = lsx.Model.load(model_checkpoint("QWEN3_8B"), gpu, 80)
+    V = cfg["vocab"]
+
+    def case(i):
+        prompt = synth.uniform_u32(7, 1000 + i, 64, V)
+        answer = synth.uniform_u32(7, 5000 + i, 8, V)
+        return prompt, np.append(answer, np.uint32(eos))
+
+    for i in range(max(1, args.warmup)):
+        model.reset()
+        model.score(*case(i))
+    gpu.synchronize()
+    n = args.cases
+    with ClockSampler(gpu.device) as clocks:
+        t0 = time.perf_counter()
+        for i in range(n):
+            model.reset()
+            model.score(*case(100 + i))
+        dt = time.perf_counter() - t0
+    steps_per_case = 64 + 9 - 1
+    step_bytes = weight_bytes_per_step(cfg)
+    peaks = measured_peaks()
+    achieved = n * steps_per_case * step_bytes / dt / 1e9
+    print(json.dumps({
+        "metric": "teacher-forced scoring cases/s (Qwen3-8B, 64-token prompt + 9 scored targets)",
+        "value": n / dt, "unit": "cases/s", "n_gpus": 1, "steps": n, "warmup": args.warmup,
+        "ms_per_step": dt / n * 1e3, "higher_is_better": True,
+        "dtype": "bf16 weights, f32 activations and KV, f64 loss",
+        "data": "synthetic: random-init Qwen3-8B architecture (seed 7), random prompt and answer ids",
+        "config": {"workload": "Qwen3-8B teacher-forced scoring, 64 prompt + 8 answer + EOS per case",
+                   "cases_timed": n, "job_cases": 1024, "decode_steps_per_case": steps_per_case,
+                   "timing": "wall clock around lsx_model_score per case (host buffers)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"],
+                     "scope": f"token-by-token decode steps, {step_bytes / 1e9:.3f} GB of weights each "
+                              "(a batched-prefill GEMM path would make this tensor-bound)"},
+        "job_seconds_estimate": 1024 / (n / dt),
+        "clocks": clocks.summary(),
+    }))
 
 
 def reference_arm(args, rank, world):

@@ -163,16 +163,17 @@ __device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch
 #pragma unroll
             for (int j = 0; j < kBatch; ++j) stale |= (uint32_t)(v[j] >> 32) != epoch;
             if (!stale) break;
+            // re-read first: the abort flag's load then overlaps the round trip
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const int i = base + tid + j * kCompute;
+                if ((uint32_t)(v[j] >> 32) != epoch) v[j] = ld_relaxed(src + i);
+            }
             if (start == 0) {
                 start = clock64();
             } else if (clock64() - start > kSpin || aborted(st)) {
                 ok = false;
                 break;
-            }
-#pragma unroll
-            for (int j = 0; j < kBatch; ++j) {
-                const int i = base + tid + j * kCompute;
-                if ((uint32_t)(v[j] >> 32) != epoch) v[j] = ld_relaxed(src + i);
             }
         }
         if (!ok) break;
@@ -221,15 +222,15 @@ __device__ bool poll_segments(const unsigned long long* s0, int n0, float* d0, c
 #pragma unroll
             for (int j = 0; j < 4; ++j) stale |= (uint32_t)(v[j] >> 32) != epoch;
             if (!stale) break;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if ((uint32_t)(v[j] >> 32) != epoch) v[j] = ld_relaxed(src[j]);
             if (start == 0) {
                 start = clock64();
             } else if (clock64() - start > kSpin || aborted(st)) {
                 ok = false;
                 break;
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if ((uint32_t)(v[j] >> 32) != epoch) v[j] = ld_relaxed(src[j]);
         }
         if (!ok) break;
 #pragma unroll
@@ -1134,12 +1135,12 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 unsigned long long v = ld_relaxed(src);
                 long long start = 0;
                 while ((uint32_t)(v & 0x1FFFull) != (e_head & 0x1FFFu)) {
+                    v = ld_relaxed(src);
                     if (start == 0) start = clock64();
                     else if (clock64() - start > kSpin || aborted(st)) {
                         ok = false;
                         break;
                     }
-                    v = ld_relaxed(src);
                 }
                 gathered[tid] = v;
             }

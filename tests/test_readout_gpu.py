@@ -132,3 +132,29 @@ def test_verify_cached_on_tiny_model(gpu, oracle, golden_tiny):
     margins = [oracle.minimum_margin(ref.readout(f.hidden, spec.apply), int(t)) for f, t in zip(frames, tokens)]
     assert abs(v.target_min_margin - min(margins)) < 1e-4
     assert v.readout_calls == 2 * len(frames)
+
+
+def test_compact_readout_matches_oracle(gpu, oracle):
+    """CompactReadout (src/diagnosis.rs:608-666): z = z0 + F ((R - I) x) per
+    observation, checked against the oracle's f32 matvec with the baseline as bias
+    (the linear tolerance of tests/gpu.rs:19-40), and its deadline and finiteness
+    checks."""
+    V, r, n = 4099, 16, 5
+    rng = np.random.default_rng(11)
+    images = [rng.standard_normal(V).astype(np.float32) * 0.1 for _ in range(r)]
+    baseline = [rng.standard_normal(V).astype(np.float32) for _ in range(n)]
+    coordinates = [rng.standard_normal(r) for _ in range(n)]
+    q, _ = np.linalg.qr(rng.standard_normal((r, r)))
+    compact = diagnosis.CompactReadout(gpu, images, baseline, coordinates)
+    got = compact.evaluate(gpu, q, diagnosis.Deadline(60.0))
+    F = np.stack(images, axis=1)  # [V, r]
+    delta = (q - np.eye(r)) @ np.stack(coordinates, axis=1)
+    for i in range(n):
+        want = oracle.matvec(F, 0, delta[:, i].astype(np.float32), baseline[i], V, r)
+        assert np.all(np.abs(got[i] - want) <= 2e-6 * (1 + np.abs(want)))
+    with pytest.raises(diagnosis.BudgetExpired):
+        compact.evaluate(gpu, q, diagnosis.Deadline(0.0))
+    bad = [b.copy() for b in baseline]
+    bad[2][7] = np.inf
+    with pytest.raises(ValueError):
+        diagnosis.CompactReadout(gpu, images, bad, coordinates).evaluate(gpu, q, diagnosis.Deadline(60.0))
