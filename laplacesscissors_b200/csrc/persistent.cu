@@ -83,6 +83,8 @@ struct PArgs {
     const FusedLayer* layers;
     const float2* rope;
     unsigned long long *t_resid, *t_qkv, *t_attn, *t_feat, *t_arg;
+    unsigned long long* t_part;  // split attention: per query head, ns partial states of D + 2 words
+    int ns, bs, split_min;       // slots per KV group, positions per block, first split position + 1
     DecodeState* state;
     int steps;
     int slots;
@@ -783,6 +785,277 @@ __device__ __forceinline__ bool attention_head(const PArgs& a, const FusedLayer&
     return true;
 }
 
+// ---- long contexts: attention split over the CTAs ---------------------------
+// Past `split_min` positions one query head per CTA leaves most SMs idle while
+// the K/V reads grow with the context.  Instead the CTAs of slot s of KV group g
+// (CTA g + KVH s, s < ns) each own the position blocks b = s, s + ns, s + 2 ns ...
+// (BS positions per block) of group g for the whole generation.  The CTA reads
+// each cached K/V row once for all R query heads of the group, and publishes per
+// head a partial softmax state (running max m, sum l, unnormalised output o[D]).
+// CTA h then merges the ns partials of query head h and publishes its attention
+// output (kernels/ops.py:88-101 evaluated in another order: the same exp/max
+// rescaling, summed over blocks).  The owner of the current position's block
+// appends its k and v to the cache, so each cached position is written and later
+// read by one CTA.
+
+// Position of local index j of slot s.
+__device__ __forceinline__ int split_position(int j, int s, int ns, int bs) {
+    return ((j / bs) * ns + s) * bs + (j % bs);
+}
+
+// Number of local positions of slot s at or before `pos`.
+__device__ __forceinline__ int split_count(int pos, int s, int ns, int bs) {
+    int n = 0;
+    for (int b = s; b * bs <= pos; b += ns) n += min(bs, pos + 1 - b * bs);
+    return n;
+}
+
+template <int DPL, int PB, int R>
+__device__ __forceinline__ bool attention_part(const PArgs& a, const FusedLayer& L, int g, int s, int pos,
+                                               uint32_t e_qkv, uint32_t e_attn, float* sm) {
+    constexpr int D = DPL * 32;
+    constexpr int CNT = R * PB;          // scores reduced together per batch
+    constexpr int LPV = 32 / CNT;        // lanes holding each reduced score
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int qw = a.QH * D, kw = a.KVH * D;
+    const int ns = a.ns, bs = a.bs;
+    float* raw = sm;                 // (R + 2) D: the group's q heads, k, v
+    float* merge = raw + (R + 2) * D;  // kWarps R (D + 2)
+    const float* kbase = L.keys + (size_t)g * D;
+    const float* vbase = L.values + (size_t)g * D;
+    const int n = split_count(pos, s, ns, bs);
+    // the first batch of cached positions does not depend on this step
+    float kv[PB][DPL], vv[PB][DPL];
+#pragma unroll
+    for (int b = 0; b < PB; ++b) {
+        const int j = warp + kWarps * b;
+        const int t = j < n ? split_position(j, s, ns, bs) : pos;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) {
+            kv[b][d] = t < pos ? __ldcg(kbase + (size_t)t * kw + lane + 32 * d) : 0.f;
+            vv[b][d] = t < pos ? __ldcg(vbase + (size_t)t * kw + lane + 32 * d) : 0.f;
+        }
+    }
+    float qg[DPL], kg[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) {
+        qg[d] = L.q_gain ? __ldg(L.q_gain + lane + 32 * d) : 1.f;
+        kg[d] = L.k_gain ? __ldg(L.k_gain + lane + 32 * d) : 1.f;
+    }
+    const int half = a.rotary / 2;
+    float2 cs[DPL / 2 > 0 ? DPL / 2 : 1];
+#pragma unroll
+    for (int d = 0; d < DPL / 2; ++d) cs[d] = a.rope[(size_t)pos * half + lane + 32 * d];
+    bool ok = poll_segments(a.t_qkv + (size_t)g * R * D, R * D, raw, a.t_qkv + qw + (size_t)g * D, D, raw + R * D,
+                            a.t_qkv + qw + kw + (size_t)g * D, D, raw + (R + 1) * D, e_qkv, a.state);
+    if (!compute_and(ok)) return false;
+    float q[R][DPL], k[DPL], v[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) q[i][d] = raw[i * D + lane + 32 * d];
+        k[d] = raw[R * D + lane + 32 * d];
+        v[d] = raw[(R + 1) * D + lane + 32 * d];
+    }
+    // QK-norm (kernels/ops.py:31-45 over head_dim) and rotate-half RoPE in registers
+    if (L.q_gain) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            float ss = 0.f;
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) ss = fmaf(q[i][d], q[i][d], ss);
+            const float inverse = rsqrtf(warp_allsum(ss) / (float)D + a.qk_eps);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) q[i][d] = q[i][d] * inverse * qg[d];
+        }
+    }
+    if (L.k_gain) {
+        float ss = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) ss = fmaf(k[d], k[d], ss);
+        const float inverse = rsqrtf(warp_allsum(ss) / (float)D + a.qk_eps);
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) k[d] = k[d] * inverse * kg[d];
+    }
+#pragma unroll
+    for (int d = 0; d < DPL / 2; ++d) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const float q1 = q[i][d], q2 = q[i][d + DPL / 2];
+            q[i][d] = q1 * cs[d].x + -1.f * q2 * cs[d].y;
+            q[i][d + DPL / 2] = q2 * cs[d].x + 1.f * q1 * cs[d].y;
+        }
+        const float k1 = k[d], k2 = k[d + DPL / 2];
+        k[d] = k1 * cs[d].x + -1.f * k2 * cs[d].y;
+        k[d + DPL / 2] = k2 * cs[d].x + 1.f * k1 * cs[d].y;
+    }
+    if (((pos / bs) % ns) == s && warp == 0) {  // kernels/ops.py:69-73: append this position's k, v
+        float* kd = L.keys + (size_t)pos * kw + (size_t)g * D;
+        float* vd = L.values + (size_t)pos * kw + (size_t)g * D;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) {
+            kd[lane + 32 * d] = k[d];
+            vd[lane + 32 * d] = v[d];
+        }
+    }
+    // Online softmax per head over this warp's positions, PB at a time.  After the
+    // reduction lane l holds score (l / LPV): head (l / LPV) / PB, position (l / LPV) % PB.
+    const int vi = lane / LPV, my_head = vi / PB, my_b = vi % PB;
+    float m[R], l[R], acc[R][DPL];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[i][d] = 0.f;
+    }
+    for (int i0 = 0; warp + kWarps * i0 < n; i0 += PB) {
+        if (i0 > 0) {
+#pragma unroll
+            for (int b = 0; b < PB; ++b) {
+                const int j = warp + kWarps * (i0 + b);
+                const int t = j < n ? split_position(j, s, ns, bs) : pos;
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) {
+                    kv[b][d] = t < pos ? __ldcg(kbase + (size_t)t * kw + lane + 32 * d) : 0.f;
+                    vv[b][d] = t < pos ? __ldcg(vbase + (size_t)t * kw + lane + 32 * d) : 0.f;
+                }
+            }
+        }
+        float sc[CNT];
+#pragma unroll
+        for (int b = 0; b < PB; ++b) {
+            const int j = warp + kWarps * (i0 + b);
+            if (j < n && split_position(j, s, ns, bs) == pos) {  // the current position, from registers
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) {
+                    kv[b][d] = k[d];
+                    vv[b][d] = v[d];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                float x = 0.f;
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) x = fmaf(q[i][d], kv[b][d], x);
+                sc[i * PB + b] = x;
+            }
+        }
+        RowReduce<CNT, 16>::run(sc, lane);
+        const bool valid = warp + kWarps * (i0 + my_b) < n;
+        const float sv = valid ? sc[0] * a.scale : -INFINITY;
+        // per-head maximum and sum over the batch: xor within the head's lane segment
+        float mb = sv;
+#pragma unroll
+        for (int o = LPV; o < PB * LPV; o <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        float mn[R], carry[R];
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            mn[i] = fmaxf(m[i], __shfl_sync(0xffffffffu, mb, i * PB * LPV));
+            carry[i] = expf(m[i] - mn[i]);
+        }
+        float mine = mn[0];
+#pragma unroll
+        for (int i = 1; i < R; ++i) mine = my_head == i ? mn[i] : mine;
+        const float p = valid ? expf(sv - mine) : 0.f;
+        float ps = p;
+#pragma unroll
+        for (int o = LPV; o < PB * LPV; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            l[i] = l[i] * carry[i] + __shfl_sync(0xffffffffu, ps, i * PB * LPV);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) acc[i][d] *= carry[i];
+#pragma unroll
+            for (int b = 0; b < PB; ++b) {
+                const float pb = __shfl_sync(0xffffffffu, p, (i * PB + b) * LPV);
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) acc[i][d] = fmaf(pb, vv[b][d], acc[i][d]);
+            }
+            m[i] = mn[i];
+        }
+    }
+    // merge the warps' states per head, then publish this slot's partial per head
+    const int stride = D + 2;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        float* slot = merge + (size_t)(warp * R + i) * stride;
+        if (lane == 0) {
+            slot[0] = m[i];
+            slot[1] = l[i];
+        }
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) slot[2 + lane + 32 * d] = acc[i][d];
+    }
+    compute_sync();
+    for (int idx = tid; idx < R * stride; idx += kCompute) {
+        const int i = idx / stride, e = idx % stride;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, merge[(w * R + i) * stride]);
+        float val;
+        if (e == 0) {
+            val = M;
+        } else {
+            val = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float* sl = merge + (size_t)(w * R + i) * stride;
+                if (sl[0] == -INFINITY) continue;
+                val = fmaf(sl[e], expf(sl[0] - M), val);
+            }
+        }
+        const int h = g * R + i;
+        st_relaxed(a.t_part + ((size_t)h * ns + s) * stride + e, tagged(e_attn, val));
+    }
+    // The merge area is rewritten only after later block-wide barriers.
+    return true;
+}
+
+// Merges the ns partial states of query head h and publishes its attention output.
+template <int DPL>
+__device__ __forceinline__ bool attention_merge(const PArgs& a, int h, uint32_t e_attn, float* sm) {
+    constexpr int D = DPL * 32;
+    const int tid = threadIdx.x;
+    const int ns = a.ns, stride = D + 2;
+    bool ok = poll_vector(a.t_part + (size_t)h * ns * stride, ns * stride, e_attn, sm, a.state);
+    if (!compute_and(ok)) return false;
+    for (int d = tid; d < D; d += kCompute) {
+        float M = -INFINITY;
+        for (int s = 0; s < ns; ++s) M = fmaxf(M, sm[s * stride]);
+        float Lsum = 0.f, O = 0.f;
+        for (int s = 0; s < ns; ++s) {
+            const float* sl = sm + (size_t)s * stride;
+            if (sl[0] == -INFINITY) continue;
+            const float ex = expf(sl[0] - M);
+            Lsum = fmaf(sl[1], ex, Lsum);
+            O = fmaf(sl[2 + d], ex, O);
+        }
+        st_relaxed(a.t_attn + (size_t)h * D + d, tagged(e_attn, O / Lsum));
+    }
+    return true;
+}
+
+template <int DPL>
+__device__ bool attention_split(const PArgs& a, const FusedLayer& L, int c, int pos, uint32_t e_qkv,
+                                uint32_t e_attn, float* sm) {
+    bool ok = true;
+    if (c < a.KVH * a.ns) {
+        const int g = c % a.KVH, s = c / a.KVH;
+        // the host enables the split only for these ratios (head_dim 256: up to 2)
+        const int ratio = a.QH / a.KVH;
+        if (ratio == 1) ok = attention_part<DPL, 8, 1>(a, L, g, s, pos, e_qkv, e_attn, sm);
+        else if (ratio == 2) ok = attention_part<DPL, 8, 2>(a, L, g, s, pos, e_qkv, e_attn, sm);
+        if constexpr (DPL < 8) {
+            if (ratio == 4) ok = attention_part<DPL, 8, 4>(a, L, g, s, pos, e_qkv, e_attn, sm);
+            else if (ratio == 8) ok = attention_part<DPL, 4, 8>(a, L, g, s, pos, e_qkv, e_attn, sm);
+        }
+        compute_sync();  // the part's scratch is read before the merge reuses it
+    }
+    if (ok && c < a.QH) ok = attention_merge<DPL>(a, c, e_attn, sm);
+    return ok;
+}
+
 // Norm gains of one width in a strided layout (i = tid + j * kCompute), for the
 // shared-memory RMSNorm used by the generic widths and the final norm.
 constexpr int kGainRegs = 24;  // widths up to 24 * kCompute
@@ -1006,8 +1279,11 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     if (!ok) break;
                     LSX_PHASE_MARK(3);
                 }
-                // attention: one query head per CTA
-                if (c < a.QH) {
+                // attention: one query head per CTA, or split over the CTAs at long contexts
+                if (a.ns > 0 && pos + 1 >= a.split_min) {
+                    ok = attention_split<DPL>(a, Lr, c, pos, e_qkv, e_attn, scratch);
+                    if (!ok) break;
+                } else if (c < a.QH) {
                     ok = attention_head<DPL, PB>(a, Lr, c, pos, e_qkv, e_attn, scratch);
                     if (!ok) break;
                 }
@@ -1201,9 +1477,28 @@ PKernel kernel_for(const FusedConfig& c) {
     return nullptr;
 }
 
-int scratch_floats(const FusedConfig& c) {
+// Split attention: slots per KV group (0: never split), at most 32.  It needs the
+// full-width rotate-half RoPE and a group ratio of 1, 2, 4 or 8 (1 or 2 at head_dim 256).
+int split_slots(const FusedConfig& c, int grid) {
+    const int ratio = c.kvheads > 0 ? c.qheads / c.kvheads : 0;
+    const bool fast_rope = c.rotary == c.head_dim && !c.interleaved;
+    const int max_ratio = c.head_dim >= 256 ? 2 : 8;
+    if (!fast_rope || ratio * c.kvheads != c.qheads || ratio > max_ratio ||
+        (ratio != 1 && ratio != 2 && ratio != 4 && ratio != 8))
+        return 0;
+    const int ns = std::min(grid / c.kvheads, 32);
+    return ns >= 2 ? ns : 0;
+}
+
+int scratch_floats(const FusedConfig& c, int grid) {
     const int D = c.head_dim;
-    const int attention = 3 * D + kWarps * (D + 2) + 3 * D;
+    int attention = 3 * D + kWarps * (D + 2) + 3 * D;
+    const int ns = split_slots(c, grid);
+    if (ns > 0) {
+        const int ratio = c.qheads / c.kvheads;
+        attention = std::max(attention, (ratio + 2) * D + kWarps * ratio * (D + 2));
+        attention = std::max(attention, ns * (D + 2));
+    }
     return (std::max(attention, 512 + 2 * 256) + 3) & ~3;
 }
 
@@ -1217,7 +1512,7 @@ SmemLayout layout_for(const FusedConfig& c, int slots, int slot_bytes, int grid,
     s.xs = (int)at;
     at += (size_t)xmax * 4;
     s.scratch = (int)at;
-    at += (size_t)scratch_floats(c) * 4;
+    at += (size_t)scratch_floats(c, grid) * 4;
     s.resid = (int)at;
     at += (size_t)rmax * 4;
     s.red = (int)at;
@@ -1294,6 +1589,13 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
     LSX_TRY(alloc((size_t)qw * 8, (void**)&t_attn_));
     LSX_TRY(alloc((size_t)c.intermediate * 8, (void**)&t_feat_));
     LSX_TRY(alloc((size_t)grid_ * 8, (void**)&t_arg_));
+    // Split attention from position split_min_ - 1 on (LSX_DECODE_SPLIT_MIN overrides;
+    // 0 turns it off).
+    ns_ = split_slots(c, grid_);
+    split_min_ = 128;
+    if (const char* v = std::getenv("LSX_DECODE_SPLIT_MIN")) split_min_ = std::max(0, std::atoi(v));
+    if (split_min_ == 0) ns_ = 0;
+    if (ns_ > 0) LSX_TRY(alloc((size_t)c.qheads * ns_ * (c.head_dim + 2) * 8, (void**)&t_part_));
     const int half = c.rotary / 2;
     if (half > 0) {
         std::vector<float2> table((size_t)c.capacity * half);
@@ -1363,6 +1665,10 @@ int PersistentDecoder::run(int steps) {
     a.t_attn = t_attn_;
     a.t_feat = t_feat_;
     a.t_arg = t_arg_;
+    a.t_part = t_part_;
+    a.ns = ns_;
+    a.bs = 16;
+    a.split_min = split_min_;
     a.state = state_;
     a.steps = steps;
     a.slots = slots_;

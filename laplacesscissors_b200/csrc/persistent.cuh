@@ -29,10 +29,11 @@ private:
     void* layers_dev_ = nullptr;
     float2* rope_ = nullptr;
     unsigned long long *t_resid_ = nullptr, *t_qkv_ = nullptr, *t_attn_ = nullptr, *t_feat_ = nullptr,
-                       *t_arg_ = nullptr;
+                       *t_arg_ = nullptr, *t_part_ = nullptr;
     size_t smem_ = 0;
     int slots_ = 0;
     int inflight_ = 0;
+    int ns_ = 0, split_min_ = 0;  // split attention: slots per KV group, first position + 1
     int grid_ = 0;
     int layer_count_ = 0;
     std::vector<void*> owned_;
