@@ -203,6 +203,18 @@ int lsx_model_score(lsx_model* model, const uint32_t* prompt, size_t prompt_leng
                     size_t count, const lsx_rotation* rotation, double* nll_out, uint32_t* argmax_out,
                     float* hidden_frames, float* logits_frames);
 
+/* lsx_model_score over `cases` independent cases of equal shape at once (the
+   per-case loop of scaling::evaluate, src/scaling.rs:181-216, batched): prompts
+   [cases x prompt_length], targets [cases x count]; nll_out and argmax_out
+   [cases x count], logits_out [cases x count x vocab] (host, each may be NULL).
+   The fed tokens of all cases go through each layer together (tensor-core GEMMs
+   with the f32 activations as two bf16 terms); results agree with lsx_model_score
+   within the decode tolerances.  The model's decode cursor and KV cache are not
+   touched.  No edit: the "after" scores use lsx_model_score with a rotation. */
+int lsx_model_score_batch(lsx_model* model, const uint32_t* prompts, size_t cases, size_t prompt_length,
+                          const uint32_t* targets, size_t count, double* nll_out, uint32_t* argmax_out,
+                          float* logits_out);
+
 /* ------------------------------------------------------ readout validation -- */
 /* Fused readout margin over many hidden states (verify_cached's target rows,
    src/diagnosis.rs:512-537 with minimum_margin src/diagnosis.rs:490-492 and argmax

@@ -1,0 +1,453 @@
+// Batched teacher-forced forward: many cases of equal length through the decoder
+// at once, each layer's projections as tensor-core GEMMs over all tokens.
+//
+// Teacher forcing (src/scaling.rs:181-216) knows every input token in advance: a
+// case feeds its prompt and then each target but the last, and scores the frames
+// from the last prompt position on.  The reference feeds them one decode step at a
+// time (Model::advance, src/model.rs:694-853); here the T = prompt + count - 1
+// tokens of every case go through each layer together, so a layer's weights are
+// read once per batch of cases instead of once per token.  Per layer:
+//
+//   x [M, H] f32 (M = cases x T rows, case-major)
+//   RMSNorm(x) -> A planes (bf16 hi/lo of the f32 activations)
+//   [q; k; v] = A Wqkv^T              (tcgen05 GEMM, f32 out)
+//   QK-norm + RoPE per head, in place (position = row within the case)
+//   causal attention within each case -> A planes
+//   x += A Wo^T                       (GEMM, residual add in the epilogue)
+//   RMSNorm(x) -> A planes
+//   [g0 u0 g1 u1 ...] = A Wgu^T       (GEMM)
+//   act(g) * u -> A planes
+//   x += A Wd^T                       (GEMM, residual add)
+//
+// then the final RMSNorm of the scored rows, the lm_head GEMM into f32 logits and
+// per row attribution::loss (src/attribution.rs:49-60) and the first argmax
+// (src/diagnosis.rs:58-70).  The f32 activations enter the tensor cores as two
+// bf16 terms (hi + lo carries 16 significant bits), each multiplied by the bf16
+// weights with f32 accumulation.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "batched.cuh"
+#include "device_common.cuh"
+
+namespace lsx {
+
+int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int M, int K,
+                        const __nv_bfloat16* w, int N, const float* bias, float* out, int ldo, bool accumulate,
+                        int* status);
+
+namespace {
+
+__device__ __forceinline__ float act_fn(float x, int kind) {
+    switch (kind) {
+    case 0: return x / (1.f + expf(-x));
+    case 1: return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
+    case 2: return fmaxf(x, 0.f);
+    default: return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+    }
+}
+
+__device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < warps; ++i) t += red[i];
+    return t;
+}
+
+// x[m] = embedding row of tokens[m] (Model::embedding_tensor, src/model.rs:620-631).
+__global__ void embed_rows_kernel(const void* __restrict__ emb, int kind, float scale, const uint32_t* __restrict__ tokens,
+                                  int H, float* __restrict__ x) {
+    const size_t m = blockIdx.x;
+    const size_t base = (size_t)tokens[m] * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        float v;
+        if (kind == LSX_BF16) v = __bfloat162float(((const __nv_bfloat16*)emb)[base + i]);
+        else if (kind == LSX_F32) v = ((const float*)emb)[base + i];
+        else v = __half2float(((const __half*)emb)[base + i]);
+        if (scale != 1.f) v = __fadd_rn(v, __fmul_rn(scale - 1.f, v));
+        x[m * H + i] = v;
+    }
+}
+
+// A planes of RMSNorm(x[rows[r]]) * gain (kernels/ops.py:31-45); rows == nullptr: r.
+__global__ void rms_planes_kernel(const float* __restrict__ x, const int* __restrict__ rows, int H,
+                                  const float* __restrict__ gain, float eps, __nv_bfloat16* __restrict__ hi,
+                                  __nv_bfloat16* __restrict__ lo) {
+    __shared__ float red[32];
+    const size_t r = blockIdx.x;
+    const float* xr = x + (size_t)(rows ? rows[r] : (int)r) * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    const float inverse = rsqrtf(block_sum(ss, red) / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) split_store(hi, lo, r * H + i, xr[i] * inverse * gain[i]);
+}
+
+// QK-norm and rotate-half RoPE in place on the q and k heads of every row; one
+// warp per (row, head).  rope: [T, D/2] (cos, sin) per position.
+template <int DPL>
+__global__ void qk_rope_kernel(float* __restrict__ qkv, int M, int T, int QH, int KVH, const float* __restrict__ q_gain,
+                               const float* __restrict__ k_gain, float eps, const float2* __restrict__ rope) {
+    constexpr int D = DPL * 32;
+    const int lane = threadIdx.x & 31;
+    const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int heads = QH + KVH;
+    if (wid >= (long long)M * heads) return;
+    const int m = (int)(wid / heads), h = (int)(wid % heads);
+    const int t = m % T;
+    const bool is_q = h < QH;
+    const float* gain = is_q ? q_gain : k_gain;
+    float* v = qkv + (size_t)m * (QH + 2 * KVH) * D + (size_t)h * D;
+    float e[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) e[j] = v[lane + 32 * j];
+    if (gain) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) ss = fmaf(e[j], e[j], ss);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inverse = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) e[j] = e[j] * inverse * gain[lane + 32 * j];
+    }
+#pragma unroll
+    for (int j = 0; j < DPL / 2; ++j) {
+        const float2 cs = rope[(size_t)t * (D / 2) + lane + 32 * j];
+        const float a = e[j], b = e[j + DPL / 2];
+        e[j] = a * cs.x + -1.f * b * cs.y;
+        e[j + DPL / 2] = b * cs.x + 1.f * a * cs.y;
+    }
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) v[lane + 32 * j] = e[j];
+}
+
+// Causal attention within each case (kernels/ops.py:76-101): one warp per (row,
+// query head), keys s <= t of the row's case in batches of 8 (online softmax).
+// Output: A planes [M, QH * D].
+template <int DPL>
+__global__ void causal_attention_kernel(const float* __restrict__ qkv, int M, int T, int QH, int KVH, float scale,
+                                        __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    constexpr int D = DPL * 32;
+    constexpr int PB = 8, LPV = 32 / PB;
+    const int lane = threadIdx.x & 31;
+    const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (wid >= (long long)M * QH) return;
+    const int m = (int)(wid / QH), h = (int)(wid % QH);
+    const int t = m % T, first = m - t;
+    const int g = h / (QH / KVH);
+    const size_t stride = (size_t)(QH + 2 * KVH) * D;
+    const float* kbase = qkv + (size_t)QH * D + (size_t)g * D;
+    const float* vbase = kbase + (size_t)KVH * D;
+    float q[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) q[j] = qkv[(size_t)m * stride + (size_t)h * D + lane + 32 * j];
+    float mx = -INFINITY, l = 0.f, acc[DPL];
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) acc[j] = 0.f;
+    const int my_b = lane / LPV;
+    for (int s0 = 0; s0 <= t; s0 += PB) {
+        float kv[PB][DPL], vv[PB][DPL], sc[PB];
+#pragma unroll
+        for (int b = 0; b < PB; ++b) {
+            const int s = s0 + b;
+            const size_t row = (size_t)(first + (s <= t ? s : t)) * stride;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) {
+                kv[b][j] = kbase[row + lane + 32 * j];
+                vv[b][j] = vbase[row + lane + 32 * j];
+            }
+            float x = 0.f;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) x = fmaf(q[j], kv[b][j], x);
+            sc[b] = x;
+        }
+        // transposing butterfly: lane l ends with the total of key l / LPV
+#pragma unroll
+        for (int cnt = PB, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+            const bool up = (lane & off) != 0;
+#pragma unroll
+            for (int i = 0; i < cnt / 2; ++i) {
+                const float keep = up ? sc[i + cnt / 2] : sc[i];
+                const float send = up ? sc[i] : sc[i + cnt / 2];
+                sc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+        for (int off = LPV / 2; off > 0; off >>= 1) sc[0] += __shfl_xor_sync(0xffffffffu, sc[0], off);
+        const bool valid = s0 + my_b <= t;
+        const float sv = valid ? sc[0] * scale : -INFINITY;
+        float mb = sv;
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float mn = fmaxf(mx, mb);
+        const float carry = expf(mx - mn);
+        const float p = valid ? expf(sv - mn) : 0.f;
+        float ps = (lane % LPV) == 0 ? p : 0.f;
+        for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        l = l * carry + ps;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] *= carry;
+#pragma unroll
+        for (int b = 0; b < PB; ++b) {
+            const float pb = __shfl_sync(0xffffffffu, p, b * LPV);
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[j] = fmaf(pb, vv[b][j], acc[j]);
+        }
+        mx = mn;
+    }
+    const size_t o = (size_t)m * QH * D + (size_t)h * D;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) split_store(hi, lo, o + lane + 32 * j, acc[j] / l);
+}
+
+// A planes of act(gate) * up from the interleaved [g0 u0 g1 u1 ...] rows.
+__global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, int I, int kind,
+                                    __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t m = i / I, f = i % I;
+        const float2 v = *reinterpret_cast<const float2*>(gu + m * 2 * I + 2 * f);
+        split_store(hi, lo, i, act_fn(v.x, kind) * v.y);
+    }
+}
+
+// First argmax of each logit row (src/diagnosis.rs:58-70) as a packed key max.
+__global__ void __launch_bounds__(1024) row_argmax_kernel(const float* __restrict__ logits, int V,
+                                                          uint32_t* __restrict__ argmax) {
+    __shared__ unsigned long long red[32];
+    const float* z = logits + (size_t)blockIdx.x * V;
+    unsigned long long best = 0ull;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const unsigned long long k = pack_arg(z[j], (uint32_t)j);
+        best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+        best = red[0] > best ? red[0] : best;
+        argmax[blockIdx.x] = 0xffffffffu - (uint32_t)(best & 0xffffffffull);
+    }
+}
+
+// attribution::loss (src/attribution.rs:49-60): logsumexp(z) - z[target] in f64.
+__global__ void __launch_bounds__(1024) row_nll_kernel(const float* __restrict__ logits, int V,
+                                                       const uint32_t* __restrict__ targets, double* __restrict__ nll) {
+    __shared__ double red[32];
+    const float* z = logits + (size_t)blockIdx.x * V;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
+    double top = -INFINITY;
+    for (int j = tid; j < V; j += blockDim.x) top = fmax(top, (double)z[j]);
+    for (int o = 16; o > 0; o >>= 1) top = fmax(top, __shfl_xor_sync(0xffffffffu, top, o));
+    if (lane == 0) red[warp] = top;
+    __syncthreads();
+    top = red[0];
+    for (int w = 1; w < warps; ++w) top = fmax(top, red[w]);
+    __syncthreads();
+    double sum = 0.0;
+    for (int j = tid; j < V; j += blockDim.x) sum += exp((double)z[j] - top);
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        double total = 0.0;
+        for (int w = 0; w < warps; ++w) total += red[w];
+        nll[blockIdx.x] = top + log(total) - (double)z[targets[blockIdx.x]];
+    }
+}
+
+}  // namespace
+
+BatchedScorer::~BatchedScorer() {
+    if (block_) cudaFree(block_);
+}
+
+bool BatchedScorer::eligible(const FusedConfig& c, std::string* why) {
+    const int dpl = c.head_dim / 32;
+    if (c.head_dim % 32 != 0 || (dpl != 2 && dpl != 4 && dpl != 8)) {
+        if (why) *why = "head_dim must be 64, 128 or 256";
+        return false;
+    }
+    if (c.rotary != c.head_dim || c.interleaved) {
+        if (why) *why = "only full-width rotate-half RoPE";
+        return false;
+    }
+    if (c.hidden % 8 != 0 || c.intermediate % 8 != 0 || c.kvheads <= 0 || c.qheads % c.kvheads != 0) {
+        if (why) *why = "widths must be multiples of 8";
+        return false;
+    }
+    return true;
+}
+
+int BatchedScorer::reserve(size_t rows, size_t scored, size_t T) {
+    const FusedConfig& c = config_;
+    const size_t H = c.hidden, V = c.vocab, D = c.head_dim;
+    const size_t qkvw = (size_t)(c.qheads + 2 * c.kvheads) * D;
+    const size_t widest = std::max(H, std::max((size_t)c.qheads * D, (size_t)c.intermediate));
+    auto up = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    Layout L{};
+    size_t at = 0;
+    L.x = at;
+    at = up(at + rows * H * 4);
+    L.work = at;  // [q; k; v] rows, then gate/up rows
+    at = up(at + rows * std::max(qkvw, 2 * (size_t)c.intermediate) * 4);
+    L.planes = at;
+    at = up(at + 2 * std::max(rows, scored) * widest * 2);
+    L.logits = at;
+    at = up(at + scored * V * 4);
+    L.rope = at;
+    at = up(at + T * (D / 2) * 8);
+    L.tokens = at;
+    at = up(at + rows * 4);
+    L.targets = at;
+    at = up(at + scored * 4);
+    L.rows = at;
+    at = up(at + scored * 4);
+    L.nll = at;
+    at = up(at + scored * 8);
+    L.argmax = at;
+    at = up(at + scored * 4);
+    L.status = at;
+    at = up(at + 16);
+    L.total = at;
+    if (L.total > capacity_) {
+        if (block_) cudaFree(block_);
+        block_ = nullptr;
+        capacity_ = 0;
+        LSX_CUDA(cudaMalloc(&block_, L.total), "batched scoring buffers");
+        capacity_ = L.total;
+    }
+    layout_ = L;
+    return LSX_OK;
+}
+
+int BatchedScorer::build(lsx_ctx* ctx, const FusedConfig& config, const std::vector<FusedLayer>& layers) {
+    std::string why;
+    if (!eligible(config, &why)) return fail(LSX_E_UNSUPPORTED, "batched scoring: " + why);
+    ctx_ = ctx;
+    config_ = config;
+    layers_ = layers;
+    return LSX_OK;
+}
+
+int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count,
+                         const uint32_t* targets, double* nll_out, uint32_t* argmax_out, float* logits_out) {
+    const FusedConfig& c = config_;
+    LSX_ENSURE(cases > 0 && T > 0 && count > 0 && first + count <= T, "check the case shape");
+    const size_t rows = cases * T, scored = cases * count;
+    LSX_ENSURE(rows <= 2147483647ull / 4 && scored * (size_t)c.vocab <= (size_t)1 << 40, "too many rows");
+    LSX_TRY(reserve(rows, scored, T));
+    const Layout& L = layout_;
+    uint8_t* base = (uint8_t*)block_;
+    float* x = (float*)(base + L.x);
+    float* work = (float*)(base + L.work);
+    const size_t widest = std::max((size_t)c.hidden, std::max((size_t)c.qheads * c.head_dim, (size_t)c.intermediate));
+    __nv_bfloat16* hi = (__nv_bfloat16*)(base + L.planes);
+    __nv_bfloat16* lo = hi + std::max(rows, scored) * widest;
+    float* logits = (float*)(base + L.logits);
+    float2* rope = (float2*)(base + L.rope);
+    uint32_t* d_tokens = (uint32_t*)(base + L.tokens);
+    uint32_t* d_targets = (uint32_t*)(base + L.targets);
+    int* d_rows = (int*)(base + L.rows);
+    double* d_nll = (double*)(base + L.nll);
+    uint32_t* d_argmax = (uint32_t*)(base + L.argmax);
+    int* status = (int*)(base + L.status);
+    cudaStream_t s = ctx_->stream;
+    const int H = c.hidden, D = c.head_dim, QH = c.qheads, KVH = c.kvheads, I = c.intermediate, V = c.vocab;
+    const int qkvw = (QH + 2 * KVH) * D;
+    const int M = (int)rows;
+
+    // host-side tables: RoPE for positions < T (as the decode engines build it),
+    // and the scored rows (first .. first + count - 1 of each case)
+    const int half = D / 2;
+    std::vector<float2> table((size_t)T * half);
+    for (size_t p = 0; p < T; ++p)
+        for (int i = 0; i < half; ++i) {
+            const double angle = (double)p * std::pow(c.theta, -2.0 * i / (double)c.rotary);
+            table[p * half + i] = make_float2((float)std::cos(angle), (float)std::sin(angle));
+        }
+    std::vector<int> scored_rows(scored);
+    for (size_t b = 0; b < cases; ++b)
+        for (size_t k = 0; k < count; ++k) scored_rows[b * count + k] = (int)(b * T + first + k);
+    LSX_CUDA(cudaMemcpyAsync(rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice, s),
+             "rope upload");
+    LSX_CUDA(cudaMemcpyAsync(d_rows, scored_rows.data(), scored * 4, cudaMemcpyHostToDevice, s), "row upload");
+    LSX_CUDA(cudaMemcpyAsync(d_tokens, tokens, rows * 4, cudaMemcpyHostToDevice, s), "token upload");
+    LSX_CUDA(cudaMemcpyAsync(d_targets, targets, scored * 4, cudaMemcpyHostToDevice, s), "target upload");
+    LSX_CUDA(cudaMemsetAsync(status, 0, 16, s), "status clear");
+    LSX_CUDA(cudaStreamSynchronize(s), "batched scoring upload");  // host tables go out of scope
+
+    embed_rows_kernel<<<M, 256, 0, s>>>(c.embedding, c.embedding_kind, c.embedding_scale, d_tokens, H, x);
+    LSX_CUDA(cudaGetLastError(), "embedding rows");
+    const int warps_per_block = 8;
+    for (const FusedLayer& Ly : layers_) {
+        rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.input_gain, c.eps, hi, lo);
+        LSX_CUDA(cudaGetLastError(), "input norm");
+        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wqkv, qkvw, Ly.bqkv, work, qkvw, false, status));
+        const long long qk_warps = (long long)M * (QH + KVH);
+        const int qk_blocks = (int)((qk_warps + warps_per_block - 1) / warps_per_block);
+        const long long at_warps = (long long)M * QH;
+        const int at_blocks = (int)((at_warps + warps_per_block - 1) / warps_per_block);
+        if (D == 128) {
+            qk_rope_kernel<4><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
+                                                                         Ly.k_gain, c.qk_eps, rope);
+            causal_attention_kernel<4><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, c.scale,
+                                                                                  hi, lo);
+        } else if (D == 64) {
+            qk_rope_kernel<2><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
+                                                                         Ly.k_gain, c.qk_eps, rope);
+            causal_attention_kernel<2><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, c.scale,
+                                                                                  hi, lo);
+        } else {
+            qk_rope_kernel<8><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
+                                                                         Ly.k_gain, c.qk_eps, rope);
+            causal_attention_kernel<8><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, c.scale,
+                                                                                  hi, lo);
+        }
+        LSX_CUDA(cudaGetLastError(), "attention");
+        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));
+        rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.post_gain, c.eps, hi, lo);
+        LSX_CUDA(cudaGetLastError(), "post norm");
+        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wgu, 2 * I, Ly.bgu, work, 2 * I, false, status));
+        const size_t feats = (size_t)M * I;
+        gated_planes_kernel<<<(int)std::min<size_t>((feats + 255) / 256, 148 * 16), 256, 0, s>>>(work, feats, I,
+                                                                                               c.activation, hi, lo);
+        LSX_CUDA(cudaGetLastError(), "gated product");
+        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
+    }
+    rms_planes_kernel<<<(int)scored, 256, 0, s>>>(x, d_rows, H, c.final_gain, c.eps, hi, lo);
+    LSX_CUDA(cudaGetLastError(), "final norm");
+    LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, (int)scored, H, c.head, V, c.head_bias, logits, V, false, status));
+    row_nll_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_targets, d_nll);
+    row_argmax_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_argmax);
+    LSX_CUDA(cudaGetLastError(), "scores");
+    int host_status[2] = {0, 0};
+    if (nll_out) LSX_CUDA(cudaMemcpyAsync(nll_out, d_nll, scored * 8, cudaMemcpyDeviceToHost, s), "nll download");
+    if (argmax_out)
+        LSX_CUDA(cudaMemcpyAsync(argmax_out, d_argmax, scored * 4, cudaMemcpyDeviceToHost, s), "argmax download");
+    if (logits_out)
+        LSX_CUDA(cudaMemcpyAsync(logits_out, logits, scored * (size_t)V * 4, cudaMemcpyDeviceToHost, s),
+                 "logits download");
+    LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
+    LSX_CUDA(cudaStreamSynchronize(s), "batched scoring");
+    if (host_status[0] != 0) return fail(LSX_E_CUDA, "batched scoring: a device wait timed out");
+    if (host_status[1] != 0) return fail(LSX_E_NONFINITE, "check the finiteness of the model outputs");
+    return LSX_OK;
+}
+
+}  // namespace lsx

@@ -1,0 +1,38 @@
+// Batched teacher-forced forward (batched.cu): equal-length cases through the
+// decoder together, with tensor-core GEMMs per layer.
+#pragma once
+
+#include <string>
+#include <vector>
+
+#include "decode.cuh"
+#include "lsx_internal.h"
+
+namespace lsx {
+
+class BatchedScorer {
+public:
+    ~BatchedScorer();
+    static bool eligible(const FusedConfig& c, std::string* why);
+    int build(lsx_ctx* ctx, const FusedConfig& config, const std::vector<FusedLayer>& layers);
+    // tokens [cases, T] (host): each case's fed tokens.  Scores rows first ..
+    // first + count - 1 of every case against targets [cases, count] (host):
+    // nll_out / argmax_out [cases, count], logits_out [cases, count, vocab]
+    // (host, each may be NULL).
+    int score(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count, const uint32_t* targets,
+              double* nll_out, uint32_t* argmax_out, float* logits_out);
+
+private:
+    struct Layout {
+        size_t x, work, planes, logits, rope, tokens, targets, rows, nll, argmax, status, total;
+    };
+    int reserve(size_t rows, size_t scored, size_t T);
+    lsx_ctx* ctx_ = nullptr;
+    FusedConfig config_{};
+    std::vector<FusedLayer> layers_;
+    void* block_ = nullptr;
+    size_t capacity_ = 0;
+    Layout layout_{};
+};
+
+}  // namespace lsx

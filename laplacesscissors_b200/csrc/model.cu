@@ -22,6 +22,7 @@
 #include <string>
 #include <vector>
 
+#include "batched.cuh"
 #include "decode.cuh"
 #include "persistent.cuh"
 #include "device_common.cuh"
@@ -574,6 +575,9 @@ struct lsx_model {
     bool fused = false;
     std::unique_ptr<FusedDecoder> decoder;
     std::unique_ptr<PersistentDecoder> persistent;  // preferred fused engine when it fits
+    std::unique_ptr<BatchedScorer> batched;          // batched teacher forcing (built on first use)
+    FusedConfig fused_config{};
+    std::vector<FusedLayer> fused_layers;
     unsigned int epoch = 0;                           // tagged-buffer epoch of the persistent engine
     // Per-op plan work buffers.
     std::vector<lsx_tensor*> work;
@@ -598,6 +602,7 @@ lsx_model::~lsx_model() {
     }
     decoder.reset();
     persistent.reset();
+    batched.reset();
     for (auto& kv : bank) lsx_tensor_free(kv.second);
     for (auto* t : owned) lsx_tensor_free(t);
     for (auto* t : work) lsx_tensor_free(t);
@@ -1136,6 +1141,8 @@ int lsx_model_load(lsx_ctx* ctx, const char* root, size_t capacity, lsx_model** 
             c.head = (const __nv_bfloat16*)m->head.weight->data;
             c.head_bias = m->head.bias ? (const float*)m->head.bias->data : nullptr;
             c.final_gain = (const float*)m->final_norm.gain->data;
+            m->fused_config = c;
+            m->fused_layers = layers;
             std::string why;
             const char* engine = getenv("LSX_DECODE_ENGINE");  // "graph" selects the PDL kernel chain
             const bool want_persistent = !(engine && std::string(engine) == "graph");
@@ -1475,6 +1482,34 @@ int lsx_model_score(lsx_model* m, const uint32_t* prompt, size_t prompt_length, 
         LSX_TRY(step_ops(m, rotation, hid.data(), logits.data(), &next));
     }
     return LSX_OK;
+}
+
+// Teacher-forced scoring of many equal-length cases at once (the per-case loop of
+// src/scaling.rs:181-216 batched over cases): every case's prompt and targets but
+// the last go through the decoder together, one tensor-core GEMM per projection.
+int lsx_model_score_batch(lsx_model* m, const uint32_t* prompts, size_t cases, size_t prompt_length,
+                          const uint32_t* targets, size_t count, double* nll_out, uint32_t* argmax_out,
+                          float* logits_out) {
+    LSX_ENSURE(m && prompts && targets, "invalid argument");
+    LSX_ENSURE(cases > 0 && prompt_length > 0 && count > 0, "give at least one case, prompt token and target");
+    LSX_ENSURE(prompt_length + count - 1 <= m->capacity, "give a context that fits the prompt and the continuation");
+    for (size_t i = 0; i < cases * prompt_length; ++i) LSX_ENSURE(prompts[i] < m->graph.vocab, "check the token range");
+    for (size_t i = 0; i < cases * count; ++i) LSX_ENSURE(targets[i] < m->graph.vocab, "check the target range");
+    if (!m->fused) return fail(LSX_E_UNSUPPORTED, "batched scoring needs the fused weight layout");
+    cudaSetDevice(m->ctx->device);
+    if (!m->batched) {
+        std::unique_ptr<BatchedScorer> b(new BatchedScorer);
+        LSX_TRY(b->build(m->ctx, m->fused_config, m->fused_layers));
+        m->batched = std::move(b);
+    }
+    const size_t T = prompt_length + count - 1;
+    std::vector<uint32_t> fed(cases * T);
+    for (size_t c = 0; c < cases; ++c) {
+        memcpy(fed.data() + c * T, prompts + c * prompt_length, prompt_length * 4);
+        if (count > 1) memcpy(fed.data() + c * T + prompt_length, targets + c * count, (count - 1) * 4);
+    }
+    return m->batched->score(fed.data(), cases, T, prompt_length - 1, count, targets, nll_out, argmax_out,
+                             logits_out);
 }
 
 }  // extern "C"

@@ -60,9 +60,12 @@ struct ReadoutParams {
     // ranks [image_k0, image_k0 + M / 2) of `image_rank` as [F_hi | F_hi | F_lo]
     __nv_bfloat16* image;
     int image_stride, image_rank, image_k0;
+    // store mode: out[M, ldo] (=|+=) A B^T + bias, columns [0, V)
+    float* out;
+    int ldo, accumulate;
 };
 
-enum { kModeMargin = 0, kModeImage = 1 };
+enum { kModeMargin = 0, kModeImage = 1, kModeStore = 2 };
 
 // ---------------------------------------------------------------- PTX ------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -217,6 +220,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // MODE kModeMargin: the margin epilogue above.  MODE kModeImage: A holds the
 // edit basis as interleaved (hi, lo) bf16 rows and the epilogue writes the edit
 // image F = W U^T (each rank's two TMEM lanes summed) into the B extension.
+// MODE kModeStore: a plain GEMM, out = A B^T (+ bias), or out += ... with
+// `accumulate` (a residual add: each output element belongs to one tile).
 template <int PLANES, int STAGES, int MODE>
 __global__ void __launch_bounds__(kReadoutThreads, 1)
     readout_margin_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
@@ -412,6 +417,58 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                             dst[k] = hi;
                             dst[p.image_rank + k] = hi;
                             dst[2 * p.image_rank + k] = lo;
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&tmem_empty[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                continue;
+            }
+            if (MODE == kModeStore) {
+                const int row = m0 + row_local;
+                const bool live = row < p.M;
+                float* orow = p.out + (size_t)(live ? row : 0) * p.ldo;
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
+#pragma unroll 1
+                for (int c = 0; c < RN / 32; ++c) {
+                    uint32_t r[32];
+                    tc_ld32(taddr + (uint32_t)(c * 32), r);
+                    tc_wait_ld();
+                    const int nb = n0 + c * 32;
+                    if (live && nb < p.V) {
+                        if (nb + 32 <= p.V && (p.ldo & 3) == 0) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                float4 v = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                                                       __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+                                if (p.bias) {
+                                    v.x += p.bias[nb + i];
+                                    v.y += p.bias[nb + i + 1];
+                                    v.z += p.bias[nb + i + 2];
+                                    v.w += p.bias[nb + i + 3];
+                                }
+                                float4* dst = reinterpret_cast<float4*>(orow + nb + i);
+                                if (p.accumulate) {
+                                    const float4 o = *dst;
+                                    v.x = o.x + v.x;
+                                    v.y = o.y + v.y;
+                                    v.z = o.z + v.z;
+                                    v.w = o.w + v.w;
+                                }
+                                nonfinite |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                                *dst = v;
+                            }
+                        } else {
+                            for (int i = 0; i < 32 && nb + i < p.V; ++i) {
+                                float v = __uint_as_float(r[i]) + (p.bias ? p.bias[nb + i] : 0.f);
+                                if (p.accumulate) v = orow[nb + i] + v;
+                                nonfinite |= !isfinite(v);
+                                orow[nb + i] = v;
+                            }
                         }
                     }
                 }
@@ -929,6 +986,40 @@ cudaError_t launch_pair(lsx_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& 
 }
 
 }  // namespace
+
+// out[M, ldo] (=|+=) (A_hi + A_lo) W^T (+ bias) on the tensor cores: A as two bf16
+// planes [M, K] (an f32 operand split hi/lo), W bf16 [N, K]; f32 accumulate.
+// status[0] receives a device error code, status[1] the non-finite flag.
+int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int M, int K,
+                        const __nv_bfloat16* w, int N, const float* bias, float* out, int ldo, bool accumulate,
+                        int* status) {
+    LSX_ENSURE(M > 0 && N > 0 && K > 0 && K % 8 == 0 && ldo >= N, "check the GEMM dimensions");
+    CUtensorMap ma, ma2, mb;
+    LSX_TRY(make_map(&ma, a_hi, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, RM));
+    LSX_TRY(make_map(&ma2, a_lo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, RM));
+    LSX_TRY(make_map(&mb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, RN));
+    ReadoutParams p{};
+    p.M = M;
+    p.V = N;
+    p.H = K;
+    p.k_blocks = (K + RK - 1) / RK;
+    p.ext_blocks = 0;
+    p.m_tiles = (M + RM - 1) / RM;
+    p.n_tiles = (N + RN - 1) / RN;
+    p.bias = bias;
+    p.status = status;
+    p.out = out;
+    p.ldo = ldo;
+    p.accumulate = accumulate ? 1 : 0;
+    auto k = readout_margin_kernel<2, 3, kModeStore>;
+    const size_t smem = readout_smem<2, 3>();
+    LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+             "GEMM smem attribute");
+    const int total = p.m_tiles * p.n_tiles;
+    k<<<std::min(total, ctx->sm_count), kReadoutThreads, smem, ctx->stream>>>(ma, ma2, mb, ma, mb, p);
+    LSX_CUDA(cudaGetLastError(), "GEMM launch");
+    return LSX_OK;
+}
 
 // Workspace bytes readout_margin_enqueue needs for exactly this hidden dtype.
 size_t readout_workspace_need(size_t vocab, size_t width, size_t rows, size_t rank, bool f32_hidden) {

@@ -47,11 +47,11 @@ def oracle_scores(oracle, root, prompt, targets, edit=None, capacity=64):
     return np.array(nll), np.array(amax, dtype=np.uint32)
 
 
-def check_argmax(got, want, oracle, root, prompt, targets):
+def check_argmax(got, want, oracle, root, prompt, targets, capacity=64):
     """Equal, except where the oracle's own top two are within 1e-3."""
     if np.array_equal(got, want):
         return
-    ref = oracle.OracleModel(root, 64)
+    ref = oracle.OracleModel(root, capacity)
     frame = None
     for t in prompt:
         frame = ref.advance(int(t))
@@ -135,3 +135,63 @@ def test_qwen3_0_6b_case_scores(gpu, oracle):
     ref_nll, ref_amax = oracle_scores(oracle, d, prompt, targets)
     assert np.all(np.abs(nll - ref_nll) <= 2e-2), (nll, ref_nll)
     check_argmax(amax, ref_amax, oracle, d, prompt, targets)
+
+
+# ---- batched teacher forcing (lsx_model_score_batch) ----------------------------
+
+def batch_cases(seed, cases, P, n, vocab):
+    prompts = np.stack([synth.uniform_u32(seed, 100 + c, P, vocab) for c in range(cases)])
+    targets = np.stack([synth.uniform_u32(seed, 900 + c, n, vocab) for c in range(cases)])
+    return prompts, targets
+
+
+def test_batched_scores_match_oracle_tiny(gpu, oracle):
+    """Every case of the batch against the oracle's token-by-token scoring: losses
+    within 1e-3 (the f32 activations enter the GEMMs as two bf16 terms), argmax
+    equal except at oracle near-ties."""
+    root = GOLDEN / "tiny_qwen3"
+    model = load(gpu, root, 32)
+    prompts, targets = batch_cases(3, 5, 7, 4, 512)
+    nll, amax, lg = model.score_batch(prompts, targets, logits=True)
+    for c in range(len(prompts)):
+        ref_nll, ref_amax = oracle_scores(oracle, root, prompts[c], targets[c])
+        assert np.all(np.abs(nll[c] - ref_nll) <= 1e-3 * (1 + np.abs(ref_nll))), (c, nll[c], ref_nll)
+        check_argmax(amax[c], ref_amax, oracle, root, prompts[c], targets[c])
+        # the logits are the frames of the sequential path
+        _, _, frames = model.score(prompts[c], targets[c], frames=True)
+        for k in range(targets.shape[1]):
+            np.testing.assert_allclose(lg[c, k], frames[k].logits, rtol=2e-3, atol=2e-3)
+
+
+def test_batched_single_case_single_target_and_checks(gpu, oracle):
+    root = GOLDEN / "tiny_qwen3"
+    model = load(gpu, root, 8)
+    nll, amax, _ = model.score_batch([[4]], [[9]])
+    ref_nll, ref_amax = oracle_scores(oracle, root, [4], [9])
+    assert abs(nll[0, 0] - ref_nll[0]) <= 1e-3 * (1 + abs(ref_nll[0]))
+    model.reset()
+    before = model.position()
+    model.score_batch([[1, 2, 3]], [[4, 5]])
+    assert model.position() == before  # the decode state is untouched
+    with pytest.raises(lsx.LsxError):
+        model.score_batch([[1] * 6], [[2] * 4])  # 6 + 4 - 1 > capacity 8
+    with pytest.raises(lsx.LsxError):
+        model.score_batch([[1]], [[model.vocab_size()]])
+
+
+@pytest.mark.parametrize("shape,vocab", [("QWEN3_0_6B", 151936), ("QWEN3_8B", 8192)])
+def test_batched_scores_wide_shapes(gpu, oracle, shape, vocab):
+    """Qwen3-0.6B and Qwen3-8B widths (2 layers): several cases of a 64-token prompt
+    and 9 targets, against the sequential path on every case (losses within 2e-2,
+    the decode tolerance) and the oracle on the first."""
+    d = Path(tempfile.mkdtemp(prefix=f"lsx-batch-{shape.lower()}-"))
+    synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(getattr(synth, shape), layers=2, vocab=vocab)), seed=6)
+    model = lsx.Model.load(d, gpu, 80)
+    prompts, targets = batch_cases(6, 3, 64, 9, vocab)
+    nll, amax, _ = model.score_batch(prompts, targets)
+    for c in range(len(prompts)):
+        seq_nll, seq_amax, _ = model.score(prompts[c], targets[c])
+        assert np.all(np.abs(nll[c] - seq_nll) <= 2e-2), (c, nll[c], seq_nll)
+    ref_nll, ref_amax = oracle_scores(oracle, d, prompts[0], targets[0], capacity=80)
+    assert np.all(np.abs(nll[0] - ref_nll) <= 2e-2), (nll[0], ref_nll)
+    check_argmax(amax[0], ref_amax, oracle, d, prompts[0], targets[0], capacity=80)
