@@ -217,6 +217,65 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     return true;
 }
 
+// Store epilogue of one accumulator tile: this thread's row of out (=|+=) the
+// tile's 256 columns (+ bias), 32 columns per TMEM load.  With `accumulate` the
+// row's current values for the next 32 columns are loaded while the present ones
+// are summed, so each chunk costs one memory round trip at most.
+__device__ __forceinline__ void store_tile(uint32_t taddr, int row, bool live, int n0, const ReadoutParams& p,
+                                           bool& nonfinite) {
+    float* orow = p.out + (size_t)(live ? row : 0) * p.ldo;
+    const bool vec = (p.ldo & 3) == 0;
+    float4 cur[8], nxt[8];
+    auto fetch = [&](int c, float4 (&dst)[8]) {
+        const int nb = n0 + c * 32;
+        if (p.accumulate && live && vec && nb + 32 <= p.V) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = __ldcg(reinterpret_cast<const float4*>(orow + nb) + i);
+        }
+    };
+    fetch(0, cur);
+#pragma unroll 1
+    for (int c = 0; c < RN / 32; ++c) {
+        uint32_t r[32];
+        tc_ld32(taddr + (uint32_t)(c * 32), r);
+        if (c + 1 < RN / 32) fetch(c + 1, nxt);
+        tc_wait_ld();
+        const int nb = n0 + c * 32;
+        if (live && nb < p.V) {
+            if (nb + 32 <= p.V && vec) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float4 v = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                           __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    if (p.bias) {
+                        v.x += p.bias[nb + 4 * i];
+                        v.y += p.bias[nb + 4 * i + 1];
+                        v.z += p.bias[nb + 4 * i + 2];
+                        v.w += p.bias[nb + 4 * i + 3];
+                    }
+                    if (p.accumulate) {
+                        v.x = cur[i].x + v.x;
+                        v.y = cur[i].y + v.y;
+                        v.z = cur[i].z + v.z;
+                        v.w = cur[i].w + v.w;
+                    }
+                    nonfinite |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+                    reinterpret_cast<float4*>(orow + nb)[i] = v;
+                }
+            } else {
+                for (int i = 0; i < 32 && nb + i < p.V; ++i) {
+                    float v = __uint_as_float(r[i]) + (p.bias ? p.bias[nb + i] : 0.f);
+                    if (p.accumulate) v = orow[nb + i] + v;
+                    nonfinite |= !isfinite(v);
+                    orow[nb + i] = v;
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+    }
+}
+
 // MODE kModeMargin: the margin epilogue above.  MODE kModeImage: A holds the
 // edit basis as interleaved (hi, lo) bf16 rows and the epilogue writes the edit
 // image F = W U^T (each rank's two TMEM lanes summed) into the B extension.
@@ -430,48 +489,8 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             }
             if (MODE == kModeStore) {
                 const int row = m0 + row_local;
-                const bool live = row < p.M;
-                float* orow = p.out + (size_t)(live ? row : 0) * p.ldo;
-                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
-#pragma unroll 1
-                for (int c = 0; c < RN / 32; ++c) {
-                    uint32_t r[32];
-                    tc_ld32(taddr + (uint32_t)(c * 32), r);
-                    tc_wait_ld();
-                    const int nb = n0 + c * 32;
-                    if (live && nb < p.V) {
-                        if (nb + 32 <= p.V && (p.ldo & 3) == 0) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 4) {
-                                float4 v = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
-                                                       __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-                                if (p.bias) {
-                                    v.x += p.bias[nb + i];
-                                    v.y += p.bias[nb + i + 1];
-                                    v.z += p.bias[nb + i + 2];
-                                    v.w += p.bias[nb + i + 3];
-                                }
-                                float4* dst = reinterpret_cast<float4*>(orow + nb + i);
-                                if (p.accumulate) {
-                                    const float4 o = *dst;
-                                    v.x = o.x + v.x;
-                                    v.y = o.y + v.y;
-                                    v.z = o.z + v.z;
-                                    v.w = o.w + v.w;
-                                }
-                                nonfinite |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
-                                *dst = v;
-                            }
-                        } else {
-                            for (int i = 0; i < 32 && nb + i < p.V; ++i) {
-                                float v = __uint_as_float(r[i]) + (p.bias ? p.bias[nb + i] : 0.f);
-                                if (p.accumulate) v = orow[nb + i] + v;
-                                nonfinite |= !isfinite(v);
-                                orow[nb + i] = v;
-                            }
-                        }
-                    }
-                }
+                store_tile(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN), row, row < p.M, n0, p,
+                           nonfinite);
                 tc_fence_before();
                 mbar_arrive(&tmem_empty[acc]);
                 if (++acc == 2) {
@@ -583,7 +602,7 @@ __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
         : "memory");
 }
 
-template <int PLANES, int STAGES>
+template <int PLANES, int STAGES, int MODE = kModeMargin>
 __global__ void __launch_bounds__(kReadoutThreads, 1)
     readout_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
                         const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_ea,
@@ -747,8 +766,19 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             tc_fence_after();
             const int row = m0 + row_local;
             const bool live = row < p.M;
-            const int tcol = live ? (int)p.targets[row] - n0 : -1;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
+            if (MODE == kModeStore) {
+                store_tile(taddr, row, live, n0, p, nonfinite);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(tmem_empty0 + (uint32_t)(acc * 8));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                continue;
+            }
+            const int tcol = live ? (int)p.targets[row] - n0 : -1;
             RowScan scan;
             scan_tile(taddr, tcol, n0, p, scan);
             nonfinite |= scan.probe != 0.f;  // NaN (non-finite logit) or never 0 otherwise
@@ -960,10 +990,10 @@ size_t pair_smem() {
 }
 
 // Launches the CTA-pair margin kernel as clusters of 2.
-template <int PLANES, int STAGES>
+template <int PLANES, int STAGES, int MODE = kModeMargin>
 cudaError_t launch_pair(lsx_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& ma2, const CUtensorMap& mb,
                         const CUtensorMap& mea, const CUtensorMap& meb, const ReadoutParams& p) {
-    auto k = readout_pair_kernel<PLANES, STAGES>;
+    auto k = readout_pair_kernel<PLANES, STAGES, MODE>;
     const size_t smem = pair_smem<PLANES, STAGES>();
     cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1011,6 +1041,14 @@ int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bflo
     p.out = out;
     p.ldo = ldo;
     p.accumulate = accumulate ? 1 : 0;
+    const char* single = getenv("LSX_GEMM_SINGLE");
+    if (!(single && single[0] == '1') && ctx->sm_count >= 2) {
+        // CTA pairs (cta_group::2): each CTA loads half of the weight tile
+        CUtensorMap mbh;
+        LSX_TRY(make_map(&mbh, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, kHalfN));
+        LSX_CUDA((launch_pair<2, 4, kModeStore>(ctx, ma, ma2, mbh, ma, mbh, p)), "GEMM launch");
+        return LSX_OK;
+    }
     auto k = readout_margin_kernel<2, 3, kModeStore>;
     const size_t smem = readout_smem<2, 3>();
     LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
