@@ -597,7 +597,10 @@ def long_decode(args, local):
                      "frac": achieved / peaks["hbm_gbs"],
                      "scope": f"{step_bytes / 1e9:.3f} GB per step (weights + f32 KV at the mean context)"},
         "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s,
-                    "note": "token by token in one persistent launch (as the reference prefills), wall clock"},
+                    "tflops": decoder_flops_per_token(cfg) * (P - 1) / prefill_s / 1e12,
+                    "note": "lsx_model_generate wall clock: the first P - 1 tokens in one batched forward "
+                            "(tcgen05 GEMMs, causal attention, KV cache filled), the last through the decode "
+                            "engine; LSX_PREFILL_MIN=0 feeds the prompt token by token as the reference"},
         "clocks": clocks.summary(),
     }))
 

@@ -222,6 +222,18 @@ __global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, 
     }
 }
 
+// Appends every row's k (after QK-norm and RoPE) and v to the f32 KV cache at
+// position = row (kernels/ops.py:69-73 for a whole prompt).
+__global__ void kv_store_kernel(const float* __restrict__ qkv, size_t total, int QH, int KVH, int D,
+                                float* __restrict__ keys, float* __restrict__ values) {
+    const size_t kw = (size_t)KVH * D, stride = (size_t)(QH + 2 * KVH) * D;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t m = i / kw, e = i % kw;
+        keys[i] = qkv[m * stride + (size_t)QH * D + e];
+        values[i] = qkv[m * stride + (size_t)(QH + KVH) * D + e];
+    }
+}
+
 // First argmax of each logit row (src/diagnosis.rs:58-70) as a packed key max.
 __global__ void __launch_bounds__(1024) row_argmax_kernel(const float* __restrict__ logits, int V,
                                                           uint32_t* __restrict__ argmax) {
@@ -345,10 +357,21 @@ int BatchedScorer::build(lsx_ctx* ctx, const FusedConfig& config, const std::vec
     return LSX_OK;
 }
 
+int BatchedScorer::prefill(const uint32_t* tokens, size_t n) {
+    LSX_ENSURE(n > 0 && n <= (size_t)config_.capacity, "check the prefill length");
+    return run(tokens, 1, n, 0, 0, nullptr, nullptr, nullptr, nullptr, true);
+}
+
 int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count,
                          const uint32_t* targets, double* nll_out, uint32_t* argmax_out, float* logits_out) {
+    LSX_ENSURE(cases > 0 && T > 0 && count > 0 && first + count <= T && targets, "check the case shape");
+    return run(tokens, cases, T, first, count, targets, nll_out, argmax_out, logits_out, false);
+}
+
+int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count,
+                       const uint32_t* targets, double* nll_out, uint32_t* argmax_out, float* logits_out,
+                       bool write_cache) {
     const FusedConfig& c = config_;
-    LSX_ENSURE(cases > 0 && T > 0 && count > 0 && first + count <= T, "check the case shape");
     const size_t rows = cases * T, scored = cases * count;
     LSX_ENSURE(rows <= 2147483647ull / 4 && scored * (size_t)c.vocab <= (size_t)1 << 40, "too many rows");
     LSX_TRY(reserve(rows, scored, T));
@@ -386,9 +409,11 @@ int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t 
         for (size_t k = 0; k < count; ++k) scored_rows[b * count + k] = (int)(b * T + first + k);
     LSX_CUDA(cudaMemcpyAsync(rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice, s),
              "rope upload");
-    LSX_CUDA(cudaMemcpyAsync(d_rows, scored_rows.data(), scored * 4, cudaMemcpyHostToDevice, s), "row upload");
+    if (scored) {
+        LSX_CUDA(cudaMemcpyAsync(d_rows, scored_rows.data(), scored * 4, cudaMemcpyHostToDevice, s), "row upload");
+        LSX_CUDA(cudaMemcpyAsync(d_targets, targets, scored * 4, cudaMemcpyHostToDevice, s), "target upload");
+    }
     LSX_CUDA(cudaMemcpyAsync(d_tokens, tokens, rows * 4, cudaMemcpyHostToDevice, s), "token upload");
-    LSX_CUDA(cudaMemcpyAsync(d_targets, targets, scored * 4, cudaMemcpyHostToDevice, s), "target upload");
     LSX_CUDA(cudaMemsetAsync(status, 0, 16, s), "status clear");
     LSX_CUDA(cudaStreamSynchronize(s), "batched scoring upload");  // host tables go out of scope
 
@@ -420,6 +445,12 @@ int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t 
                                                                                   hi, lo);
         }
         LSX_CUDA(cudaGetLastError(), "attention");
+        if (write_cache) {
+            const size_t kv = (size_t)M * KVH * D;
+            kv_store_kernel<<<(int)std::min<size_t>((kv + 255) / 256, 148 * 16), 256, 0, s>>>(work, kv, QH, KVH, D,
+                                                                                             Ly.keys, Ly.values);
+            LSX_CUDA(cudaGetLastError(), "KV append");
+        }
         LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));
         rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.post_gain, c.eps, hi, lo);
         LSX_CUDA(cudaGetLastError(), "post norm");
@@ -430,13 +461,20 @@ int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t 
         LSX_CUDA(cudaGetLastError(), "gated product");
         LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
     }
+    int host_status[2] = {0, 0};
+    if (scored == 0) {  // prefill: the KV cache is the result
+        LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
+        LSX_CUDA(cudaStreamSynchronize(s), "batched prefill");
+        if (host_status[0] != 0) return fail(LSX_E_CUDA, "batched prefill: a device wait timed out");
+        if (host_status[1] != 0) return fail(LSX_E_NONFINITE, "check the finiteness of the model outputs");
+        return LSX_OK;
+    }
     rms_planes_kernel<<<(int)scored, 256, 0, s>>>(x, d_rows, H, c.final_gain, c.eps, hi, lo);
     LSX_CUDA(cudaGetLastError(), "final norm");
     LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, (int)scored, H, c.head, V, c.head_bias, logits, V, false, status));
     row_nll_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_targets, d_nll);
     row_argmax_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_argmax);
     LSX_CUDA(cudaGetLastError(), "scores");
-    int host_status[2] = {0, 0};
     if (nll_out) LSX_CUDA(cudaMemcpyAsync(nll_out, d_nll, scored * 8, cudaMemcpyDeviceToHost, s), "nll download");
     if (argmax_out)
         LSX_CUDA(cudaMemcpyAsync(argmax_out, d_argmax, scored * 4, cudaMemcpyDeviceToHost, s), "argmax download");

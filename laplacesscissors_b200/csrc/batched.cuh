@@ -21,12 +21,17 @@ public:
     // (host, each may be NULL).
     int score(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count, const uint32_t* targets,
               double* nll_out, uint32_t* argmax_out, float* logits_out);
+    // The first n tokens of a generation (host) through the decoder at once: fills
+    // positions 0 .. n-1 of the layers' KV caches as n decode steps would.
+    int prefill(const uint32_t* tokens, size_t n);
 
 private:
     struct Layout {
         size_t x, work, planes, logits, rope, tokens, targets, rows, nll, argmax, status, total;
     };
     int reserve(size_t rows, size_t scored, size_t T);
+    int run(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count, const uint32_t* targets,
+            double* nll_out, uint32_t* argmax_out, float* logits_out, bool write_cache);
     lsx_ctx* ctx_ = nullptr;
     FusedConfig config_{};
     std::vector<FusedLayer> layers_;

@@ -982,6 +982,22 @@ void base_state(lsx_model* m, const lsx_rotation* rotation) {
     fill_rotation(st, rotation);
 }
 
+int ensure_batched(lsx_model* m) {
+    if (!m->batched) {
+        std::unique_ptr<BatchedScorer> b(new BatchedScorer);
+        LSX_TRY(b->build(m->ctx, m->fused_config, m->fused_layers));
+        m->batched = std::move(b);
+    }
+    return LSX_OK;
+}
+
+// Prompts at least this long (less the last token) are prefilled in one batched
+// forward; LSX_PREFILL_MIN overrides, 0 feeds every prompt token by token.
+size_t batched_prefill_min() {
+    const char* v = getenv("LSX_PREFILL_MIN");
+    return v ? (size_t)std::max(0, atoi(v)) : 64;
+}
+
 int check_rotation(lsx_model* m, const lsx_rotation* rotation) {
     if (rotation) {
         LSX_ENSURE(rotation->ctx == m->ctx, "the rotation belongs to another context");
@@ -1345,10 +1361,21 @@ int lsx_model_generate(lsx_model* m, const uint32_t* prompt, size_t prompt_lengt
     const bool want_frames = hidden_frames || logits_frames;
     if (m->fused) {
         if (want_frames) LSX_TRY(ensure_frames(m, maximum));
-        LSX_K(cudaMemcpyAsync(m->d_prompt, prompt, prompt_length * 4, cudaMemcpyHostToDevice, s), "prompt upload");
+        // A long prompt: all but its last token in one batched forward that fills
+        // the KV cache, then the decode engine continues from the last token.
+        size_t skip = 0;
+        const size_t min_batch = batched_prefill_min();
+        if (min_batch > 0 && prompt_length - 1 >= min_batch && BatchedScorer::eligible(m->fused_config, nullptr)) {
+            LSX_TRY(ensure_batched(m));
+            LSX_TRY(m->batched->prefill(prompt, prompt_length - 1));
+            skip = prompt_length - 1;
+            m->cursor = skip;
+        }
+        LSX_K(cudaMemcpyAsync(m->d_prompt, prompt + skip, (prompt_length - skip) * 4, cudaMemcpyHostToDevice, s),
+              "prompt upload");
         base_state(m, rotation);
         DecodeState* st = m->host_state;
-        st->prompt_length = (int)prompt_length;
+        st->prompt_length = (int)(prompt_length - skip);
         st->maximum = (int)maximum;
         st->n_stop = (int)stop_count;
         for (size_t i = 0; i < stop_count; ++i) st->stop[i] = stop_tokens[i];
@@ -1357,7 +1384,7 @@ int lsx_model_generate(lsx_model* m, const uint32_t* prompt, size_t prompt_lengt
             st->hidden_frames = m->d_frames;
             st->logits_frames = m->d_frames + maximum * H;
         }
-        LSX_TRY(run_fused(m, (int)(prompt_length + maximum - 1)));
+        LSX_TRY(run_fused(m, (int)(prompt_length - skip + maximum - 1)));
         size_t n = (size_t)m->host_state->generated;
         LSX_K(cudaMemcpyAsync(tokens_out, m->d_tokens, n * 4, cudaMemcpyDeviceToHost, s), "token download");
         if (hidden_frames)
@@ -1497,11 +1524,7 @@ int lsx_model_score_batch(lsx_model* m, const uint32_t* prompts, size_t cases, s
     for (size_t i = 0; i < cases * count; ++i) LSX_ENSURE(targets[i] < m->graph.vocab, "check the target range");
     if (!m->fused) return fail(LSX_E_UNSUPPORTED, "batched scoring needs the fused weight layout");
     cudaSetDevice(m->ctx->device);
-    if (!m->batched) {
-        std::unique_ptr<BatchedScorer> b(new BatchedScorer);
-        LSX_TRY(b->build(m->ctx, m->fused_config, m->fused_layers));
-        m->batched = std::move(b);
-    }
+    LSX_TRY(ensure_batched(m));
     const size_t T = prompt_length + count - 1;
     std::vector<uint32_t> fed(cases * T);
     for (size_t c = 0; c < cases; ++c) {

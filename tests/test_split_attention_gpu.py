@@ -111,3 +111,29 @@ def test_wide_split_matches_oracle(gpu, oracle, shape, ratio):
     prompt = synth.prompt_tokens(11, 160, 8192)
     tokens, _, frames = model.generate(prompt, 8, frames=True)
     check_against_oracle(oracle, d, 192, prompt, tokens, frames, 8)
+
+
+def test_batched_prefill_matches_token_by_token(gpu, oracle):
+    """A prompt of 200 tokens is prefilled in one batched forward (tensor-core
+    GEMMs filling the KV cache) before the decode engine continues; the generation
+    matches the token-by-token prefill (LSX_PREFILL_MIN=0) and the oracle."""
+    root = small_long_checkpoint()
+    prompt = synth.prompt_tokens(8, 200, 512)
+    saved = os.environ.get("LSX_PREFILL_MIN")
+    try:
+        os.environ["LSX_PREFILL_MIN"] = "0"
+        slow = load(gpu, root, 256, 128)
+        ts, _, fs = slow.generate(prompt, 10, frames=True)
+        os.environ["LSX_PREFILL_MIN"] = "64"
+        fast = load(gpu, root, 256, 128)
+        tf, _, ff = fast.generate(prompt, 10, frames=True)
+    finally:
+        if saved is None:
+            os.environ.pop("LSX_PREFILL_MIN", None)
+        else:
+            os.environ["LSX_PREFILL_MIN"] = saved
+    assert fast.position() == slow.position() == 200 + 9
+    check_against_oracle(oracle, root, 256, prompt, tf, ff, 10)
+    n = next((i for i, (a, b) in enumerate(zip(ts, tf)) if a != b), len(ts))
+    for i in range(n):
+        assert rel_l2(ff[i].logits, fs[i].logits) < 1e-3
