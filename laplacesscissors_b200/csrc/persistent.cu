@@ -339,22 +339,34 @@ struct EpiCtx {
     int act;
 };
 
-// Partial dot of one 16-byte chunk of bf16 weights with eight f32 values, as two
-// independent FMA chains.
-__device__ __forceinline__ void dot8_split(uint4 w, float4 x0, float4 x1, float& s0, float& s1) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-    const float2 p0 = __bfloat1622float2(h[0]);
-    const float2 p1 = __bfloat1622float2(h[1]);
-    const float2 p2 = __bfloat1622float2(h[2]);
-    const float2 p3 = __bfloat1622float2(h[3]);
-    s0 = fmaf(p0.x, x0.x, s0);
-    s1 = fmaf(p0.y, x0.y, s1);
-    s0 = fmaf(p1.x, x0.z, s0);
-    s1 = fmaf(p1.y, x0.w, s1);
-    s0 = fmaf(p2.x, x1.x, s0);
-    s1 = fmaf(p2.y, x1.y, s1);
-    s0 = fmaf(p3.x, x1.z, s0);
-    s1 = fmaf(p3.y, x1.w, s1);
+// Partial dot of one 16-byte chunk of bf16 weights with eight f32 values, with
+// packed f32x2 FMAs (two multiply-adds per instruction):
+// each 32-bit word of w holds two bf16 weights, widened to an f32 pair by a shift
+// and a mask; s0 accumulates words 0 and 2, s1 words 1 and 3, two lanes each.
+__device__ __forceinline__ unsigned long long pack_f32x2(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long widen_bf16x2(uint32_t u) {
+    unsigned long long r;
+    asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r)
+        : "r"(u));
+    return r;
+}
+__device__ __forceinline__ void fma_f32x2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float sum_f32x2(unsigned long long v) {
+    return __uint_as_float((uint32_t)v) + __uint_as_float((uint32_t)(v >> 32));
+}
+__device__ __forceinline__ void dot8_x2(uint4 w, float4 x0, float4 x1, unsigned long long& s0,
+                                        unsigned long long& s1) {
+    fma_f32x2(s0, widen_bf16x2(w.x), pack_f32x2(x0.x, x0.y));
+    fma_f32x2(s1, widen_bf16x2(w.y), pack_f32x2(x0.z, x0.w));
+    fma_f32x2(s0, widen_bf16x2(w.z), pack_f32x2(x1.x, x1.y));
+    fma_f32x2(s1, widen_bf16x2(w.w), pack_f32x2(x1.z, x1.w));
 }
 
 // Sums CNT per-lane partials across the warp.  Each halving round exchanges half
@@ -506,9 +518,9 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                 }
                 float acc[NR];
                 {
-                    float a0[NR], a1[NR];
+                    unsigned long long a0[NR], a1[NR];
 #pragma unroll
-                    for (int i = 0; i < NR; ++i) a0[i] = a1[i] = 0.f;
+                    for (int i = 0; i < NR; ++i) a0[i] = a1[i] = 0ull;
                     if (KCH > 0) {
 #pragma unroll
                         for (int j = 0; j < KCH; ++j) {
@@ -516,7 +528,7 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
 #pragma unroll
                             for (int i = 0; i < NV; ++i) w[i] = reinterpret_cast<const uint4*>(rp[i])[lane + 32 * j];
 #pragma unroll
-                            for (int i = 0; i < NV; ++i) dot8_split(w[i], x.v[2 * j], x.v[2 * j + 1], a0[i], a1[i]);
+                            for (int i = 0; i < NV; ++i) dot8_x2(w[i], x.v[2 * j], x.v[2 * j + 1], a0[i], a1[i]);
                         }
                     } else {
                         const float4* x4 = reinterpret_cast<const float4*>(xs);
@@ -525,11 +537,11 @@ __device__ __forceinline__ bool run_gemv(const Ring& ring, Cursor& cur, const Op
                             const float4 x1 = perm ? x4[(K >> 3) + cc] : x4[2 * cc + 1];
 #pragma unroll
                             for (int i = 0; i < NV; ++i)
-                                dot8_split(reinterpret_cast<const uint4*>(rp[i])[cc], x0, x1, a0[i], a1[i]);
+                                dot8_x2(reinterpret_cast<const uint4*>(rp[i])[cc], x0, x1, a0[i], a1[i]);
                         }
                     }
 #pragma unroll
-                    for (int i = 0; i < NR; ++i) acc[i] = a0[i] + a1[i];
+                    for (int i = 0; i < NR; ++i) acc[i] = sum_f32x2(a0[i]) + sum_f32x2(a1[i]);
                 }
                 RowReduce<NR, 16>::run(acc, lane);
                 float d = gain ? acc[0] * inverse : acc[0];
