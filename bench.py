@@ -46,7 +46,7 @@ METRIC = "decode tok/s (Qwen3-0.6B bs1, % HBM roofline); readout-margin rows/s"
 # dominant kernel of each leg on this workload, from ncu captures of this script
 # (--profile): persistent_decode_kernel per 55-step generation, and
 # readout_pair_kernel per 4096-row validation.
-DECODE_TRAFFIC_PER_LAUNCH = 65_563_098_000 + 40_558_336
+DECODE_TRAFFIC_PER_LAUNCH = 65_560_912_000 + 31_543_296
 READOUT_TRAFFIC_PER_LAUNCH = 339_733_248 + 4_837_888
 
 
