@@ -407,7 +407,7 @@ def main():
                          "long4b: Qwen3-4B decode after a long prompt; score8b: Qwen3-8B teacher-forced scoring")
     ap.add_argument("--prompt", type=int, default=4096, help="long4b: prompt length")
     ap.add_argument("--cases", type=int, default=64, help="score8b: cases timed (of the 1024-case job)")
-    ap.add_argument("--batch", type=int, default=32, help="score8b: cases per lsx_model_score_batch call "
+    ap.add_argument("--batch", type=int, default=64, help="score8b: cases per lsx_model_score_batch call "
                                                           "(0: one lsx_model_score call per case)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling aid: device legs only, no e2e or CPU legs, warm-up as given")

@@ -205,15 +205,18 @@ int lsx_model_score(lsx_model* model, const uint32_t* prompt, size_t prompt_leng
 
 /* lsx_model_score over `cases` independent cases of equal shape at once (the
    per-case loop of scaling::evaluate, src/scaling.rs:181-216, batched): prompts
-   [cases x prompt_length], targets [cases x count]; nll_out and argmax_out
-   [cases x count], logits_out [cases x count x vocab] (host, each may be NULL).
-   The fed tokens of all cases go through each layer together (tensor-core GEMMs
-   with the f32 activations as two bf16 terms); results agree with lsx_model_score
-   within the decode tolerances.  The model's decode cursor and KV cache are not
-   touched.  No edit: the "after" scores use lsx_model_score with a rotation. */
+   [cases x prompt_length], targets [cases x count].  Per scored position:
+   nll_out (attribution::loss), argmax_out (first argmax), margin_out
+   (minimum_margin of the target, src/diagnosis.rs:490-492), all [cases x count],
+   and logits_out [cases x count x vocab] (host, each may be NULL).  With
+   `rotation` (rank at most 256) the scores come from the edited readout of the
+   unedited hidden states, as lsx_model_score's.  The fed tokens of all cases go
+   through each layer together (tensor-core GEMMs with the f32 activations as two
+   bf16 terms); results agree with lsx_model_score within the decode tolerances.
+   The model's decode cursor and KV cache are not touched. */
 int lsx_model_score_batch(lsx_model* model, const uint32_t* prompts, size_t cases, size_t prompt_length,
-                          const uint32_t* targets, size_t count, double* nll_out, uint32_t* argmax_out,
-                          float* logits_out);
+                          const uint32_t* targets, size_t count, const lsx_rotation* rotation, double* nll_out,
+                          uint32_t* argmax_out, double* margin_out, float* logits_out);
 
 /* ------------------------------------------------------ readout validation -- */
 /* Fused readout margin over many hidden states (verify_cached's target rows,

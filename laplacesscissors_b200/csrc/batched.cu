@@ -85,16 +85,66 @@ __global__ void embed_rows_kernel(const void* __restrict__ emb, int kind, float 
 }
 
 // A planes of RMSNorm(x[rows[r]]) * gain (kernels/ops.py:31-45); rows == nullptr: r.
+// With `out` the normalised rows are written there in f32 instead.
 __global__ void rms_planes_kernel(const float* __restrict__ x, const int* __restrict__ rows, int H,
                                   const float* __restrict__ gain, float eps, __nv_bfloat16* __restrict__ hi,
-                                  __nv_bfloat16* __restrict__ lo) {
+                                  __nv_bfloat16* __restrict__ lo, float* __restrict__ out = nullptr) {
     __shared__ float red[32];
     const size_t r = blockIdx.x;
     const float* xr = x + (size_t)(rows ? rows[r] : (int)r) * H;
     float ss = 0.f;
     for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
     const float inverse = rsqrtf(block_sum(ss, red) / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += blockDim.x) split_store(hi, lo, r * H + i, xr[i] * inverse * gain[i]);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = xr[i] * inverse * gain[i];
+        if (out) out[r * H + i] = v;
+        else split_store(hi, lo, r * H + i, v);
+    }
+}
+
+// The readout edit on each final hidden row, then its A planes: a plane rotation
+// h + u (a hu + b hv) + v (a hv - b hu) (kernels/ops.py:125-135 with
+// ReadoutRotation::coefficients, src/rotation.rs:50-53), or a joint rotation
+// h + basis^T ((R - I) (basis h)) (DeviceRotation::apply, src/model.rs:350-361).
+__global__ void edit_rows_kernel(const float* __restrict__ h, int H, int kind, float a, float b,
+                                 const float* __restrict__ u, const float* __restrict__ v, int rank,
+                                 const float* __restrict__ basis, const float* __restrict__ delta,
+                                 __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    __shared__ float red[32];
+    __shared__ float coords[256], shift[256];
+    const size_t r = blockIdx.x;
+    const float* hr = h + r * H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    if (kind == 1) {
+        float pu = 0.f, pv = 0.f;
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
+            pu = fmaf(hr[i], u[i], pu);
+            pv = fmaf(hr[i], v[i], pv);
+        }
+        const float hu = block_sum(pu, red);
+        const float hv = block_sum(pv, red);
+        for (int i = threadIdx.x; i < H; i += blockDim.x)
+            split_store(hi, lo, r * H + i, hr[i] + u[i] * (a * hu + b * hv) + v[i] * (a * hv - b * hu));
+        return;
+    }
+    for (int k = warp; k < rank; k += warps) {
+        float d = 0.f;
+        for (int j = lane; j < H; j += 32) d = fmaf(basis[(size_t)k * H + j], hr[j], d);
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == 0) coords[k] = d;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rank; i += blockDim.x) {
+        float d = 0.f;
+        for (int j = 0; j < rank; ++j) d = fmaf(delta[i * rank + j], coords[j], d);
+        shift[i] = d;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+        float d = 0.f;
+        for (int k = 0; k < rank; ++k) d = fmaf(basis[(size_t)k * H + j], shift[k], d);
+        split_store(hi, lo, r * H + j, __fadd_rn(hr[j], d));
+    }
 }
 
 // QK-norm and rotate-half RoPE in place on the q and k heads of every row; one
@@ -234,52 +284,56 @@ __global__ void kv_store_kernel(const float* __restrict__ qkv, size_t total, int
     }
 }
 
-// First argmax of each logit row (src/diagnosis.rs:58-70) as a packed key max.
-__global__ void __launch_bounds__(1024) row_argmax_kernel(const float* __restrict__ logits, int V,
-                                                          uint32_t* __restrict__ argmax) {
-    __shared__ unsigned long long red[32];
-    const float* z = logits + (size_t)blockIdx.x * V;
-    unsigned long long best = 0ull;
-    for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        const unsigned long long k = pack_arg(z[j], (uint32_t)j);
-        best = k > best ? k : best;
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
-    }
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
-        best = red[0] > best ? red[0] : best;
-        argmax[blockIdx.x] = 0xffffffffu - (uint32_t)(best & 0xffffffffull);
-    }
-}
-
-// attribution::loss (src/attribution.rs:49-60): logsumexp(z) - z[target] in f64.
-__global__ void __launch_bounds__(1024) row_nll_kernel(const float* __restrict__ logits, int V,
-                                                       const uint32_t* __restrict__ targets, double* __restrict__ nll) {
+// Per logit row: attribution::loss (src/attribution.rs:49-60, f64 logsumexp minus
+// the target's logit), the first argmax (src/diagnosis.rs:58-70) and the target
+// margin f64(z_t) - f64(max over j != t, lowest index on ties) (src/diagnosis.rs:
+// 71-80, 490-492), from packed (value, index) keys.
+__global__ void __launch_bounds__(1024) row_scores_kernel(const float* __restrict__ logits, int V,
+                                                          const uint32_t* __restrict__ targets,
+                                                          double* __restrict__ nll, uint32_t* __restrict__ argmax,
+                                                          double* __restrict__ margin) {
+    __shared__ unsigned long long kbest[32], kother[32];
     __shared__ double red[32];
     const float* z = logits + (size_t)blockIdx.x * V;
+    const uint32_t t = targets[blockIdx.x];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
-    double top = -INFINITY;
-    for (int j = tid; j < V; j += blockDim.x) top = fmax(top, (double)z[j]);
-    for (int o = 16; o > 0; o >>= 1) top = fmax(top, __shfl_xor_sync(0xffffffffu, top, o));
-    if (lane == 0) red[warp] = top;
+    unsigned long long best = 0ull, other = 0ull;
+    for (int j = tid; j < V; j += blockDim.x) {
+        const unsigned long long k = pack_arg(z[j], (uint32_t)j);
+        best = k > best ? k : best;
+        if ((uint32_t)j != t) other = k > other ? k : other;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const unsigned long long o2 = __shfl_xor_sync(0xffffffffu, other, o);
+        best = b2 > best ? b2 : best;
+        other = o2 > other ? o2 : other;
+    }
+    if (lane == 0) {
+        kbest[warp] = best;
+        kother[warp] = other;
+    }
     __syncthreads();
-    top = red[0];
-    for (int w = 1; w < warps; ++w) top = fmax(top, red[w]);
-    __syncthreads();
+    best = kbest[0];
+    other = kother[0];
+    for (int w = 1; w < warps; ++w) {
+        best = kbest[w] > best ? kbest[w] : best;
+        other = kother[w] > other ? kother[w] : other;
+    }
+    const double top = (double)z[0xffffffffu - (uint32_t)(best & 0xffffffffull)];
     double sum = 0.0;
     for (int j = tid; j < V; j += blockDim.x) sum += exp((double)z[j] - top);
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    __syncthreads();
     if (lane == 0) red[warp] = sum;
     __syncthreads();
     if (tid == 0) {
         double total = 0.0;
         for (int w = 0; w < warps; ++w) total += red[w];
-        nll[blockIdx.x] = top + log(total) - (double)z[targets[blockIdx.x]];
+        const double zt = (double)z[t];
+        nll[blockIdx.x] = top + log(total) - zt;
+        argmax[blockIdx.x] = 0xffffffffu - (uint32_t)(best & 0xffffffffull);
+        margin[blockIdx.x] = other ? zt - (double)z[0xffffffffu - (uint32_t)(other & 0xffffffffull)] : INFINITY;
     }
 }
 
@@ -317,7 +371,7 @@ int BatchedScorer::reserve(size_t rows, size_t scored, size_t T) {
     L.x = at;
     at = up(at + rows * H * 4);
     L.work = at;  // [q; k; v] rows, then gate/up rows
-    at = up(at + rows * std::max(qkvw, 2 * (size_t)c.intermediate) * 4);
+    at = up(at + rows * std::max(std::max(qkvw, 2 * (size_t)c.intermediate), H) * 4);
     L.planes = at;
     at = up(at + 2 * std::max(rows, scored) * widest * 2);
     L.logits = at;
@@ -334,6 +388,8 @@ int BatchedScorer::reserve(size_t rows, size_t scored, size_t T) {
     at = up(at + scored * 8);
     L.argmax = at;
     at = up(at + scored * 4);
+    L.margin = at;
+    at = up(at + scored * 8);
     L.status = at;
     at = up(at + 16);
     L.total = at;
@@ -359,18 +415,19 @@ int BatchedScorer::build(lsx_ctx* ctx, const FusedConfig& config, const std::vec
 
 int BatchedScorer::prefill(const uint32_t* tokens, size_t n) {
     LSX_ENSURE(n > 0 && n <= (size_t)config_.capacity, "check the prefill length");
-    return run(tokens, 1, n, 0, 0, nullptr, nullptr, nullptr, nullptr, true);
+    return run(tokens, 1, n, 0, 0, nullptr, nullptr, Outputs{}, true);
 }
 
 int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count,
-                         const uint32_t* targets, double* nll_out, uint32_t* argmax_out, float* logits_out) {
+                         const uint32_t* targets, const lsx_rotation* rotation, const Outputs& out) {
     LSX_ENSURE(cases > 0 && T > 0 && count > 0 && first + count <= T && targets, "check the case shape");
-    return run(tokens, cases, T, first, count, targets, nll_out, argmax_out, logits_out, false);
+    if (rotation) LSX_ENSURE(rotation->width == (size_t)config_.hidden && rotation->rank <= 256,
+                             "the edit must match the model width (rank at most 256)");
+    return run(tokens, cases, T, first, count, targets, rotation, out, false);
 }
 
 int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count,
-                       const uint32_t* targets, double* nll_out, uint32_t* argmax_out, float* logits_out,
-                       bool write_cache) {
+                       const uint32_t* targets, const lsx_rotation* rotation, const Outputs& out, bool write_cache) {
     const FusedConfig& c = config_;
     const size_t rows = cases * T, scored = cases * count;
     LSX_ENSURE(rows <= 2147483647ull / 4 && scored * (size_t)c.vocab <= (size_t)1 << 40, "too many rows");
@@ -389,6 +446,7 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
     int* d_rows = (int*)(base + L.rows);
     double* d_nll = (double*)(base + L.nll);
     uint32_t* d_argmax = (uint32_t*)(base + L.argmax);
+    double* d_margin = (double*)(base + L.margin);
     int* status = (int*)(base + L.status);
     cudaStream_t s = ctx_->stream;
     const int H = c.hidden, D = c.head_dim, QH = c.qheads, KVH = c.kvheads, I = c.intermediate, V = c.vocab;
@@ -469,17 +527,28 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
         if (host_status[1] != 0) return fail(LSX_E_NONFINITE, "check the finiteness of the model outputs");
         return LSX_OK;
     }
-    rms_planes_kernel<<<(int)scored, 256, 0, s>>>(x, d_rows, H, c.final_gain, c.eps, hi, lo);
+    if (rotation) {  // the edited readout of the unedited hidden state
+        rms_planes_kernel<<<(int)scored, 256, 0, s>>>(x, d_rows, H, c.final_gain, c.eps, hi, lo, work);
+        const bool joint = rotation->joint;
+        edit_rows_kernel<<<(int)scored, 256, 0, s>>>(
+            work, H, joint ? 2 : 1, rotation->cosine_minus_one, rotation->sine,
+            joint ? nullptr : (const float*)rotation->u->data, joint ? nullptr : (const float*)rotation->v->data,
+            (int)rotation->rank, joint ? (const float*)rotation->basis->data : nullptr,
+            joint ? (const float*)rotation->delta->data : nullptr, hi, lo);
+    } else {
+        rms_planes_kernel<<<(int)scored, 256, 0, s>>>(x, d_rows, H, c.final_gain, c.eps, hi, lo);
+    }
     LSX_CUDA(cudaGetLastError(), "final norm");
     LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, (int)scored, H, c.head, V, c.head_bias, logits, V, false, status));
-    row_nll_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_targets, d_nll);
-    row_argmax_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_argmax);
+    row_scores_kernel<<<(int)scored, 1024, 0, s>>>(logits, V, d_targets, d_nll, d_argmax, d_margin);
     LSX_CUDA(cudaGetLastError(), "scores");
-    if (nll_out) LSX_CUDA(cudaMemcpyAsync(nll_out, d_nll, scored * 8, cudaMemcpyDeviceToHost, s), "nll download");
-    if (argmax_out)
-        LSX_CUDA(cudaMemcpyAsync(argmax_out, d_argmax, scored * 4, cudaMemcpyDeviceToHost, s), "argmax download");
-    if (logits_out)
-        LSX_CUDA(cudaMemcpyAsync(logits_out, logits, scored * (size_t)V * 4, cudaMemcpyDeviceToHost, s),
+    if (out.nll) LSX_CUDA(cudaMemcpyAsync(out.nll, d_nll, scored * 8, cudaMemcpyDeviceToHost, s), "nll download");
+    if (out.argmax)
+        LSX_CUDA(cudaMemcpyAsync(out.argmax, d_argmax, scored * 4, cudaMemcpyDeviceToHost, s), "argmax download");
+    if (out.margin)
+        LSX_CUDA(cudaMemcpyAsync(out.margin, d_margin, scored * 8, cudaMemcpyDeviceToHost, s), "margin download");
+    if (out.logits)
+        LSX_CUDA(cudaMemcpyAsync(out.logits, logits, scored * (size_t)V * 4, cudaMemcpyDeviceToHost, s),
                  "logits download");
     LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
     LSX_CUDA(cudaStreamSynchronize(s), "batched scoring");

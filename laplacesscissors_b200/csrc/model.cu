@@ -1515,14 +1515,15 @@ int lsx_model_score(lsx_model* m, const uint32_t* prompt, size_t prompt_length, 
 // src/scaling.rs:181-216 batched over cases): every case's prompt and targets but
 // the last go through the decoder together, one tensor-core GEMM per projection.
 int lsx_model_score_batch(lsx_model* m, const uint32_t* prompts, size_t cases, size_t prompt_length,
-                          const uint32_t* targets, size_t count, double* nll_out, uint32_t* argmax_out,
-                          float* logits_out) {
+                          const uint32_t* targets, size_t count, const lsx_rotation* rotation, double* nll_out,
+                          uint32_t* argmax_out, double* margin_out, float* logits_out) {
     LSX_ENSURE(m && prompts && targets, "invalid argument");
     LSX_ENSURE(cases > 0 && prompt_length > 0 && count > 0, "give at least one case, prompt token and target");
     LSX_ENSURE(prompt_length + count - 1 <= m->capacity, "give a context that fits the prompt and the continuation");
     for (size_t i = 0; i < cases * prompt_length; ++i) LSX_ENSURE(prompts[i] < m->graph.vocab, "check the token range");
     for (size_t i = 0; i < cases * count; ++i) LSX_ENSURE(targets[i] < m->graph.vocab, "check the target range");
     if (!m->fused) return fail(LSX_E_UNSUPPORTED, "batched scoring needs the fused weight layout");
+    LSX_TRY(check_rotation(m, rotation));
     cudaSetDevice(m->ctx->device);
     LSX_TRY(ensure_batched(m));
     const size_t T = prompt_length + count - 1;
@@ -1531,8 +1532,12 @@ int lsx_model_score_batch(lsx_model* m, const uint32_t* prompts, size_t cases, s
         memcpy(fed.data() + c * T, prompts + c * prompt_length, prompt_length * 4);
         if (count > 1) memcpy(fed.data() + c * T + prompt_length, targets + c * count, (count - 1) * 4);
     }
-    return m->batched->score(fed.data(), cases, T, prompt_length - 1, count, targets, nll_out, argmax_out,
-                             logits_out);
+    BatchedScorer::Outputs out;
+    out.nll = nll_out;
+    out.argmax = argmax_out;
+    out.margin = margin_out;
+    out.logits = logits_out;
+    return m->batched->score(fed.data(), cases, T, prompt_length - 1, count, targets, rotation, out);
 }
 
 }  // extern "C"

@@ -240,11 +240,12 @@ class Model:
         fr = [Frame(hid[i].copy(), lg[i].copy()) for i in range(n)] if frames else None
         return nll, amax, fr
 
-    def score_batch(self, prompts, targets, logits: bool = False):
+    def score_batch(self, prompts, targets, rotation: DeviceRotation | None = None, logits: bool = False):
         """Teacher-forced scoring of many equal-shape cases at once
-        (lsx_model_score_batch): prompts [cases, P], targets [cases, n].  Returns
-        (nll f64 [cases, n], argmax u32 [cases, n], logits f32 [cases, n, vocab] or
-        None).  Leaves the decode cursor and KV cache as they were."""
+        (lsx_model_score_batch): prompts [cases, P], targets [cases, n], optionally
+        through the edited readout.  Returns (nll f64 [cases, n], argmax u32
+        [cases, n], margin f64 [cases, n], logits f32 [cases, n, vocab] or None).
+        Leaves the decode cursor and KV cache as they were."""
         p = np.ascontiguousarray(prompts, dtype=np.uint32)
         t = np.ascontiguousarray(targets, dtype=np.uint32)
         if p.ndim != 2 or t.ndim != 2 or p.shape[0] != t.shape[0]:
@@ -252,10 +253,11 @@ class Model:
         cases, n = t.shape
         nll = np.empty((cases, n), dtype=np.float64)
         amax = np.empty((cases, n), dtype=np.uint32)
+        margin = np.empty((cases, n), dtype=np.float64)
         lg = np.empty((cases, n, self.vocab_size()), dtype=np.float32) if logits else None
-        check(lib.lsx_model_score_batch(self._h, _up(p), cases, p.shape[1], _up(t), n, _dp(nll), _up(amax),
-                                        _fp(lg) if logits else None))
-        return nll, amax, lg
+        check(lib.lsx_model_score_batch(self._h, _up(p), cases, p.shape[1], _up(t), n, _rot(rotation), _dp(nll),
+                                        _up(amax), _dp(margin), _fp(lg) if logits else None))
+        return nll, amax, margin, lg
 
 
 __all__ = ["Model", "DeviceRotation", "Frame"]

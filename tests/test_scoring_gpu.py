@@ -152,21 +152,24 @@ def test_batched_scores_match_oracle_tiny(gpu, oracle):
     root = GOLDEN / "tiny_qwen3"
     model = load(gpu, root, 32)
     prompts, targets = batch_cases(3, 5, 7, 4, 512)
-    nll, amax, lg = model.score_batch(prompts, targets, logits=True)
+    nll, amax, margin, lg = model.score_batch(prompts, targets, logits=True)
     for c in range(len(prompts)):
         ref_nll, ref_amax = oracle_scores(oracle, root, prompts[c], targets[c])
         assert np.all(np.abs(nll[c] - ref_nll) <= 1e-3 * (1 + np.abs(ref_nll))), (c, nll[c], ref_nll)
         check_argmax(amax[c], ref_amax, oracle, root, prompts[c], targets[c])
-        # the logits are the frames of the sequential path
+        # the logits are the frames of the sequential path; margins follow
+        # minimum_margin (src/diagnosis.rs:490-492) of those logits
         _, _, frames = model.score(prompts[c], targets[c], frames=True)
         for k in range(targets.shape[1]):
             np.testing.assert_allclose(lg[c, k], frames[k].logits, rtol=2e-3, atol=2e-3)
+            want = oracle.minimum_margin(lg[c, k], int(targets[c, k]))
+            assert abs(margin[c, k] - want) <= 1e-9 * (1 + abs(want))
 
 
 def test_batched_single_case_single_target_and_checks(gpu, oracle):
     root = GOLDEN / "tiny_qwen3"
     model = load(gpu, root, 8)
-    nll, amax, _ = model.score_batch([[4]], [[9]])
+    nll, amax, _, _ = model.score_batch([[4]], [[9]])
     ref_nll, ref_amax = oracle_scores(oracle, root, [4], [9])
     assert abs(nll[0, 0] - ref_nll[0]) <= 1e-3 * (1 + abs(ref_nll[0]))
     model.reset()
@@ -188,10 +191,34 @@ def test_batched_scores_wide_shapes(gpu, oracle, shape, vocab):
     synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(getattr(synth, shape), layers=2, vocab=vocab)), seed=6)
     model = lsx.Model.load(d, gpu, 80)
     prompts, targets = batch_cases(6, 3, 64, 9, vocab)
-    nll, amax, _ = model.score_batch(prompts, targets)
+    nll, amax, _, _ = model.score_batch(prompts, targets)
     for c in range(len(prompts)):
         seq_nll, seq_amax, _ = model.score(prompts[c], targets[c])
         assert np.all(np.abs(nll[c] - seq_nll) <= 2e-2), (c, nll[c], seq_nll)
     ref_nll, ref_amax = oracle_scores(oracle, d, prompts[0], targets[0], capacity=80)
     assert np.all(np.abs(nll[0] - ref_nll) <= 2e-2), (nll[0], ref_nll)
     check_argmax(amax[0], ref_amax, oracle, d, prompts[0], targets[0], capacity=80)
+
+
+def test_batched_edited_scores_match_sequential(gpu, golden_tiny):
+    """The "after" pass (src/scaling.rs:199-203): the edited readout of the
+    unedited hidden states, batched, against lsx_model_score with the same plane
+    and joint edits."""
+    root = GOLDEN / "tiny_qwen3"
+    model = load(gpu, root, 32)
+    prompts, targets = batch_cases(4, 3, 6, 3, 512)
+    plane = DeviceRotation.upload(gpu, ReadoutRotation(golden_tiny["plane_u"], golden_tiny["plane_v"],
+                                                       float(golden_tiny["plane_tangent"])), model.hidden_size)
+    rng = np.random.default_rng(2)
+    basis, _ = np.linalg.qr(rng.standard_normal((model.hidden_size, 4)))
+    q, _ = np.linalg.qr(rng.standard_normal((4, 4)))
+    if np.linalg.det(q) < 0:
+        q[:, 0] *= -1
+    joint = DeviceRotation.upload_edit(gpu, lsx.SubspaceRotation(basis.T.copy(), q), model.hidden_size)
+    for edit in (plane, joint):
+        nll, amax, margin, _ = model.score_batch(prompts, targets, rotation=edit)
+        plain, _, _, _ = model.score_batch(prompts, targets)
+        assert not np.allclose(nll, plain)
+        for c in range(len(prompts)):
+            seq_nll, seq_amax, _ = model.score(prompts[c], targets[c], edit)
+            assert np.all(np.abs(nll[c] - seq_nll) <= 1e-3 * (1 + np.abs(seq_nll))), (c, nll[c], seq_nll)
