@@ -111,7 +111,7 @@ def _load() -> C.CDLL:
     path = os.environ.get("LSX_LIBRARY", str(LIBRARY))
     if not Path(path).exists():
         raise ImportError(
-            f"liblsx.so not found at {path}; build it with `python -m laplacesscissors_b200.build` "
+            f"liblsx.so not found at {path}; build it with `python laplacesscissors_b200/build.py` "
             "(the CUDA library is required: there is no fallback)")
     lib = C.CDLL(path)
     for name, (res, args) in SIGNATURES.items():

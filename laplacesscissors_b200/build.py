@@ -1,6 +1,6 @@
 """Builds liblsx.so (the CUDA sm_100a kernels and the C ABI of include/lsx.h) in-tree.
 
-Usage: python -m laplacesscissors_b200.build [--force] [--jobs N]
+Usage: python laplacesscissors_b200/build.py [--force] [--jobs N]
 
 Each csrc/*.cu compiles to _build/<name>.o with nvcc for sm_100a only; the objects
 link into laplacesscissors_b200/liblsx.so.  A source is rebuilt when it or any
