@@ -402,9 +402,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "score8b"], default="all",
+    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "score8b", "readout_vocab"],
+                    default="all",
                     help="all: the headline line; decode/readout/gemv: one leg only (with --profile); "
-                         "long4b: Qwen3-4B decode after a long prompt; score8b: Qwen3-8B teacher-forced scoring")
+                         "long4b: Qwen3-4B decode after a long prompt; score8b: Qwen3-8B teacher-forced scoring; "
+                         "readout_vocab: the validation workload with the lm_head split by rows over the GPUs")
     ap.add_argument("--prompt", type=int, default=4096, help="long4b: prompt length")
     ap.add_argument("--cases", type=int, default=64, help="score8b: cases timed (of the 1024-case job)")
     ap.add_argument("--batch", type=int, default=64, help="score8b: cases per lsx_model_score_batch call "
@@ -420,6 +422,8 @@ def main():
         return long_decode(args, local)
     if args.workload == "score8b":
         return scoring(args, local)
+    if args.workload == "readout_vocab":
+        return vocab_readout(args, rank, local, world)
     if args.profile:
         return profile_run(args, local)
     if args.warmup < 3:
@@ -509,6 +513,72 @@ def main():
             line["readout"]["cpu_baseline"] = {"value": rv, "unit": "rows/s", "cores": rcores, "kind": "port",
                                                "sample": rsample}
         print(json.dumps(line))
+    dist.close()
+
+
+def vocab_readout(args, rank, local, world):
+    """The readout-validation workload (4096 rows, rank-16 edit) with the lm_head
+    split by rows over the ranks: each GPU scores all rows against its vocabulary
+    block (lsx_readout_shard_device), one NCCL all-reduce MAX of the packed keys and
+    one of the target logits merge the blocks, and lsx_readout_merge_device gives
+    the margins.  Total work is fixed (strong scaling); each step is one whole
+    validation, timed with CUDA events on the library stream, max over ranks."""
+    import torch
+
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import DeviceRotation
+    from laplacesscissors_b200._lib import BF16, lib
+    from laplacesscissors_b200.sharding import vocab_shard, vocab_sharded_margin
+    args.warmup = max(args.warmup, 3)
+    dist = Dist(world, local)
+    gpu = lsx.Gpu(local)
+    peaks = measured_peaks()
+    w, hidden, targets, edit = readout_inputs(0, 1)
+    v0, v1 = vocab_shard(VOCAB, world, rank)
+    shard = gpu.upload_raw(np.ascontiguousarray(w.reshape(VOCAB, HIDDEN)[v0:v1]), BF16)
+    del w
+    rot = DeviceRotation.upload_edit(gpu, edit, HIDDEN)
+    dev = torch.device("cuda", local)
+    d_hidden = torch.from_numpy(hidden.view(np.int16)).to(dev)
+    d_targets = torch.from_numpy(targets.astype(np.uint32).view(np.int32)).to(dev)
+    ws = torch.empty(lib.lsx_readout_workspace_bytes(v1 - v0, HIDDEN, READOUT_ROWS, rot.handle), dtype=torch.uint8,
+                     device=dev)
+    torch.cuda.synchronize(dev)
+
+    def step():
+        return vocab_sharded_margin(gpu, shard, None, v0, v1 - v0, HIDDEN, d_hidden.data_ptr(), BF16, READOUT_ROWS,
+                                    d_targets.data_ptr(), rot, workspace=ws)
+
+    stream, event = cuda_timer(gpu)
+    for _ in range(args.warmup):
+        step()
+    gpu.synchronize()
+    dist.barrier()
+    start, stop = event(), event()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        stop.synchronize()
+    ms = dist.max(start.elapsed_time(stop)) / args.steps
+    if rank == 0:
+        tflops = 2.0 * READOUT_ROWS * VOCAB * HIDDEN / (ms / 1e3) / 1e12
+        print(json.dumps({
+            "metric": "readout-margin rows/s (lm_head split by vocabulary rows)",
+            "value": READOUT_ROWS / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate",
+            "data": "synthetic: lm_head N(0, 0.02) seed 7, 4096 RMSNorm'd rows, rank-16 Givens edit",
+            "config": {"workload": "4096 rows x lm_head [151936, 1024], rank-16 edit, vocab-sharded",
+                       "vocab_rows_per_gpu": VOCAB // world, "collective": "2 NCCL all-reduce MAX per step",
+                       "l2": "lm_head shard read once per step"},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": tflops / (world * peaks["bf16_tflops"]),
+                         "scope": f"whole validation over {world} GPU(s), {peaks['source']} burst peak x GPUs"},
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps * 6,
+        }))
     dist.close()
 
 

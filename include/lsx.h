@@ -240,6 +240,32 @@ int lsx_readout_margin_device(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_
                               double* margin_out, uint32_t* argmax_out, float* target_logit_out,
                               void* workspace, size_t workspace_bytes);
 size_t lsx_readout_workspace_bytes(size_t vocab, size_t width, size_t rows, const lsx_rotation* rotation);
+/* Vocabulary-sharded validation (the multi-GPU split of the lm_head by rows; the
+   reference runs the whole readout on one device, src/model.rs:664-685).  One
+   shard's part: `weight_shard` holds lm_head rows [vocab_offset, vocab_offset +
+   shard_vocab) ([shard_vocab x width] BF16), `bias_shard` the same slice of the
+   bias or NULL, targets are global token ids.  Per row it writes, to device
+   buffers, the packed key of the shard's best column other than the target
+   (total-order f32 value << 32 | (0xFFFFFFFF - global index), so the larger key
+   is the larger logit and, on equal logits, the lower index: the rule of other(),
+   src/diagnosis.rs:71-80) and the target's logit (-inf when the target lies
+   outside the shard).  The shards' partials combine by an element-wise maximum
+   (an all-reduce MAX of the keys as unsigned 64-bit integers and of the target
+   logits); lsx_readout_merge_device then gives margins and first argmaxes equal
+   to lsx_readout_margin_device's over the whole vocabulary.  workspace must hold
+   lsx_readout_workspace_bytes(shard_vocab, ...) bytes.  Asynchronous on the
+   context's stream. */
+int lsx_readout_shard_device(lsx_ctx* ctx, const lsx_tensor* weight_shard, const lsx_tensor* bias_shard,
+                             size_t vocab_offset, size_t shard_vocab, size_t width, const void* hidden,
+                             lsx_dtype hidden_kind, size_t rows, const uint32_t* targets,
+                             const lsx_rotation* rotation, uint64_t* other_key_out, float* target_logit_out,
+                             void* workspace, size_t workspace_bytes);
+/* Margins (f64(z_t) - f64(z_competitor), minimum_margin, src/diagnosis.rs:490-492),
+   first argmaxes (src/diagnosis.rs:58-70) and target logits from merged partials;
+   device pointers, any output may be NULL. */
+int lsx_readout_merge_device(lsx_ctx* ctx, const uint64_t* other_key, const float* target_logit,
+                             const uint32_t* targets, size_t rows, double* margin_out, uint32_t* argmax_out,
+                             float* target_logit_out);
 /* The device-pointer readout margin without an edit, for callers that must not
    allocate device memory (their memory is already fully committed, or an
    allocation at that point would be illegal or would stall other work).  It has

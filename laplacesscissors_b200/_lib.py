@@ -102,6 +102,8 @@ SIGNATURES = {
     "lsx_readout_margin_device": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P, P, P, SZ]),
     "lsx_readout_workspace_bytes": (SZ, [SZ, SZ, SZ, P]),
     "lsx_readout_margin_fixed": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P]),
+    "lsx_readout_shard_device": (I, [P, P, P, SZ, SZ, SZ, P, I, SZ, P, P, P, P, P, SZ]),
+    "lsx_readout_merge_device": (I, [P, P, P, P, SZ, P, P, P]),
     "lsx_synth_normal": (I, [U64, U64, U64, SZ, D, I, P]),
     "lsx_synth_uniform_u32": (I, [U64, U64, U64, SZ, U32, UP]),
 }

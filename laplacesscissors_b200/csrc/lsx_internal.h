@@ -122,6 +122,8 @@ struct lsx_rotation {
     lsx_tensor* v = nullptr;
     float cosine_minus_one = 0.f, sine = 0.f;
     // Joint: basis [rank x width], transpose [width x rank], delta = R - I [rank x rank].
+    // A plane also carries basis = [u; v] and delta = R - I (2 x 2), which the fused
+    // readout reads from the device for its rank-r correction.
     lsx_tensor* basis = nullptr;
     lsx_tensor* transpose = nullptr;
     lsx_tensor* delta = nullptr;

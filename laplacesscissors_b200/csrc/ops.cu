@@ -689,17 +689,22 @@ int lsx_rotation_plane(lsx_ctx* ctx, const double* u, const double* v, double ta
     double t = tangent, a = -2.0 * t * t / (1.0 + t * t), b = 2.0 * t / (1.0 + t * t);
     r->cosine_minus_one = (float)a;
     r->sine = (float)b;
-    int s = lsx_upload_f32(ctx, uf.data(), width, &r->u);
-    if (s == LSX_OK) s = lsx_upload_f32(ctx, vf.data(), width, &r->v);
-    if (s != LSX_OK) {
-        lsx_rotation_free(r);
-        return s;
-    }
     // ReadoutEdit::subspace (src/response.rs:240-251): basis [u; v], transform
     // [[1+a, b], [-b, 1+a]], so R - I = [[a, b], [-b, a]].
     r->basis64.assign(u, u + width);
     r->basis64.insert(r->basis64.end(), v, v + width);
     r->delta64 = {a, b, -b, a};
+    std::vector<float> uv(uf);
+    uv.insert(uv.end(), vf.begin(), vf.end());
+    const float dr[4] = {(float)a, (float)b, (float)-b, (float)a};
+    int s = lsx_upload_f32(ctx, uf.data(), width, &r->u);
+    if (s == LSX_OK) s = lsx_upload_f32(ctx, vf.data(), width, &r->v);
+    if (s == LSX_OK) s = lsx_upload_f32(ctx, uv.data(), uv.size(), &r->basis);
+    if (s == LSX_OK) s = lsx_upload_f32(ctx, dr, 4, &r->delta);
+    if (s != LSX_OK) {
+        lsx_rotation_free(r);
+        return s;
+    }
     *out = r;
     return LSX_OK;
 }

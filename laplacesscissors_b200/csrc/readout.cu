@@ -52,20 +52,17 @@ struct ReadoutParams {
     int M, V, H;
     int k_blocks, ext_blocks, m_tiles, n_tiles;
     const uint32_t* targets;
+    int vocab_offset;               // global index of column 0 (a vocabulary shard's first row)
     const float* bias;
     unsigned long long* other_key;  // [M] packed (value, index) of the best non-target
     float* target_logit;            // [M]
     int* status;                    // [0] device error code, [1] non-finite flag
-    // image mode: the extension block [V, image_stride] receives F = W U^T for
-    // ranks [image_k0, image_k0 + M / 2) of `image_rank` as [F_hi | F_hi | F_lo]
-    __nv_bfloat16* image;
-    int image_stride, image_rank, image_k0;
     // store mode: out[M, ldo] (=|+=) A B^T + bias, columns [0, V)
     float* out;
     int ldo, accumulate;
 };
 
-enum { kModeMargin = 0, kModeImage = 1, kModeStore = 2 };
+enum { kModeMargin = 0, kModeStore = 2 };
 
 // ---------------------------------------------------------------- PTX ------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -276,9 +273,7 @@ __device__ __forceinline__ void store_tile(uint32_t taddr, int row, bool live, i
     }
 }
 
-// MODE kModeMargin: the margin epilogue above.  MODE kModeImage: A holds the
-// edit basis as interleaved (hi, lo) bf16 rows and the epilogue writes the edit
-// image F = W U^T (each rank's two TMEM lanes summed) into the B extension.
+// MODE kModeMargin: the margin epilogue above.
 // MODE kModeStore: a plain GEMM, out = A B^T (+ bias), or out += ... with
 // `accumulate` (a residual add: each output element belongs to one tile).
 template <int PLANES, int STAGES, int MODE>
@@ -453,40 +448,6 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 break;
             }
             tc_fence_after();
-            if (MODE == kModeImage) {
-                // TMEM lane 2k + 0/1: rank k's hi/lo part; lanes of one rank are adjacent.
-                const int kl = row_local >> 1;
-                const bool writer = (lane & 1) == 0 && 2 * kl < p.M;
-                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
-                const int k = p.image_k0 + kl;
-#pragma unroll 1
-                for (int c = 0; c < RN / 32; ++c) {
-                    uint32_t r[32];
-                    tc_ld32(taddr + (uint32_t)(c * 32), r);
-                    tc_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float v = __uint_as_float(r[i]);
-                        const float f = v + __shfl_down_sync(0xffffffffu, v, 1);
-                        const int n = n0 + c * 32 + i;
-                        if (writer && n < p.V) {
-                            const __nv_bfloat16 hi = __float2bfloat16_rn(f);
-                            const __nv_bfloat16 lo = __float2bfloat16_rn(f - __bfloat162float(hi));
-                            __nv_bfloat16* dst = p.image + (size_t)n * p.image_stride;
-                            dst[k] = hi;
-                            dst[p.image_rank + k] = hi;
-                            dst[2 * p.image_rank + k] = lo;
-                        }
-                    }
-                }
-                tc_fence_before();
-                mbar_arrive(&tmem_empty[acc]);
-                if (++acc == 2) {
-                    acc = 0;
-                    acc_phase ^= 1u;
-                }
-                continue;
-            }
             if (MODE == kModeStore) {
                 const int row = m0 + row_local;
                 store_tile(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN), row, row < p.M, n0, p,
@@ -501,7 +462,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             }
             const int row = m0 + row_local;
             const bool live = row < p.M;
-            const int tcol = live ? (int)p.targets[row] - n0 : -1;
+            const int tcol = live ? (int)((long long)p.targets[row] - p.vocab_offset - n0) : -1;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
             RowScan scan;
             scan_tile(taddr, tcol, n0, p, scan);
@@ -511,7 +472,8 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             tc_fence_before();
             mbar_arrive(&tmem_empty[acc]);
             if (live) {
-                if (best_col >= 0) atomicMax(&p.other_key[row], pack_arg(best, (uint32_t)(n0 + best_col)));
+                if (best_col >= 0)
+                    atomicMax(&p.other_key[row], pack_arg(best, (uint32_t)(p.vocab_offset + n0 + best_col)));
                 if (tcol >= 0 && tcol < RN && n0 + tcol < p.V) p.target_logit[row] = tval;
             }
             if (++acc == 2) {
@@ -778,7 +740,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 }
                 continue;
             }
-            const int tcol = live ? (int)p.targets[row] - n0 : -1;
+            const int tcol = live ? (int)((long long)p.targets[row] - p.vocab_offset - n0) : -1;
             RowScan scan;
             scan_tile(taddr, tcol, n0, p, scan);
             nonfinite |= scan.probe != 0.f;  // NaN (non-finite logit) or never 0 otherwise
@@ -788,7 +750,8 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tmem_empty0 + (uint32_t)(acc * 8));
             if (live) {
-                if (best_col >= 0) atomicMax(&p.other_key[row], pack_arg(best, (uint32_t)(n0 + best_col)));
+                if (best_col >= 0)
+                    atomicMax(&p.other_key[row], pack_arg(best, (uint32_t)(p.vocab_offset + n0 + best_col)));
                 if (tcol >= 0 && tcol < RN && n0 + tcol < p.V) p.target_logit[row] = tval;
             }
             if (++acc == 2) {
@@ -833,57 +796,338 @@ __global__ void basis_split_kernel(const float* __restrict__ basis, int H, int k
     }
 }
 
-// c = (R - I) U h per hidden row, written as [c_hi | c_lo | c_hi] into the
-// extension block of A; also splits f32 hidden rows into bf16 hi/lo planes.
+// ------------------------------------------------------- edit image kernel --
+// F = W U^T for ranks [k0, k0 + kc) of the edit, written as the B extension of
+// the margin GEMM: row n of `image` holds [F_hi | F_hi | F_lo] (each `rank` wide)
+// and zeros up to `ext_k`.  The lm_head is the A operand here (128 vocab rows per
+// tile, one per TMEM lane) and the basis, as interleaved (hi, lo) bf16 rows, the B
+// operand (N = np columns, 2 kc rounded up to 32; rows past 2 kc read as zero), so
+// each epilogue thread owns one vocab row and writes it contiguously.  One pass
+// reads the lm_head once and is bound by HBM.
+//   warp 0     TMA producer (W tile 128 x 64, basis tile np x 64 per stage)
+//   warp 1     TMEM owner, single-thread MMA issuer (M = 128, N = np, K = 16)
+//   warps 2-5  epilogue: F_k = lane 2k + lane 2k + 1 of the accumulator, hi/lo split
+constexpr int kImageM = 128;
+constexpr int kImageMaxN = 128;        // 64 ranks per pass
+constexpr int kImageRanks = kImageMaxN / 2;
+constexpr int kImageThreads = 192;
+
+struct ImageParams {
+    int V, k_blocks, n_tiles, np, stages;
+    int rank, k0, kc, ext_k;
+    __nv_bfloat16* image;
+    int* status;
+};
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v) {
+    __align__(16) __nv_bfloat16 b[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = __float2bfloat16_rn(v[e]);
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(b);
+}
+
+__global__ void __launch_bounds__(kImageThreads, 1)
+    edit_image_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_u,
+                      const ImageParams p) {
+    constexpr int kTileW = kImageM * RK * 2;  // 16 KB
+    const int tile_u = p.np * RK * 2;
+    const int stage_bytes = kTileW + tile_u;
+    const int S = p.stages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* tmem_full = empty + S;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued_count = const_cast<int*>(abort_flag) + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 4 * 32);
+        }
+        *abort_flag = 0;
+        *issued_count = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {  // TMEM: two accumulators of np <= 128 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---------------- TMA producer ----------------
+            int stage = 0, issued = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sw = smem + (size_t)stage * stage_bytes;
+                    mbar_expect_tx(&full[stage], (uint32_t)stage_bytes);
+                    tma_load_2d(sw, &map_w, kb * RK, tile * kImageM, &full[stage]);
+                    tma_load_2d(sw + kTileW, &map_u, kb * RK, 0, &full[stage]);
+                    ++issued;
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            *issued_count = issued;
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---------------- MMA issuer ----------------
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.np >> 3) << 17) |
+                                   ((uint32_t)(kImageM >> 4) << 24);
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+                if (!wait_or_abort(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * p.np);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!wait_or_abort(&full[stage], phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sw = smem_u32(smem + (size_t)stage * stage_bytes);
+                    const uint64_t adesc = smem_desc_sw128(sw), bdesc = smem_desc_sw128(sw + kTileW);
+#pragma unroll
+                    for (int k = 0; k < RK / 16; ++k)
+                        tc_mma(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+                    tc_commit(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else {  // ---------------- epilogue warps 2..5 ----------------
+        const int quarter = warp & 3;
+        const int R = p.rank, k0 = p.k0, kc = p.kc;
+        const bool vec = (R % 8) == 0 && (k0 % 8) == 0 && (kc % 8) == 0 && (p.ext_k % 8) == 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+            const bool ok = wait_or_abort(&tmem_full[acc], acc_phase, abort_flag);
+            if (__any_sync(0xffffffffu, !ok)) {
+                if (lane == 0) {
+                    atomicExch(&p.status[0], kDeviceTimeoutEpilogue);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int n = tile * kImageM + quarter * 32 + lane;
+            const bool live = n < p.V;
+            __nv_bfloat16* dst = p.image + (size_t)(live ? n : 0) * p.ext_k;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.np);
+#pragma unroll 1
+            for (int c = 0; c < p.np / 32; ++c) {
+                uint32_t r[32];
+                tc_ld32(taddr + (uint32_t)(c * 32), r);
+                tc_wait_ld_regs(r);
+                float hi[16], lo[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float f = __uint_as_float(r[2 * j]) + __uint_as_float(r[2 * j + 1]);
+                    const __nv_bfloat16 h = __float2bfloat16_rn(f);
+                    hi[j] = __bfloat162float(h);
+                    lo[j] = f - hi[j];
+                }
+                if (!live) continue;
+                const int kb = 16 * c;  // first rank of this chunk, relative to k0
+                if (vec) {
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        if (kb + 8 * g + 8 <= kc) {
+                            const int k = k0 + kb + 8 * g;
+                            store_bf16x8(dst + k, hi + 8 * g);
+                            store_bf16x8(dst + R + k, hi + 8 * g);
+                            store_bf16x8(dst + 2 * R + k, lo + 8 * g);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (kb + j < kc) {
+                            const int k = k0 + kb + j;
+                            dst[k] = __float2bfloat16_rn(hi[j]);
+                            dst[R + k] = __float2bfloat16_rn(hi[j]);
+                            dst[2 * R + k] = __float2bfloat16_rn(lo[j]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);
+            if (live && k0 == 0)  // the padding columns of the extension block
+                for (int k = 3 * R; k < p.ext_k; ++k) dst[k] = __float2bfloat16_rn(0.f);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    __syncthreads();
+    if (*abort_flag) {
+        if (threadIdx.x == 0) {
+            const int issued = *issued_count;
+            for (int i = 0; i < S && i < issued; ++i) {
+                const int last = issued - 1 - ((issued - 1 - i) % S);
+                mbar_wait_bounded(&full[i], (uint32_t)((last / S) & 1));
+            }
+        }
+        __syncthreads();
+    }
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem_base) : "memory");
+}
+
+// c = (R - I) U h per hidden row (one warp per row), written as
+// [c_hi | c_lo | c_hi | 0 ...] into the extension block of A; with F32 hidden rows
+// also the bf16 hi/lo planes of the main product.  Each lane holds 8-element
+// slices of h (16-byte loads) and accumulates kRankBlock basis dot products at
+// once; U is read through L1 (every warp of the GPU reads the same rows).
+constexpr int kRankBlock = 16;
+constexpr int kMaxEditRank = 256;
+
 __global__ void __launch_bounds__(256) edit_coefficients_kernel(const void* __restrict__ hidden, int hidden_kind,
                                                                 int M, int H, const float* __restrict__ basis,
                                                                 const float* __restrict__ delta, int rank,
                                                                 __nv_bfloat16* __restrict__ ext_a, int ext_k,
                                                                 __nv_bfloat16* __restrict__ plane_hi,
                                                                 __nv_bfloat16* __restrict__ plane_lo) {
-    __shared__ float coords[8][256];
+    __shared__ float coords[8][kMaxEditRank];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x * 8 + warp;
     if (i >= M) return;
-    auto h_at = [&](int j) -> float {
-        if (hidden_kind == LSX_F32) return ((const float*)hidden)[(size_t)i * H + j];
-        return __bfloat162float(((const __nv_bfloat16*)hidden)[(size_t)i * H + j]);
+    const int nv = H >> 3;  // 8-element slices per row
+    auto load8 = [&](int v, float (&h)[8]) {
+        if (hidden_kind == LSX_F32) {
+            const float4* src = reinterpret_cast<const float4*>((const float*)hidden + (size_t)i * H) + 2 * v;
+            const float4 a = __ldg(src), b = __ldg(src + 1);
+            h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w;
+            h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
+        } else {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>((const __nv_bfloat16*)hidden + (size_t)i * H) + v);
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(b2[e]);
+                h[2 * e] = f.x;
+                h[2 * e + 1] = f.y;
+            }
+        }
     };
     if (plane_hi) {
-        for (int j = lane; j < H; j += 32) {
-            float h = h_at(j);
-            __nv_bfloat16 hi = __float2bfloat16_rn(h);
-            plane_hi[(size_t)i * H + j] = hi;
-            plane_lo[(size_t)i * H + j] = __float2bfloat16_rn(h - __bfloat162float(hi));
+        for (int v = lane; v < nv; v += 32) {
+            float h[8];
+            load8(v, h);
+            __align__(16) __nv_bfloat16 hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                hi[e] = __float2bfloat16_rn(h[e]);
+                lo[e] = __float2bfloat16_rn(h[e] - __bfloat162float(hi[e]));
+            }
+            reinterpret_cast<uint4*>(plane_hi + (size_t)i * H)[v] = *reinterpret_cast<const uint4*>(hi);
+            reinterpret_cast<uint4*>(plane_lo + (size_t)i * H)[v] = *reinterpret_cast<const uint4*>(lo);
         }
     }
     if (rank == 0) return;
-    for (int k = 0; k < rank; ++k) {
-        float d = 0.f;
-        for (int j = lane; j < H; j += 32) d = fmaf(basis[(size_t)k * H + j], h_at(j), d);
-        d = warp_allsum(d);
-        if (lane == 0) coords[warp][k] = d;
+    for (int k0 = 0; k0 < rank; k0 += kRankBlock) {
+        float acc[kRankBlock];
+#pragma unroll
+        for (int k = 0; k < kRankBlock; ++k) acc[k] = 0.f;
+        for (int v = lane; v < nv; v += 32) {
+            float h[8];
+            load8(v, h);
+#pragma unroll
+            for (int k = 0; k < kRankBlock; ++k) {
+                if (k0 + k < rank) {
+                    const float4* u = reinterpret_cast<const float4*>(basis + (size_t)(k0 + k) * H) + 2 * v;
+                    const float4 a = __ldg(u), b = __ldg(u + 1);
+                    float d = acc[k];
+                    d = fmaf(a.x, h[0], d);
+                    d = fmaf(a.y, h[1], d);
+                    d = fmaf(a.z, h[2], d);
+                    d = fmaf(a.w, h[3], d);
+                    d = fmaf(b.x, h[4], d);
+                    d = fmaf(b.y, h[5], d);
+                    d = fmaf(b.z, h[6], d);
+                    d = fmaf(b.w, h[7], d);
+                    acc[k] = d;
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kRankBlock; ++k) {
+            const float t = warp_allsum(acc[k]);
+            if (lane == 0 && k0 + k < rank) coords[warp][k0 + k] = t;
+        }
     }
     __syncwarp();
     __nv_bfloat16* dst = ext_a + (size_t)i * ext_k;
-    for (int k = lane; k < ext_k; k += 32) dst[k] = __float2bfloat16_rn(0.f);
-    __syncwarp();
+    for (int k = 3 * rank + lane; k < ext_k; k += 32) dst[k] = __float2bfloat16_rn(0.f);
     for (int k = lane; k < rank; k += 32) {
         float c = 0.f;
         for (int q = 0; q < rank; ++q) c = fmaf(delta[k * rank + q], coords[warp][q], c);
-        __nv_bfloat16 hi = __float2bfloat16_rn(c);
-        __nv_bfloat16 lo = __float2bfloat16_rn(c - __bfloat162float(hi));
+        const __nv_bfloat16 hi = __float2bfloat16_rn(c);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(c - __bfloat162float(hi));
         dst[k] = hi;
         dst[rank + k] = lo;
         dst[2 * rank + k] = hi;
     }
 }
 
-__global__ void readout_init_kernel(unsigned long long* other_key, float* target_logit, int M, int* status) {
+// A target logit starts as NaN (never set: a target outside the vocabulary), or
+// as -inf for a vocabulary shard, whose merge takes the maximum over shards.
+__global__ void readout_init_kernel(unsigned long long* other_key, float* target_logit, int M, int* status,
+                                    bool shard) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < M) {
         other_key[i] = 0ull;
-        target_logit[i] = __int_as_float(0x7fc00000);
+        target_logit[i] = shard ? -INFINITY : __int_as_float(0x7fc00000);
     }
     if (i < 2) status[i] = 0;
 }
@@ -945,7 +1189,6 @@ int make_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, u
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-constexpr int kImageRanks = RM / 2;  // ranks per image pass (two A rows each)
 
 struct Layout {
     size_t ext_k, planes_off, planes_bytes, ext_a_off, ext_b_off, basis_off, delta_off, image_a_off, key_off,
@@ -1064,11 +1307,21 @@ size_t readout_workspace_need(size_t vocab, size_t width, size_t rows, size_t ra
     return layout_for(vocab, width, rows, rank, f32_hidden).total;
 }
 
+// One vocabulary shard's outputs: per-row partials instead of margins.
+struct ShardOut {
+    size_t vocab_offset;
+    unsigned long long* other_key;
+    float* target_logit;
+};
+
 // Enqueues the whole validation on ctx->stream.  All pointers are device pointers.
-int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
-                           const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
-                           const lsx_rotation* rotation, double* margin, uint32_t* argmax, float* target_logit,
-                           void* workspace, size_t workspace_bytes, int* host_status) {
+// With `shard`, `weight` holds lm_head rows [vocab_offset, vocab_offset + vocab),
+// targets are global ids, and the per-row partials land in the shard's buffers
+// (no finalize).
+int readout_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
+                    const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
+                    const lsx_rotation* rotation, double* margin, uint32_t* argmax, float* target_logit,
+                    void* workspace, size_t workspace_bytes, int* host_status, const ShardOut* shard) {
     LSX_ENSURE(weight && weight->kind == LSX_BF16, "the readout weight must be a BF16 tensor");
     LSX_ENSURE(vocab > 1 && width > 0 && weight->count == vocab * width, "check the readout weight dimensions");
     LSX_ENSURE(!bias || (bias->kind == LSX_F32 && bias->count == vocab), "the readout bias is F32 [vocab]");
@@ -1076,6 +1329,8 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
     LSX_ENSURE(rows > 0 && rows <= 2147483647ull && vocab <= 2147483647ull, "check the row count");
     LSX_ENSURE(width % 8 == 0, "the readout width must be a multiple of 8");
     if (rotation) LSX_ENSURE(rotation->width == width, "the rotation width does not match the readout");
+    if (rotation) LSX_ENSURE(rotation->rank >= 1 && rotation->rank <= (size_t)kMaxEditRank, "the edit rank is 1..256");
+    LSX_ENSURE((uintptr_t)hidden % 16 == 0, "hidden states must be 16-byte aligned");
     const size_t rank = rotation ? rotation->rank : 0;
     const bool f32_hidden = hidden_kind == LSX_F32;
     Layout L = layout_for(vocab, width, rows, rank, f32_hidden);
@@ -1083,56 +1338,69 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
     uint8_t* ws = (uint8_t*)workspace;
     cudaStream_t s = ctx->stream;
     int* status = (int*)(ws + L.status_off);
-    unsigned long long* keys = (unsigned long long*)(ws + L.key_off);
-    float* tlog = (float*)(ws + L.tlog_off);
+    unsigned long long* keys = shard ? shard->other_key : (unsigned long long*)(ws + L.key_off);
+    float* tlog = shard ? shard->target_logit : (float*)(ws + L.tlog_off);
+    if (shard)
+        LSX_ENSURE(shard->vocab_offset + vocab <= 2147483647ull, "check the vocabulary shard range");
     __nv_bfloat16* plane_hi = f32_hidden ? (__nv_bfloat16*)(ws + L.planes_off) : nullptr;
     __nv_bfloat16* plane_lo = f32_hidden ? plane_hi + rows * width : nullptr;
     __nv_bfloat16* ext_a = (__nv_bfloat16*)(ws + L.ext_a_off);
     __nv_bfloat16* ext_b = (__nv_bfloat16*)(ws + L.ext_b_off);
     const int M = (int)rows, V = (int)vocab, H = (int)width;
 
-    readout_init_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, M, status);
+    readout_init_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, M, status, shard != nullptr);
     LSX_CUDA(cudaGetLastError(), "readout init");
     if (rank > 0) {
-        // Edit basis and R - I in f32 from the f64 host copies.
-        std::vector<float> b(rank * width), d(rank * rank);
-        for (size_t i = 0; i < b.size(); ++i) b[i] = (float)rotation->basis64[i];
-        for (size_t i = 0; i < d.size(); ++i) d[i] = (float)rotation->delta64[i];
-        float* dbasis = (float*)(ws + L.basis_off);
-        float* ddelta = (float*)(ws + L.delta_off);
-        LSX_CUDA(cudaMemcpyAsync(dbasis, b.data(), b.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
-        LSX_CUDA(cudaMemcpyAsync(ddelta, d.data(), d.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
-        LSX_CUDA(cudaStreamSynchronize(s), "edit upload");  // host vectors go out of scope
-        LSX_CUDA(cudaMemsetAsync(ext_b, 0, vocab * L.ext_k * 2, s), "extension clear");
-        // F = W U^T on the tensor cores, up to kImageRanks ranks per pass.
+        // Edit basis and R - I in f32: the rotation's device copies when it lives
+        // on this device, else uploaded from its f64 host copies.
+        const float* dbasis;
+        const float* ddelta;
+        if (rotation->basis && rotation->delta && rotation->ctx && rotation->ctx->device == ctx->device) {
+            dbasis = (const float*)rotation->basis->data;
+            ddelta = (const float*)rotation->delta->data;
+        } else {
+            std::vector<float> b(rank * width), d(rank * rank);
+            for (size_t i = 0; i < b.size(); ++i) b[i] = (float)rotation->basis64[i];
+            for (size_t i = 0; i < d.size(); ++i) d[i] = (float)rotation->delta64[i];
+            float* ub = (float*)(ws + L.basis_off);
+            float* ud = (float*)(ws + L.delta_off);
+            LSX_CUDA(cudaMemcpyAsync(ub, b.data(), b.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
+            LSX_CUDA(cudaMemcpyAsync(ud, d.data(), d.size() * 4, cudaMemcpyHostToDevice, s), "edit upload");
+            LSX_CUDA(cudaStreamSynchronize(s), "edit upload");  // host vectors go out of scope
+            dbasis = ub;
+            ddelta = ud;
+        }
+        // F = W U^T on the tensor cores, up to kImageRanks ranks per pass; the
+        // passes also write the extension block's zero padding.
         __nv_bfloat16* image_a = (__nv_bfloat16*)(ws + L.image_a_off);
         CUtensorMap mw;
-        LSX_TRY(make_map(&mw, weight->data, width, vocab, width * 2, RN));
-        auto ik = readout_margin_kernel<1, 4, kModeImage>;
-        const size_t ismem = readout_smem<1, 4>();
-        LSX_CUDA(cudaFuncSetAttribute((const void*)ik, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem),
-                 "edit image smem attribute");
+        LSX_TRY(make_map(&mw, weight->data, width, vocab, width * 2, kImageM));
+        const int n_tiles = (V + kImageM - 1) / kImageM;
         for (int k0 = 0; k0 < (int)rank; k0 += kImageRanks) {
             const int kc = std::min(kImageRanks, (int)rank - k0);
             basis_split_kernel<<<std::min(ctx->sm_count, (kc * H + 255) / 256), 256, 0, s>>>(dbasis, H, k0, kc,
                                                                                            image_a);
             LSX_CUDA(cudaGetLastError(), "edit basis split");
-            CUtensorMap mu;
-            LSX_TRY(make_map(&mu, image_a, width, 2 * (size_t)kc, width * 2, RM));
-            ReadoutParams q{};
-            q.M = 2 * kc;
+            ImageParams q{};
             q.V = V;
-            q.H = H;
             q.k_blocks = (H + RK - 1) / RK;
-            q.ext_blocks = 0;
-            q.m_tiles = 1;
-            q.n_tiles = (V + RN - 1) / RN;
-            q.status = status;
+            q.n_tiles = n_tiles;
+            q.np = ((2 * kc + 31) / 32) * 32;
+            q.rank = (int)rank;
+            q.k0 = k0;
+            q.kc = kc;
+            q.ext_k = (int)L.ext_k;
             q.image = ext_b;
-            q.image_stride = (int)L.ext_k;
-            q.image_rank = (int)rank;
-            q.image_k0 = k0;
-            ik<<<std::min(q.n_tiles, ctx->sm_count), kReadoutThreads, ismem, s>>>(mu, mu, mw, mu, mw, q);
+            q.status = status;
+            const int stage_bytes = kImageM * RK * 2 + q.np * RK * 2;
+            q.stages = std::min(8, (int)((200u << 10) / stage_bytes));
+            const size_t ismem = (size_t)q.stages * stage_bytes + 1024 + (2 * q.stages + 4) * 8 + 16;
+            CUtensorMap mu;
+            LSX_TRY(make_map(&mu, image_a, width, 2 * (size_t)kc, width * 2, (uint32_t)q.np));
+            LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)ismem),
+                     "edit image smem attribute");
+            edit_image_kernel<<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
             LSX_CUDA(cudaGetLastError(), "edit image");
         }
         edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, dbasis, ddelta, (int)rank,
@@ -1165,6 +1433,7 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
     p.m_tiles = (M + RM - 1) / RM;
     p.n_tiles = (V + RN - 1) / RN;
     p.targets = targets;
+    p.vocab_offset = shard ? (int)shard->vocab_offset : 0;
     p.bias = bias ? (const float*)bias->data : nullptr;
     p.other_key = keys;
     p.target_logit = tlog;
@@ -1195,12 +1464,22 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
         k<<<grid, kReadoutThreads, smem, s>>>(ma, ma2, mb, mea, meb, p);
     }
     LSX_CUDA(cudaGetLastError(), "readout margin launch");
-    readout_finalize_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, targets, M, margin, argmax, target_logit);
-    LSX_CUDA(cudaGetLastError(), "readout finalize");
+    if (!shard) {
+        readout_finalize_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, targets, M, margin, argmax, target_logit);
+        LSX_CUDA(cudaGetLastError(), "readout finalize");
+    }
     if (host_status) {
         LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
     }
     return LSX_OK;
+}
+
+int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
+                           const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
+                           const lsx_rotation* rotation, double* margin, uint32_t* argmax, float* target_logit,
+                           void* workspace, size_t workspace_bytes, int* host_status) {
+    return readout_enqueue(ctx, weight, bias, vocab, width, hidden, hidden_kind, rows, targets, rotation, margin,
+                           argmax, target_logit, workspace, workspace_bytes, host_status, nullptr);
 }
 
 }  // namespace lsx
@@ -1208,6 +1487,32 @@ int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_ten
 using namespace lsx;
 
 extern "C" {
+
+int lsx_readout_shard_device(lsx_ctx* ctx, const lsx_tensor* weight_shard, const lsx_tensor* bias_shard,
+                             size_t vocab_offset, size_t shard_vocab, size_t width, const void* hidden,
+                             lsx_dtype hidden_kind, size_t rows, const uint32_t* targets,
+                             const lsx_rotation* rotation, uint64_t* other_key_out, float* target_logit_out,
+                             void* workspace, size_t workspace_bytes) {
+    LSX_ENSURE(ctx && hidden && targets && other_key_out && target_logit_out, "invalid argument");
+    cudaSetDevice(ctx->device);
+    const ShardOut shard{vocab_offset, (unsigned long long*)other_key_out, target_logit_out};
+    return readout_enqueue(ctx, weight_shard, bias_shard, shard_vocab, width, hidden, hidden_kind, rows, targets,
+                           rotation, nullptr, nullptr, nullptr, workspace, workspace_bytes, nullptr, &shard);
+}
+
+int lsx_readout_merge_device(lsx_ctx* ctx, const uint64_t* other_key, const float* target_logit,
+                             const uint32_t* targets, size_t rows, double* margin_out, uint32_t* argmax_out,
+                             float* target_logit_out) {
+    LSX_ENSURE(ctx && other_key && target_logit && targets, "invalid argument");
+    LSX_ENSURE(rows > 0 && rows <= 2147483647ull, "check the row count");
+    cudaSetDevice(ctx->device);
+    const int M = (int)rows;
+    readout_finalize_kernel<<<(M + 255) / 256, 256, 0, ctx->stream>>>((const unsigned long long*)other_key,
+                                                                      target_logit, targets, M, margin_out,
+                                                                      argmax_out, target_logit_out);
+    LSX_CUDA(cudaGetLastError(), "readout merge");
+    return LSX_OK;
+}
 
 size_t lsx_readout_workspace_bytes(size_t vocab, size_t width, size_t rows, const lsx_rotation* rotation) {
     // Sized for F32 hidden states (the larger case).

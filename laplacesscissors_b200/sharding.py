@@ -96,23 +96,79 @@ def shard_partials(logits: np.ndarray, targets: np.ndarray, v0: int) -> tuple[np
     return keys, tl
 
 
+def merge_partials_(keys, target_logit, group=None) -> None:
+    """In-place max-merge of vocabulary-shard partials across `group`: `keys` is an
+    int64 tensor holding the bits of the packed unsigned keys, `target_logit` f32.
+    The keys are compared as unsigned 64-bit integers, so the sign bit is flipped
+    around a signed all-reduce MAX.  Runs on the tensors' device (NCCL for CUDA
+    tensors, gloo on CPU) and on the current stream."""
+    import torch
+    import torch.distributed as dist
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    flip = torch.tensor(-(1 << 63), dtype=torch.int64, device=keys.device)
+    keys.bitwise_xor_(flip)
+    dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+    keys.bitwise_xor_(flip)
+    dist.all_reduce(target_logit, op=dist.ReduceOp.MAX, group=group)
+
+
 def merge_vocab_partials(keys: np.ndarray, target_logit: np.ndarray, targets: np.ndarray, group=None):
     """Max-reduces the shards' packed competitor keys and target logits across the
     group and returns (margin f64, first argmax u32, target logit f32) per row."""
     import torch
-    import torch.distributed as dist
     device = _device_of(group)
-    k = torch.from_numpy(np.ascontiguousarray(keys, dtype=np.uint64).view(np.int64)).to(device)
-    # Packed keys are compared as unsigned: flip the sign bit so signed max agrees.
-    k = k ^ torch.tensor(-(1 << 63), dtype=torch.int64, device=device)
-    dist.all_reduce(k, op=dist.ReduceOp.MAX, group=group)
-    k = (k ^ torch.tensor(-(1 << 63), dtype=torch.int64, device=device)).cpu().numpy().view(np.uint64)
-    t = torch.from_numpy(np.ascontiguousarray(target_logit, dtype=np.float32)).to(device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    k = torch.from_numpy(np.ascontiguousarray(keys, dtype=np.uint64).view(np.int64).copy()).to(device)
+    t = torch.from_numpy(np.ascontiguousarray(target_logit, dtype=np.float32).copy()).to(device)
+    merge_partials_(k, t, group)
+    k = k.cpu().numpy().view(np.uint64)
     tl = t.cpu().numpy()
     other, other_idx = unpack_key(k)
     margin = tl.astype(np.float64) - other.astype(np.float64)
     tgt = np.asarray(targets, dtype=np.uint32)
     # the target is the argmax when it beats the best other, or ties it with a lower index
     amax = np.where((tl > other) | ((tl == other) & (tgt < other_idx)), tgt, other_idx).astype(np.uint32)
+    return margin, amax, tl
+
+
+def vocab_sharded_margin(gpu, weight_shard, bias_shard, vocab_offset: int, shard_vocab: int, width: int,
+                         hidden_ptr: int, hidden_kind: int, rows: int, targets_ptr: int, rotation=None, group=None,
+                         workspace=None):
+    """Readout validation with the lm_head split by rows across the ranks of
+    `group` (one GPU per rank), on device-resident inputs.
+
+    This rank holds lm_head rows [vocab_offset, vocab_offset + shard_vocab)
+    (`weight_shard`, a BF16 Tensor) and scores every hidden row against them with
+    lsx_readout_shard_device; one NCCL all-reduce MAX of the packed competitor keys
+    and one of the target logits combine the shards, and lsx_readout_merge_device
+    turns the merged partials into margins and first argmaxes.  All work is ordered
+    on the library's stream.  `hidden_ptr` / `targets_ptr` are device addresses
+    ([rows, width] of `hidden_kind`; global target ids as u32).  Returns device
+    tensors (margin f64, argmax int32 holding the u32 ids, target logit f32)."""
+    import ctypes as C
+
+    import torch
+
+    from ._lib import check, lib
+    dev = torch.device("cuda", gpu.device)
+    rot = rotation.handle if rotation is not None else None
+    stream = torch.cuda.ExternalStream(gpu.stream(), device=dev)
+    with torch.cuda.stream(stream):
+        if workspace is None:
+            workspace = torch.empty(lib.lsx_readout_workspace_bytes(shard_vocab, width, rows, rot),
+                                    dtype=torch.uint8, device=dev)
+        keys = torch.empty(rows, dtype=torch.int64, device=dev)
+        tlog = torch.empty(rows, dtype=torch.float32, device=dev)
+        check(lib.lsx_readout_shard_device(gpu.handle, weight_shard.handle, bias_shard.handle if bias_shard else None,
+                                           int(vocab_offset), int(shard_vocab), int(width), C.c_void_p(hidden_ptr),
+                                           int(hidden_kind), int(rows), C.c_void_p(targets_ptr), rot,
+                                           C.c_void_p(keys.data_ptr()), C.c_void_p(tlog.data_ptr()),
+                                           C.c_void_p(workspace.data_ptr()), workspace.numel()))
+        merge_partials_(keys, tlog, group)
+        margin = torch.empty(rows, dtype=torch.float64, device=dev)
+        amax = torch.empty(rows, dtype=torch.int32, device=dev)
+        tl = torch.empty(rows, dtype=torch.float32, device=dev)
+        check(lib.lsx_readout_merge_device(gpu.handle, C.c_void_p(keys.data_ptr()), C.c_void_p(tlog.data_ptr()),
+                                           C.c_void_p(targets_ptr), int(rows), C.c_void_p(margin.data_ptr()),
+                                           C.c_void_p(amax.data_ptr()), C.c_void_p(tl.data_ptr())))
     return margin, amax, tl

@@ -73,6 +73,22 @@ def test_margin_with_edits(gpu, oracle, kind):
         check_rows(margin, amax, tl, ref, 1e-5)
 
 
+@pytest.mark.parametrize("rank", [5, 70, 130])
+def test_margin_with_wide_edits(gpu, oracle, rank):
+    """Edit ranks that are not multiples of 8, and ranks that need more than one
+    pass of the edit-image kernel (64 ranks per pass)."""
+    V, H, n = 1031, 256, 96
+    w, hidden, targets = problem(V, H, n)
+    h32 = synth.bf16_to_f32(hidden)
+    spec = lsx.random_subspace_rotation(H, rank, 3.0, seed=6)
+    edited = np.stack([spec.apply(h) for h in h32.astype(np.float64)]).astype(np.float32)
+    ref = oracle.readout_rows(w, oracle.BF16, None, V, H, edited, targets)
+    weight = gpu.upload_raw(w, BF16)
+    rot = DeviceRotation.upload_edit(gpu, spec, H)
+    margin, amax, tl = diagnosis.readout_margin(gpu, weight, None, V, H, hidden, targets, rot)
+    check_rows(margin, amax, tl, ref, 1e-5)
+
+
 def test_ties_resolve_to_lowest_index(gpu, oracle):
     """Duplicate vocab rows produce exact ties: first argmax, lowest-index competitor."""
     V, H, n = 600, 64, 130
