@@ -175,6 +175,12 @@ int lsx_model_embedding_vector(lsx_model* model, uint32_t token, float* out);
 int lsx_model_readout(lsx_model* model, const float* hidden, const lsx_rotation* rotation, float* logits_out);
 /* Model::head_image (src/model.rs:643-652): W u without bias for an f64 direction. */
 int lsx_model_head_image(lsx_model* model, const double* vector, float* out);
+/* Model::head_image for `count` directions at once, as the joint search calls it
+   once per basis axis (src/diagnosis.rs:777-781): out[k * vocab + i] = (W f32(u_k))[i]
+   for vectors [count x hidden] (f64, row-major).  One tensor-core pass over the
+   lm_head per 32 directions, each f32 direction entering exactly as three bf16
+   terms; results equal lsx_model_head_image's up to f32 summation order. */
+int lsx_model_head_images(lsx_model* model, const double* vectors, size_t count, float* out);
 /* Model::head_row (src/model.rs:653-663). */
 int lsx_model_head_row(lsx_model* model, uint32_t token, float* out);
 /* Readout weight and bias of the model (non-owning; bias NULL when absent). */
@@ -240,6 +246,20 @@ int lsx_readout_margin_device(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_
                               double* margin_out, uint32_t* argmax_out, float* target_logit_out,
                               void* workspace, size_t workspace_bytes);
 size_t lsx_readout_workspace_bytes(size_t vocab, size_t width, size_t rows, const lsx_rotation* rotation);
+/* CompactReadout::evaluate (src/diagnosis.rs:643-665) fused with minimum_margin,
+   other and argmax (src/diagnosis.rs:58-80, 490-492): for observation o the scores
+   z_o = image c_o + baseline_o are reduced on the device, never stored, to
+     margin_out[o] = f64(z_o[t_o]) - f64(max_{j != t_o} z_o[j]),
+     other_out[o]  = that competitor (lowest index on ties),
+     argmax_out[o] = first index of max_j z_o[j].
+   image: F32 tensor [vocab x rank] (the transposed head images, rank <= 256);
+   baseline: F32 tensor [count x vocab] (each observation's current logits);
+   coefficients [count x rank] f32 and targets [count] are host arrays, outputs
+   host arrays (any may be NULL).  A non-finite score fails with LSX_E_NONFINITE,
+   as the reference rejects it. */
+int lsx_compact_margin(lsx_ctx* ctx, const lsx_tensor* image, const lsx_tensor* baseline, size_t vocab,
+                       size_t rank, size_t count, const float* coefficients, const uint32_t* targets,
+                       double* margin_out, uint32_t* other_out, uint32_t* argmax_out);
 /* Vocabulary-sharded validation (the multi-GPU split of the lm_head by rows; the
    reference runs the whole readout on one device, src/model.rs:664-685).  One
    shard's part: `weight_shard` holds lm_head rows [vocab_offset, vocab_offset +

@@ -94,6 +94,7 @@ SIGNATURES = {
     "lsx_model_readout": (I, [P, FP, P, FP]),
     "lsx_model_head_image": (I, [P, DP, FP]),
     "lsx_model_head_row": (I, [P, U32, FP]),
+    "lsx_model_head_images": (I, [P, DP, SZ, FP]),
     "lsx_model_head": (I, [P, PP, PP]),
     "lsx_model_generate": (I, [P, UP, SZ, SZ, UP, SZ, P, UP, C.POINTER(SZ), C.POINTER(I), FP, FP]),
     "lsx_model_score": (I, [P, UP, SZ, UP, SZ, P, DP, UP, FP, FP]),
@@ -102,6 +103,7 @@ SIGNATURES = {
     "lsx_readout_margin_device": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P, P, P, SZ]),
     "lsx_readout_workspace_bytes": (SZ, [SZ, SZ, SZ, P]),
     "lsx_readout_margin_fixed": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P]),
+    "lsx_compact_margin": (I, [P, P, P, SZ, SZ, SZ, FP, UP, DP, UP, UP]),
     "lsx_readout_shard_device": (I, [P, P, P, SZ, SZ, SZ, P, I, SZ, P, P, P, P, P, SZ]),
     "lsx_readout_merge_device": (I, [P, P, P, P, SZ, P, P, P]),
     "lsx_synth_normal": (I, [U64, U64, U64, SZ, D, I, P]),

@@ -109,6 +109,11 @@ cudaError_t launch_rotate(cudaStream_t s, const float* h, const float* u, const 
                           size_t width, float* out);
 cudaError_t launch_all_finite(cudaStream_t s, const float* x, size_t n, int* flag);
 
+// ---- head images on the tensor cores (readout.cu) ----
+size_t head_images_scratch(size_t count, size_t width);
+int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, size_t width, const float* dirs_host,
+                        size_t count, float* out, void* scratch);
+
 }  // namespace lsx
 
 // Rotation kept on the device in the form DeviceRotation uses (src/model.rs:285-299),

@@ -1323,6 +1323,33 @@ int lsx_model_head_image(lsx_model* m, const double* vector, float* out) {
     return LSX_OK;
 }
 
+int lsx_model_head_images(lsx_model* m, const double* vectors, size_t count, float* out) {
+    LSX_ENSURE(m && vectors && out && count > 0, "invalid argument");
+    const size_t H = m->graph.hidden, V = m->graph.vocab;
+    std::vector<float> v(count * H);
+    for (size_t i = 0; i < v.size(); ++i) {
+        LSX_ENSURE(std::isfinite(vectors[i]), "check the readout direction dimension");
+        v[i] = (float)vectors[i];
+    }
+    if (m->head.weight->kind != LSX_BF16 || H % 8 != 0) {  // one matvec per direction
+        for (size_t k = 0; k < count; ++k) LSX_TRY(lsx_model_head_image(m, vectors + k * H, out + k * V));
+        return LSX_OK;
+    }
+    cudaSetDevice(m->ctx->device);
+    const size_t out_bytes = (count * V * 4 + 255) & ~size_t(255);
+    void* block = nullptr;
+    LSX_TRY(device_alloc(m->ctx, out_bytes + head_images_scratch(count, H), &block));
+    float* d_out = (float*)block;
+    int rc = head_images_enqueue(m->ctx, m->head.weight, V, H, v.data(), count, d_out, (uint8_t*)block + out_bytes);
+    if (rc == LSX_OK) {
+        cudaError_t e = cudaMemcpyAsync(out, d_out, count * V * 4, cudaMemcpyDeviceToHost, m->ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(m->ctx->stream);
+        if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("head images", e));
+    }
+    device_release(m->ctx, block);
+    return rc;
+}
+
 int lsx_model_head_row(lsx_model* m, uint32_t token, float* out) {
     LSX_ENSURE(m && out, "invalid argument");
     LSX_ENSURE(token < m->graph.vocab, "check the output token range");

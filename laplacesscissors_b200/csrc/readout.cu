@@ -796,6 +796,25 @@ __global__ void basis_split_kernel(const float* __restrict__ basis, int H, int k
     }
 }
 
+// Directions [count, H] f32 as the B operand of the f32 image pass: rows 4k .. 4k + 3
+// hold bf16 hi, mid, lo of direction k0 + k (their sum is the f32 value exactly)
+// and a zero row.
+__global__ void direction_split_kernel(const float* __restrict__ dirs, int H, int k0, int kc,
+                                       __nv_bfloat16* __restrict__ out) {
+    const int total = kc * H;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int k = i / H, j = i - k * H;
+        const float u = dirs[(size_t)(k0 + k) * H + j];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(u);
+        const float r1 = u - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        out[(size_t)(4 * k) * H + j] = hi;
+        out[(size_t)(4 * k + 1) * H + j] = mid;
+        out[(size_t)(4 * k + 2) * H + j] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        out[(size_t)(4 * k + 3) * H + j] = __float2bfloat16_rn(0.f);
+    }
+}
+
 // ------------------------------------------------------- edit image kernel --
 // F = W U^T for ranks [k0, k0 + kc) of the edit, written as the B extension of
 // the margin GEMM: row n of `image` holds [F_hi | F_hi | F_lo] (each `rank` wide)
@@ -815,9 +834,16 @@ constexpr int kImageThreads = 192;
 struct ImageParams {
     int V, k_blocks, n_tiles, np, stages;
     int rank, k0, kc, ext_k;
-    __nv_bfloat16* image;
+    __nv_bfloat16* image;  // extension mode: [V, ext_k] bf16
+    float* out;            // f32 mode: [rank, V] f32, row k = W u_k
     int* status;
 };
+
+// Epilogue forms of edit_image_kernel.
+//   kImageExtension: basis rows interleaved (hi, lo); writes [F_hi | F_hi | F_lo].
+//   kImageF32: direction rows in groups of four (hi, mid, lo, 0), which hold an f32
+//              direction exactly; writes W u_k in f32 (the head image of u_k).
+enum { kImageExtension = 0, kImageF32 = 1 };
 
 __device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v) {
     __align__(16) __nv_bfloat16 b[8];
@@ -826,6 +852,7 @@ __device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v)
     *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(b);
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(kImageThreads, 1)
     edit_image_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_u,
                       const ImageParams p) {
@@ -959,8 +986,35 @@ __global__ void __launch_bounds__(kImageThreads, 1)
             tc_fence_after();
             const int n = tile * kImageM + quarter * 32 + lane;
             const bool live = n < p.V;
-            __nv_bfloat16* dst = p.image + (size_t)(live ? n : 0) * p.ext_k;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * p.np);
+            if constexpr (MODE == kImageF32) {
+                // eight directions per 32-column chunk: columns 4j .. 4j + 3 of direction j
+#pragma unroll 1
+                for (int c = 0; c < p.np / 32; ++c) {
+                    uint32_t r[32];
+                    tc_ld32(taddr + (uint32_t)(c * 32), r);
+                    tc_wait_ld_regs(r);
+                    if (live) {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int k = 8 * c + j;
+                            if (k < kc) {
+                                const float f = (__uint_as_float(r[4 * j + 2]) + __uint_as_float(r[4 * j + 1])) +
+                                                __uint_as_float(r[4 * j]);
+                                p.out[(size_t)(k0 + k) * p.V + n] = f;
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&tmem_empty[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+                continue;
+            }
+            __nv_bfloat16* dst = p.image + (size_t)(live ? n : 0) * p.ext_k;
 #pragma unroll 1
             for (int c = 0; c < p.np / 32; ++c) {
                 uint32_t r[32];
@@ -1136,7 +1190,7 @@ __global__ void readout_init_kernel(unsigned long long* other_key, float* target
 // when it beats the best other, or ties it with a lower index.
 __global__ void readout_finalize_kernel(const unsigned long long* other_key, const float* target_logit,
                                         const uint32_t* targets, int M, double* margin, uint32_t* argmax,
-                                        float* target_out) {
+                                        float* target_out, uint32_t* other_out = nullptr) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= M) return;
     const unsigned long long k = other_key[i];
@@ -1147,6 +1201,77 @@ __global__ void readout_finalize_kernel(const unsigned long long* other_key, con
     if (margin) margin[i] = (double)tv - (double)ov;
     if (argmax) argmax[i] = (tv > ov || (tv == ov && t < oi)) ? t : oi;
     if (target_out) target_out[i] = tv;
+    if (other_out) other_out[i] = oi;
+}
+
+// ------------------------------------------------------ compact readout ----
+// CompactReadout::evaluate (src/diagnosis.rs:643-665) fused with the margin rules:
+// for observation o, z_o = image c_o + baseline_o (image [V, r] f32 row-major, the
+// transposed head images; c_o the observation's (R - I) coordinates; baseline_o its
+// current logits), reduced at once to the target logit and the best other column
+// (packed key, lowest index on ties) instead of being stored.  A block scores
+// kCompactObs observations over a grid-stride share of the vocabulary, so each
+// image row it reads (from L2) serves all of them; baselines stream from HBM once.
+constexpr int kCompactObs = 8;
+constexpr int kCompactThreads = 256;
+
+__global__ void __launch_bounds__(kCompactThreads) compact_margin_kernel(
+    const float* __restrict__ image, const float* __restrict__ baseline, const float* __restrict__ coefficients,
+    const uint32_t* __restrict__ targets, int V, int r, int n, unsigned long long* other_key, float* target_logit,
+    int* status) {
+    __shared__ float cs[kCompactObs][kMaxEditRank];
+    __shared__ unsigned long long red[kCompactThreads / 32][kCompactObs];
+    const int o0 = blockIdx.y * kCompactObs;
+    const int no = min(kCompactObs, n - o0);
+    for (int i = threadIdx.x; i < kCompactObs * r; i += blockDim.x) {
+        const int o = i / r, k = i - o * r;
+        cs[o][k] = o < no ? coefficients[(size_t)(o0 + o) * r + k] : 0.f;
+    }
+    __syncthreads();
+    uint32_t tg[kCompactObs];
+#pragma unroll
+    for (int o = 0; o < kCompactObs; ++o) tg[o] = o < no ? targets[o0 + o] : 0xffffffffu;
+    unsigned long long best[kCompactObs];
+#pragma unroll
+    for (int o = 0; o < kCompactObs; ++o) best[o] = 0ull;
+    bool bad = false;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+        float acc[kCompactObs];
+#pragma unroll
+        for (int o = 0; o < kCompactObs; ++o) acc[o] = 0.f;
+        const float* row = image + (size_t)i * r;
+        for (int k = 0; k < r; ++k) {
+            const float w = __ldg(row + k);
+#pragma unroll
+            for (int o = 0; o < kCompactObs; ++o) acc[o] = fmaf(w, cs[o][k], acc[o]);
+        }
+#pragma unroll
+        for (int o = 0; o < kCompactObs; ++o) {
+            if (o < no) {
+                const float z = acc[o] + __ldcs(baseline + (size_t)(o0 + o) * V + i);
+                bad |= !isfinite(z);
+                if ((uint32_t)i == tg[o]) {
+                    target_logit[o0 + o] = z;
+                } else {
+                    const unsigned long long key = pack_arg(z, (uint32_t)i);
+                    best[o] = key > best[o] ? key : best[o];
+                }
+            }
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 0; o < kCompactObs; ++o) {
+        const unsigned long long b = warp_max_u64(best[o]);
+        if (lane == 0) red[warp][o] = b;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&status[1], 1);
+    __syncthreads();
+    if (threadIdx.x < no) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kCompactThreads / 32; ++w) b = red[w][threadIdx.x] > b ? red[w][threadIdx.x] : b;
+        if (b) atomicMax(&other_key[o0 + threadIdx.x], b);
+    }
 }
 
 // ------------------------------------------------------------ host side ----
@@ -1397,10 +1522,10 @@ int readout_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bi
             const size_t ismem = (size_t)q.stages * stage_bytes + 1024 + (2 * q.stages + 4) * 8 + 16;
             CUtensorMap mu;
             LSX_TRY(make_map(&mu, image_a, width, 2 * (size_t)kc, width * 2, (uint32_t)q.np));
-            LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)ismem),
+            LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel<kImageExtension>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem),
                      "edit image smem attribute");
-            edit_image_kernel<<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
+            edit_image_kernel<kImageExtension><<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
             LSX_CUDA(cudaGetLastError(), "edit image");
         }
         edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, dbasis, ddelta, (int)rank,
@@ -1474,6 +1599,63 @@ int readout_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bi
     return LSX_OK;
 }
 
+// Device scratch head_images_enqueue needs for `count` directions of width H.
+size_t head_images_scratch(size_t count, size_t width) {
+    return align256(count * width * 4) + align256((size_t)kImageMaxN * width * 2) + 256;
+}
+
+// out[k, :] = W u_k (f32) for the f32 directions dirs_host [count, width]: one
+// tcgen05 pass over W per 32 directions (kImageF32).  W is BF16 [vocab, width].
+// Enqueued on ctx->stream; `scratch` holds head_images_scratch() bytes; the host
+// copy of the directions is taken before return.
+int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, size_t width, const float* dirs_host,
+                        size_t count, float* out, void* scratch) {
+    LSX_ENSURE(weight && weight->kind == LSX_BF16 && weight->count == vocab * width, "the head weight must be BF16");
+    LSX_ENSURE(count > 0 && count <= 4096 && width % 8 == 0 && vocab <= 2147483647ull, "check the head image sizes");
+    uint8_t* b = (uint8_t*)scratch;
+    float* dirs = (float*)b;
+    __nv_bfloat16* rows = (__nv_bfloat16*)(b + align256(count * width * 4));
+    int* status = (int*)(b + align256(count * width * 4) + align256((size_t)kImageMaxN * width * 2));
+    cudaStream_t s = ctx->stream;
+    LSX_CUDA(cudaMemcpyAsync(dirs, dirs_host, count * width * 4, cudaMemcpyHostToDevice, s), "direction upload");
+    LSX_CUDA(cudaMemsetAsync(status, 0, 8, s), "status clear");
+    CUtensorMap mw;
+    LSX_TRY(make_map(&mw, weight->data, width, vocab, width * 2, kImageM));
+    const int V = (int)vocab, H = (int)width;
+    const int n_tiles = (V + kImageM - 1) / kImageM;
+    constexpr int kDirs = kImageMaxN / 4;  // directions per pass
+    for (int k0 = 0; k0 < (int)count; k0 += kDirs) {
+        const int kc = std::min(kDirs, (int)count - k0);
+        direction_split_kernel<<<std::min(ctx->sm_count, (kc * H + 255) / 256), 256, 0, s>>>(dirs, H, k0, kc, rows);
+        LSX_CUDA(cudaGetLastError(), "direction split");
+        ImageParams q{};
+        q.V = V;
+        q.k_blocks = (H + RK - 1) / RK;
+        q.n_tiles = n_tiles;
+        q.np = ((4 * kc + 31) / 32) * 32;
+        q.rank = (int)count;
+        q.k0 = k0;
+        q.kc = kc;
+        q.out = out;
+        q.status = status;
+        const int stage_bytes = kImageM * RK * 2 + q.np * RK * 2;
+        q.stages = std::min(8, (int)((200u << 10) / stage_bytes));
+        const size_t ismem = (size_t)q.stages * stage_bytes + 1024 + (2 * q.stages + 4) * 8 + 16;
+        CUtensorMap mu;
+        LSX_TRY(make_map(&mu, rows, width, 4 * (size_t)kc, width * 2, (uint32_t)q.np));
+        LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel<kImageF32>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem),
+                 "head image smem attribute");
+        edit_image_kernel<kImageF32><<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
+        LSX_CUDA(cudaGetLastError(), "head images");
+    }
+    int host_status[2] = {0, 0};
+    LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
+    LSX_CUDA(cudaStreamSynchronize(s), "head images");
+    if (host_status[0] != 0) return fail(LSX_E_CUDA, "head image kernel reported status " + std::to_string(host_status[0]));
+    return LSX_OK;
+}
+
 int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
                            const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
                            const lsx_rotation* rotation, double* margin, uint32_t* argmax, float* target_logit,
@@ -1511,6 +1693,73 @@ int lsx_readout_merge_device(lsx_ctx* ctx, const uint64_t* other_key, const floa
                                                                       target_logit, targets, M, margin_out,
                                                                       argmax_out, target_logit_out);
     LSX_CUDA(cudaGetLastError(), "readout merge");
+    return LSX_OK;
+}
+
+int lsx_compact_margin(lsx_ctx* ctx, const lsx_tensor* image, const lsx_tensor* baseline, size_t vocab,
+                       size_t rank, size_t count, const float* coefficients, const uint32_t* targets,
+                       double* margin_out, uint32_t* other_out, uint32_t* argmax_out) {
+    LSX_ENSURE(ctx && image && baseline && coefficients && targets, "invalid argument");
+    LSX_ENSURE(image->kind == LSX_F32 && baseline->kind == LSX_F32, "the compact image and baselines are F32");
+    LSX_ENSURE(rank >= 1 && rank <= (size_t)kMaxEditRank && vocab > 1 && vocab <= 2147483647ull && count > 0 &&
+                   count <= 2147483647ull,
+               "check the compact readout sizes");
+    LSX_ENSURE(image->count == vocab * rank && baseline->count == count * vocab,
+               "check the compact image and baseline dimensions");
+    for (size_t i = 0; i < count; ++i) LSX_ENSURE(targets[i] < vocab, "check the target token range");
+    for (size_t i = 0; i < count * rank; ++i)
+        LSX_ENSURE(std::isfinite(coefficients[i]), "check the finiteness of the compact coefficients");
+    cudaSetDevice(ctx->device);
+    const size_t n = count;
+    const size_t total = align256(n * rank * 4) + align256(n * 4) + align256(n * 8) + align256(n * 4) +
+                         align256(n * 8) + align256(n * 4) + align256(n * 4) + 256;
+    void* block = nullptr;
+    LSX_TRY(device_alloc(ctx, total, &block));
+    uint8_t* b = (uint8_t*)block;
+    size_t at = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t* p = b + at;
+        at += align256(bytes);
+        return p;
+    };
+    float* d_coef = (float*)take(n * rank * 4);
+    uint32_t* d_targets = (uint32_t*)take(n * 4);
+    unsigned long long* d_keys = (unsigned long long*)take(n * 8);
+    float* d_tlog = (float*)take(n * 4);
+    double* d_margin = (double*)take(n * 8);
+    uint32_t* d_other = (uint32_t*)take(n * 4);
+    uint32_t* d_argmax = (uint32_t*)take(n * 4);
+    int* d_status = (int*)take(16);
+    cudaStream_t s = ctx->stream;
+    int status[2] = {0, 0};
+    cudaError_t e = cudaMemcpyAsync(d_coef, coefficients, n * rank * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_targets, targets, n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        readout_init_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(d_keys, d_tlog, (int)n, d_status, false);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        const int V = (int)vocab;
+        dim3 grid((unsigned)std::min<size_t>((vocab + kCompactThreads * 4 - 1) / (kCompactThreads * 4), 4096),
+                  (unsigned)((n + kCompactObs - 1) / kCompactObs));
+        compact_margin_kernel<<<grid, kCompactThreads, 0, s>>>((const float*)image->data,
+                                                              (const float*)baseline->data, d_coef, d_targets, V,
+                                                              (int)rank, (int)n, d_keys, d_tlog, d_status);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) {
+        readout_finalize_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(d_keys, d_tlog, d_targets, (int)n, d_margin,
+                                                                      d_argmax, nullptr, d_other);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && margin_out) e = cudaMemcpyAsync(margin_out, d_margin, n * 8, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && other_out) e = cudaMemcpyAsync(other_out, d_other, n * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && argmax_out) e = cudaMemcpyAsync(argmax_out, d_argmax, n * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(status, d_status, 8, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    device_release(ctx, block);
+    if (e != cudaSuccess) return fail(LSX_E_CUDA, cuda_message("compact readout", e));
+    if (status[1] != 0) return fail(LSX_E_NONFINITE, "check the finite scores of the compact readout");
     return LSX_OK;
 }
 

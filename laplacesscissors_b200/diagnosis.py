@@ -228,6 +228,8 @@ class CompactReadout:
         self.coordinates = np.stack([np.asarray(c, dtype=np.float64) for c in coordinates], axis=1)  # [rank, n]
         self.vocabulary = vocab
         self.rank = rank
+        self._baseline_block = None  # [n, vocab] for evaluate_margins, uploaded on first use
+        self._baseline_host = baseline
 
     def evaluate(self, gpu: Gpu, rotation: np.ndarray, deadline: Deadline) -> list[np.ndarray]:
         rank = rotation.shape[0]
@@ -241,6 +243,31 @@ class CompactReadout:
                 raise ValueError("check the finite scores of the compact readout")
             out.append(scores)
         return out
+
+    def evaluate_margins(self, gpu: Gpu, rotation: np.ndarray, targets, deadline: Deadline | None = None):
+        """evaluate() reduced on the device to what the joint search reads from each
+        observation's scores (src/diagnosis.rs:790-815): minimum_margin against its
+        target, the competitor other() picks and the first argmax; the V-wide
+        scores are never stored or downloaded (lsx_compact_margin).  Returns
+        (margin f64 [n], other u32 [n], argmax u32 [n])."""
+        if deadline is not None:
+            deadline.check()
+        rank = rotation.shape[0]
+        delta = (rotation - np.eye(rank)) @ self.coordinates  # [rank, n]
+        n = delta.shape[1]
+        if self._baseline_block is None:
+            self._baseline_block = gpu.upload_f32(np.stack([np.asarray(z, dtype=np.float32)
+                                                            for z in self._baseline_host]))
+        coefficients = np.ascontiguousarray(delta.T, dtype=np.float32)  # [n, rank]
+        t = np.ascontiguousarray(targets, dtype=np.uint32)
+        if t.size != n:
+            raise ValueError("one target per observation")
+        margin = np.empty(n, dtype=np.float64)
+        other_ = np.empty(n, dtype=np.uint32)
+        amax = np.empty(n, dtype=np.uint32)
+        check(lib.lsx_compact_margin(gpu.handle, self.image.handle, self._baseline_block.handle, self.vocabulary,
+                                     rank, n, _fp(coefficients), _up(t), _dp(margin), _up(other_), _up(amax)))
+        return margin, other_, amax
 
 
 __all__ = [

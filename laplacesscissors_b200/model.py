@@ -188,6 +188,16 @@ class Model:
         check(lib.lsx_model_head_image(self._h, _dp(v), _fp(out)))
         return out
 
+    def head_images(self, gpu: Gpu, vectors) -> np.ndarray:
+        """head_image for every row of `vectors` [count, hidden] in one tensor-core
+        pass over the lm_head per 32 directions; returns [count, vocab] f32."""
+        v = np.ascontiguousarray(np.atleast_2d(vectors), dtype=np.float64)
+        if v.shape[1] != self.hidden_size:
+            raise ValueError("check the readout direction dimension")
+        out = np.empty((v.shape[0], self.vocab_size()), dtype=np.float32)
+        check(lib.lsx_model_head_images(self._h, _dp(v), v.shape[0], _fp(out)))
+        return out
+
     def head_row(self, gpu: Gpu, token: int) -> np.ndarray:
         out = np.empty(self.hidden_size, dtype=np.float32)
         check(lib.lsx_model_head_row(self._h, int(token), _fp(out)))
