@@ -302,6 +302,40 @@ int lsx_readout_margin_fixed(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_t
                              size_t rows, const uint32_t* targets, double* margin_out,
                              uint32_t* argmax_out, float* target_logit_out);
 
+/* ------------------------------------------------ plane-candidate feasibility -- */
+/* FeasibleSet (src/interval.rs:47-212): the open forbidden intervals of a plane
+   rotation's half-angle tangent t in [-bound, bound], merged as quadratic
+   constraints a t^2 + b t + c >= 0 arrive, with the reference's screening and work
+   counters.  Host code; needs no GPU. */
+typedef struct lsx_feasible lsx_feasible;
+/* FeasibleSet::new: bound in (0, 1e6]. */
+int lsx_feasible_create(double bound, lsx_feasible** out);
+int lsx_feasible_free(lsx_feasible* set);
+/* FeasibleSet::constrain; LSX_E_ARGUMENT for non-finite coefficients. */
+int lsx_feasible_constrain(lsx_feasible* set, double a, double b, double c);
+/* FeasibleSet::is_empty: 1 when no tangent is feasible. */
+int lsx_feasible_is_empty(const lsx_feasible* set);
+/* FeasibleSet::nearest: *found = 0 when empty, else the feasible tangent nearest 0
+   (ties: the smaller magnitude, then the smaller value). */
+int lsx_feasible_nearest(const lsx_feasible* set, double* tangent, int* found);
+/* FeasibleSet::intervals: writes up to `capacity` (lower, upper) pairs and returns
+   how many feasible intervals there are. */
+size_t lsx_feasible_intervals(const lsx_feasible* set, double* out, size_t capacity);
+/* Work counters: constraints, screened, square_roots, inserted_intervals. */
+int lsx_feasible_work(const lsx_feasible* set, uint64_t* work);
+/* The plane candidate's constraint loop (src/diagnosis.rs:1118-1143) into `set`:
+   for each point p (target t_p, frame logits [points x vocab] row p, f64 projections
+   hu_p = u.h_p, hv_p = v.h_p) and each j != t_p, the constraint (c - 2 beta, 2 alpha,
+   c) with du = wu[t] - wu[j], dv = wv[t] - wv[j], alpha = du hv - dv hu,
+   beta = du hu + dv hv, c = z[t] - z[j] - margin - guard (wu, wv the head images of
+   u and v); stops as soon as the set is empty.  Every constraint is formed and
+   screened on the GPU against the current hull; the host merges the rest in the
+   reference's order, so the set and its counters equal the sequential loop's.
+   Host arrays. */
+int lsx_plane_feasible(lsx_ctx* ctx, lsx_feasible* set, const float* wu, const float* wv, size_t vocab,
+                       const float* logits, const uint32_t* targets, const double* hu, const double* hv,
+                       size_t points, double margin, double guard);
+
 /* ---------------------------------------------------- synthetic checkpoints -- */
 /* Seeded N(0, std^2) values rounded to `kind` (BF16 or F32): element i of stream
    `stream` under `seed` is a pure function of (seed, stream, i), so any slice can

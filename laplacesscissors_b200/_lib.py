@@ -106,6 +106,14 @@ SIGNATURES = {
     "lsx_compact_margin": (I, [P, P, P, SZ, SZ, SZ, FP, UP, DP, UP, UP]),
     "lsx_readout_shard_device": (I, [P, P, P, SZ, SZ, SZ, P, I, SZ, P, P, P, P, P, SZ]),
     "lsx_readout_merge_device": (I, [P, P, P, P, SZ, P, P, P]),
+    "lsx_feasible_create": (I, [D, PP]),
+    "lsx_feasible_free": (I, [P]),
+    "lsx_feasible_constrain": (I, [P, D, D, D]),
+    "lsx_feasible_is_empty": (I, [P]),
+    "lsx_feasible_nearest": (I, [P, DP, C.POINTER(I)]),
+    "lsx_feasible_intervals": (SZ, [P, DP, SZ]),
+    "lsx_feasible_work": (I, [P, C.POINTER(C.c_uint64)]),
+    "lsx_plane_feasible": (I, [P, P, FP, FP, SZ, FP, UP, DP, DP, SZ, D, D]),
     "lsx_synth_normal": (I, [U64, U64, U64, SZ, D, I, P]),
     "lsx_synth_uniform_u32": (I, [U64, U64, U64, SZ, U32, UP]),
 }

@@ -43,7 +43,7 @@ def host_compiler() -> list[str]:
 def common_flags() -> list[str]:
     return ARCH + host_compiler() + [
         "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
-        "-Xcompiler", "-fPIC,-fopenmp,-Wall,-Wno-unused-function",
+        "-Xcompiler", "-fPIC,-fopenmp,-Wall,-Wno-unused-function,-ffp-contract=off",
         "-I", str(INCLUDE), "-I", str(CSRC),
     ]
 

@@ -50,6 +50,11 @@ class ModelStruct(C.Structure):
                 ("final_gain", C.c_void_p), ("final_bias", C.c_void_p), ("blocks", C.POINTER(Block))]
 
 
+class FeasibleStruct(C.Structure):
+    _fields_ = [("bound", C.c_double), ("lower", C.c_void_p), ("upper", C.c_void_p), ("count", C.c_size_t),
+                ("capacity", C.c_size_t), ("work", C.c_uint64 * 4)]
+
+
 def _load() -> C.CDLL:
     lib = C.CDLL(str(build()))
     V, SZ, I, D, F = C.c_void_p, C.c_size_t, C.c_int, C.c_double, C.c_float
@@ -74,6 +79,13 @@ def _load() -> C.CDLL:
         "lsxo_embedding": (None, [C.POINTER(ModelStruct), C.c_uint32, V]),
         "lsxo_readout_rows": (None, [V, I, V, SZ, SZ, V, SZ, V, V, V, V, I]),
         "lsxo_version": (C.c_char_p, []),
+        "lsxo_feasible_init": (I, [C.POINTER(FeasibleStruct), D]),
+        "lsxo_feasible_free": (None, [C.POINTER(FeasibleStruct)]),
+        "lsxo_feasible_constrain": (I, [C.POINTER(FeasibleStruct), D, D, D]),
+        "lsxo_feasible_is_empty": (I, [C.POINTER(FeasibleStruct)]),
+        "lsxo_feasible_nearest": (I, [C.POINTER(FeasibleStruct), C.POINTER(D)]),
+        "lsxo_feasible_intervals": (SZ, [C.POINTER(FeasibleStruct), V, SZ]),
+        "lsxo_plane_feasible": (I, [C.POINTER(FeasibleStruct), V, V, SZ, V, V, V, V, SZ, D, D]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -395,3 +407,50 @@ class OracleModel:
 __all__ = ["lib", "OracleModel", "readout_rows", "matvec", "norm", "rope", "attention", "gated", "combine",
            "plane_rotation", "plane_apply", "subspace_apply", "argmax", "other", "minimum_margin", "loss",
            "take_row", "read_checkpoint", "widen", "build"]
+
+
+# ------------------------------------------------------------ FeasibleSet ---
+class Feasible:
+    """src/interval.rs:47-212 (the oracle's C restatement)."""
+
+    def __init__(self, bound: float):
+        self._s = FeasibleStruct()
+        if lib.lsxo_feasible_init(C.byref(self._s), float(bound)) != 0:
+            raise ValueError("the half-angle bound must lie in (0, 1e6]")
+
+    def __del__(self):
+        try:
+            lib.lsxo_feasible_free(C.byref(self._s))
+        except Exception:
+            pass
+
+    def constrain(self, a: float, b: float, c: float) -> None:
+        if lib.lsxo_feasible_constrain(C.byref(self._s), float(a), float(b), float(c)) != 0:
+            raise ValueError("finite quadratic coefficients are required")
+
+    def is_empty(self) -> bool:
+        return bool(lib.lsxo_feasible_is_empty(C.byref(self._s)))
+
+    def nearest(self):
+        t = C.c_double()
+        return t.value if lib.lsxo_feasible_nearest(C.byref(self._s), C.byref(t)) else None
+
+    def intervals(self) -> list[tuple[float, float]]:
+        n = lib.lsxo_feasible_intervals(C.byref(self._s), None, 0)
+        out = np.empty(2 * max(n, 1), dtype=np.float64)
+        lib.lsxo_feasible_intervals(C.byref(self._s), ptr(out), n)
+        return [(float(out[2 * i]), float(out[2 * i + 1])) for i in range(n)]
+
+    def work(self) -> tuple[int, int, int, int]:
+        return tuple(int(x) for x in self._s.work)
+
+    def plane(self, wu, wv, logits, targets, hu, hv, margin: float, guard: float) -> None:
+        """The constraint loop of src/diagnosis.rs:1118-1143 (sequential, on the host)."""
+        wu, wv = f32(wu), f32(wv)
+        z = f32(logits)
+        t = np.ascontiguousarray(targets, dtype=np.uint32)
+        hu = np.ascontiguousarray(hu, dtype=np.float64)
+        hv = np.ascontiguousarray(hv, dtype=np.float64)
+        if lib.lsxo_plane_feasible(C.byref(self._s), ptr(wu), ptr(wv), wu.size, ptr(z), ptr(t), ptr(hu), ptr(hv),
+                                   t.size, float(margin), float(guard)) != 0:
+            raise ValueError("finite quadratic coefficients are required")

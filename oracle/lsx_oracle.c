@@ -411,3 +411,263 @@ void lsxo_readout_rows(const void* head, int kind, const float* bias, size_t voc
     }
     free(z);
 }
+
+
+/* ------------------------------------------------------------ FeasibleSet --
+ * src/interval.rs:47-212.  Every operation below keeps the reference's f64
+ * evaluation order; the Makefile compiles with -ffp-contract=off so that only the
+ * explicit fma() calls (the reference's mul_add) fuse. */
+static int endpoint_cmp(double x, double y) {
+    if (x == y) return 0;
+    /* f64::total_cmp */
+    int64_t a, b;
+    memcpy(&a, &x, 8);
+    memcpy(&b, &y, 8);
+    a ^= (int64_t)(((uint64_t)(a >> 63)) >> 1);
+    b ^= (int64_t)(((uint64_t)(b >> 63)) >> 1);
+    return a < b ? -1 : (a > b ? 1 : 0);
+}
+
+int lsxo_feasible_init(lsxo_feasible* f, double bound) {
+    memset(f, 0, sizeof(*f));
+    if (!(isfinite(bound) && bound > 0. && bound <= 1e6)) return -1;
+    f->bound = bound;
+    return 0;
+}
+
+void lsxo_feasible_free(lsxo_feasible* f) {
+    free(f->lower);
+    free(f->upper);
+    f->lower = f->upper = NULL;
+    f->count = f->capacity = 0;
+}
+
+/* number of keys strictly below x (Endpoint order) */
+static size_t keys_below(const lsxo_feasible* f, double x) {
+    size_t lo = 0, hi = f->count;
+    while (lo < hi) {
+        size_t mid = (lo + hi) / 2;
+        if (endpoint_cmp(f->lower[mid], x) < 0) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+/* FeasibleSet::containing: the forbidden interval with the largest key < x, if x < its upper. */
+static int containing(const lsxo_feasible* f, double x, double* a, double* b) {
+    size_t n = keys_below(f, x);
+    if (n == 0) return 0;
+    if (x < f->upper[n - 1]) {
+        *a = f->lower[n - 1];
+        *b = f->upper[n - 1];
+        return 1;
+    }
+    return 0;
+}
+
+static int hull(const lsxo_feasible* f, double* left, double* right) {
+    double a, b;
+    *left = containing(f, -f->bound, &a, &b) ? b : -f->bound;
+    *right = containing(f, f->bound, &a, &b) ? a : f->bound;
+    return *left <= *right;
+}
+
+int lsxo_feasible_is_empty(const lsxo_feasible* f) {
+    double l, r;
+    return !hull(f, &l, &r);
+}
+
+static void remove_at(lsxo_feasible* f, size_t i) {
+    memmove(f->lower + i, f->lower + i + 1, (f->count - i - 1) * sizeof(double));
+    memmove(f->upper + i, f->upper + i + 1, (f->count - i - 1) * sizeof(double));
+    f->count--;
+}
+
+static void insert_key(lsxo_feasible* f, double a, double b) {
+    size_t i = keys_below(f, a);
+    if (i < f->count && endpoint_cmp(f->lower[i], a) == 0) {  /* BTreeMap::insert replaces the value */
+        f->upper[i] = b;
+        return;
+    }
+    if (f->count == f->capacity) {
+        f->capacity = f->capacity ? 2 * f->capacity : 16;
+        f->lower = (double*)realloc(f->lower, f->capacity * sizeof(double));
+        f->upper = (double*)realloc(f->upper, f->capacity * sizeof(double));
+    }
+    memmove(f->lower + i + 1, f->lower + i, (f->count - i) * sizeof(double));
+    memmove(f->upper + i + 1, f->upper + i, (f->count - i) * sizeof(double));
+    f->lower[i] = a;
+    f->upper[i] = b;
+    f->count++;
+}
+
+static double fmax_rs(double x, double y) { return isnan(x) ? y : (isnan(y) ? x : (x > y ? x : y)); }
+
+static void exclude(lsxo_feasible* f, double a, double b) {
+    if (a >= b || b <= -f->bound || a >= f->bound) return;
+    f->work[3]++;
+    /* the largest key <= a whose interval reaches past a */
+    size_t n = keys_below(f, a);
+    if (n < f->count && endpoint_cmp(f->lower[n], a) == 0) n++;
+    if (n > 0 && f->upper[n - 1] > a) {
+        a = f->lower[n - 1];
+        b = fmax_rs(b, f->upper[n - 1]);
+        remove_at(f, n - 1);
+    }
+    for (;;) {
+        size_t i = keys_below(f, a); /* smallest key >= a */
+        if (i >= f->count || f->lower[i] >= b) break;
+        b = fmax_rs(b, f->upper[i]);
+        remove_at(f, i);
+    }
+    insert_key(f, a, b);
+}
+
+int lsxo_feasible_constrain(lsxo_feasible* f, double a, double b, double c) {
+    if (!(isfinite(a) && isfinite(b) && isfinite(c))) return -1;
+    f->work[0]++;
+    double left, right;
+    if (!hull(f, &left, &right)) return 0;
+    double magnitude = fmax_rs(fmax_rs(fabs(a), fabs(b)), fabs(c));
+    if (magnitude == 0.) {
+        f->work[1]++;
+        return 0;
+    }
+    uint64_t bits;
+    memcpy(&bits, &magnitude, 8);
+    uint64_t exponent = (bits >> 52) & 0x7ff;
+    if (exponent < 1) exponent = 1;
+    uint64_t sbits = exponent << 52;
+    double scale;
+    memcpy(&scale, &sbits, 8);
+    a = a / scale;
+    b = b / scale;
+    c = c / scale;
+    const double eps8 = 8. * 2.220446049250313e-16;
+#define CERTAIN(t)                                                                                   \
+    ((fma(a, (t) * (t), fma(b, (t), c)) >= eps8 * (fabs(a) * (t) * (t) + fabs(b) * fabs(t) + fabs(c))) || \
+     (a == 0. && b == 0. && c >= 0.))
+    int vertex_ok = 1;
+    if (a > 0.) {
+        double vertex = -b / (2. * a);
+        vertex_ok = vertex <= left || vertex >= right || 4. * a * c - b * b >= 0.;
+    }
+    if (CERTAIN(left) && CERTAIN(right) && vertex_ok) {
+        f->work[1]++;
+        return 0;
+    }
+#undef CERTAIN
+    const double inf = INFINITY;
+    if (a == 0.) {
+        if (b > 0.) exclude(f, -inf, -c / b);
+        else if (b < 0.) exclude(f, -c / b, inf);
+        else if (c < 0.) exclude(f, -inf, inf);
+        return 0;
+    }
+    double discriminant = fma(b, b, -4. * a * c);
+    if (discriminant < 0.) {
+        if (a < 0.) exclude(f, -inf, inf);
+    } else if (discriminant == 0.) {
+        if (a < 0.) {
+            double root = -b / (2. * a);
+            exclude(f, -inf, root);
+            exclude(f, root, inf);
+        }
+    } else {
+        f->work[2]++;
+        double first, second;
+        if (b == 0.) {
+            double root = sqrt(-c / a);
+            first = -root;
+            second = root;
+        } else {
+            double q = -0.5 * (b + copysign(sqrt(discriminant), b));
+            first = q / a;
+            second = c / q;
+        }
+        double lo = first < second ? first : second, hi = first < second ? second : first;
+        /* f64::min / f64::max of two non-NaN values */
+        if (a > 0.) {
+            exclude(f, lo, hi);
+        } else {
+            exclude(f, -inf, lo);
+            exclude(f, hi, inf);
+        }
+    }
+    return 0;
+}
+
+/* |x|.total_cmp(|y|).then(x.total_cmp(y)) == Less */
+static int abs_then_value_less(double x, double y) {
+    double ax = fabs(x), ay = fabs(y);
+    int64_t ia, ib;
+    memcpy(&ia, &ax, 8);
+    memcpy(&ib, &ay, 8);
+    if (ia != ib) return ia < ib; /* non-negative doubles order like their bits */
+    int64_t a, b;
+    memcpy(&a, &x, 8);
+    memcpy(&b, &y, 8);
+    a ^= (int64_t)(((uint64_t)(a >> 63)) >> 1);
+    b ^= (int64_t)(((uint64_t)(b >> 63)) >> 1);
+    return a < b;
+}
+
+int lsxo_feasible_nearest(const lsxo_feasible* f, double* t) {
+    double l, r, a, b;
+    if (!hull(f, &l, &r)) return 0;
+    if (!containing(f, 0., &a, &b)) {
+        *t = 0.;
+        return 1;
+    }
+    int have = 0;
+    double best = 0.;
+    double cand[2] = {a, b};
+    for (int i = 0; i < 2; ++i) {
+        if (!(fabs(cand[i]) <= f->bound)) continue;
+        if (!have || abs_then_value_less(cand[i], best)) best = cand[i];
+        have = 1;
+    }
+    if (have) *t = best;
+    return have;
+}
+
+size_t lsxo_feasible_intervals(const lsxo_feasible* f, double* out, size_t capacity) {
+    double cursor = -f->bound;
+    size_t n = 0;
+    for (size_t i = 0; i < f->count; ++i) {
+        if (f->lower[i] >= cursor) {
+            if (n < capacity) {
+                out[2 * n] = cursor;
+                out[2 * n + 1] = f->lower[i] < f->bound ? f->lower[i] : f->bound;
+            }
+            n++;
+        }
+        cursor = fmax_rs(cursor, f->upper[i]);
+        if (cursor > f->bound) return n;
+    }
+    if (n < capacity) {
+        out[2 * n] = cursor;
+        out[2 * n + 1] = f->bound;
+    }
+    return n + 1;
+}
+
+int lsxo_plane_feasible(lsxo_feasible* f, const float* wu, const float* wv, size_t vocab, const float* logits,
+                        const uint32_t* targets, const double* hu, const double* hv, size_t points, double margin,
+                        double guard) {
+    for (size_t p = 0; p < points; ++p) {
+        const float* z = logits + p * vocab;
+        const size_t t = targets[p];
+        for (size_t j = 0; j < vocab; ++j) {
+            if (j == t) continue;
+            const double du = (double)wu[t] - (double)wu[j];
+            const double dv = (double)wv[t] - (double)wv[j];
+            const double alpha = du * hv[p] - dv * hu[p];
+            const double beta = du * hu[p] + dv * hv[p];
+            const double c = (double)z[t] - (double)z[j] - margin - guard;
+            if (lsxo_feasible_constrain(f, c - 2. * beta, 2. * alpha, c) != 0) return -1;
+            if (lsxo_feasible_is_empty(f)) return 0;
+        }
+    }
+    return 0;
+}

@@ -117,6 +117,36 @@ void lsxo_readout_rows(const void* head, int kind, const float* bias, size_t voc
                        const float* inputs, size_t n, const uint32_t* targets, double* margin,
                        uint32_t* argmax, float* target_logit, int threads);
 
+/* FeasibleSet (src/interval.rs:47-212): open forbidden intervals of the half-angle
+   tangent t in [-bound, bound], merged as quadratic constraints a t^2 + b t + c >= 0
+   arrive.  Sorted array of (lower, upper) with the Endpoint order (equal when ==,
+   otherwise f64::total_cmp). */
+typedef struct lsxo_feasible {
+    double bound;
+    double *lower, *upper;
+    size_t count, capacity;
+    uint64_t work[4]; /* constraints, screened, square_roots, inserted_intervals */
+} lsxo_feasible;
+/* 0 on success, -1 for an invalid bound (FeasibleSet::new). */
+int lsxo_feasible_init(lsxo_feasible* f, double bound);
+void lsxo_feasible_free(lsxo_feasible* f);
+/* FeasibleSet::constrain: 0, or -1 for non-finite coefficients. */
+int lsxo_feasible_constrain(lsxo_feasible* f, double a, double b, double c);
+int lsxo_feasible_is_empty(const lsxo_feasible* f);
+/* FeasibleSet::nearest: 1 and *t when some, else 0. */
+int lsxo_feasible_nearest(const lsxo_feasible* f, double* t);
+/* FeasibleSet::intervals: writes up to `capacity` (lower, upper) pairs and returns
+   the number of feasible intervals. */
+size_t lsxo_feasible_intervals(const lsxo_feasible* f, double* out, size_t capacity);
+/* The plane candidate's constraint loop (src/diagnosis.rs:1118-1143): for each point
+   p (target t_p, frame logits z_p [vocab], projections hu_p, hv_p) and each j != t_p,
+   the constraint (c - 2 beta, 2 alpha, c) with du = wu[t] - wu[j], dv = wv[t] - wv[j],
+   alpha = du hv - dv hu, beta = du hu + dv hv, c = z[t] - z[j] - margin - guard, all
+   f64; stops once the set is empty.  0, or -1 on non-finite coefficients. */
+int lsxo_plane_feasible(lsxo_feasible* f, const float* wu, const float* wv, size_t vocab, const float* logits,
+                        const uint32_t* targets, const double* hu, const double* hv, size_t points, double margin,
+                        double guard);
+
 /* Version string of the oracle build. */
 const char* lsxo_version(void);
 
