@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -402,11 +403,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "score8b", "readout_vocab"],
+    ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "score8b", "readout_vocab",
+                                           "plane"],
                     default="all",
                     help="all: the headline line; decode/readout/gemv: one leg only (with --profile); "
                          "long4b: Qwen3-4B decode after a long prompt; score8b: Qwen3-8B teacher-forced scoring; "
-                         "readout_vocab: the validation workload with the lm_head split by rows over the GPUs")
+                         "readout_vocab: the validation workload with the lm_head split by rows over the GPUs; "
+                         "plane: the plane search's constraint loop (GPU-screened) against the oracle's host loop")
     ap.add_argument("--prompt", type=int, default=4096, help="long4b: prompt length")
     ap.add_argument("--cases", type=int, default=64, help="score8b: cases timed (of the 1024-case job)")
     ap.add_argument("--batch", type=int, default=64, help="score8b: cases per lsx_model_score_batch call "
@@ -424,6 +427,8 @@ def main():
         return scoring(args, local)
     if args.workload == "readout_vocab":
         return vocab_readout(args, rank, local, world)
+    if args.workload == "plane":
+        return plane_bench(args, local)
     if args.profile:
         return profile_run(args, local)
     if args.warmup < 3:
@@ -580,6 +585,63 @@ def vocab_readout(args, rank, local, world):
             "gpu_launches": args.steps * 6,
         }))
     dist.close()
+
+
+def plane_bench(args, local, points: int = 64):
+    """The plane search's constraint loop (src/diagnosis.rs:1118-1143) for one plane
+    over the Qwen3-0.6B vocabulary and `points` target points: seeded head images
+    and frame logits with each target 0.2-1.0 above its best competitor, so a few
+    constraints bind and the set stays non-empty (every constraint is evaluated).
+    lsx_plane_feasible (GPU formation and screening, host merge) end to end with
+    host arrays, against the oracle's sequential host loop on the same inputs;
+    constraints per second."""
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200.feasible import FeasibleSet, plane_constraints
+    from oracle import binding as oracle
+    gpu = lsx.Gpu(local)
+    rng = np.random.default_rng(7)
+    V, P = VOCAB, points
+    wu = rng.standard_normal(V).astype(np.float32)
+    wv = rng.standard_normal(V).astype(np.float32)
+    z = (rng.standard_normal((P, V)) * 3).astype(np.float32)
+    t = rng.integers(0, V, P).astype(np.uint32)
+    for p in range(P):
+        z[p, t[p]] = np.float32(z[p].max() + rng.uniform(0.2, 1.0))
+    hu, hv = rng.standard_normal(P) * 3, rng.standard_normal(P) * 3
+    bound_deg, margin, guard = 30.0, 0.1, 0.01
+
+    def ours():
+        f = FeasibleSet.for_angle(bound_deg)
+        plane_constraints(gpu, f, wu, wv, z, t, hu, hv, margin, guard)
+        return f
+
+    for _ in range(max(3, args.warmup)):
+        f = ours()
+    with ClockSampler(local) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            f = ours()
+        dt = (time.perf_counter() - t0) / args.steps
+    constraints = f.work()[0]
+    ref = oracle.Feasible(math.tan(math.radians(bound_deg) / 2.0))
+    t1 = time.perf_counter()
+    ref.plane(wu, wv, z, t, hu, hv, margin, guard)
+    cpu = time.perf_counter() - t1
+    assert ref.work() == f.work() and ref.intervals() == f.intervals() and ref.nearest() == f.nearest()
+    print(json.dumps({
+        "metric": "plane constraints/s (src/diagnosis.rs:1118-1143 loop, one plane)",
+        "value": constraints / dt, "unit": "constraints/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "dtype": "f64 constraints from f32 head images and logits",
+        "data": "synthetic: seeded head images and frame logits, targets 0.2-1.0 above the best competitor",
+        "config": {"workload": f"{P} target points x {V} vocabulary entries, half-angle bound 15 degrees",
+                   "constraints": constraints, "work": f.work(),
+                   "timing": "wall clock around lsx_plane_feasible with host arrays (uploads, screening passes, "
+                             "mask downloads and the host merge)"},
+        "cpu_baseline": {"value": constraints / cpu, "unit": "constraints/s", "cores": 1, "kind": "port",
+                         "sample": "the whole loop once (oracle restatement, sequential as the reference)"},
+        "clocks": clocks.summary(),
+    }))
 
 
 def profile_run(args, local):

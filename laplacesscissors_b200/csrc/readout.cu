@@ -836,6 +836,7 @@ struct ImageParams {
     int rank, k0, kc, ext_k;
     __nv_bfloat16* image;  // extension mode: [V, ext_k] bf16
     float* out;            // f32 mode: [rank, V] f32, row k = W u_k
+    int accumulate;        // f32 mode: out += instead of out =
     int* status;
 };
 
@@ -1001,7 +1002,8 @@ __global__ void __launch_bounds__(kImageThreads, 1)
                             if (k < kc) {
                                 const float f = (__uint_as_float(r[4 * j + 2]) + __uint_as_float(r[4 * j + 1])) +
                                                 __uint_as_float(r[4 * j]);
-                                p.out[(size_t)(k0 + k) * p.V + n] = f;
+                                float* o = p.out + (size_t)(k0 + k) * p.V + n;
+                                *o = p.accumulate ? *o + f : f;
                             }
                         }
                     }
@@ -1078,46 +1080,28 @@ __global__ void __launch_bounds__(kImageThreads, 1)
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem_base) : "memory");
 }
 
-// c = (R - I) U h per hidden row (one warp per row), written as
-// [c_hi | c_lo | c_hi | 0 ...] into the extension block of A; with F32 hidden rows
-// also the bf16 hi/lo planes of the main product.  Each lane holds 8-element
-// slices of h (16-byte loads) and accumulates kRankBlock basis dot products at
-// once; U is read through L1 (every warp of the GPU reads the same rows).
 constexpr int kRankBlock = 16;
 constexpr int kMaxEditRank = 256;
 
+// c = (R - I) U h per hidden row (one warp per row) from the edit coordinates
+// coords[k, row] = U_k . h_row ([rank, M], as the f32 image pass leaves them),
+// written as [c_hi | c_lo | c_hi | 0 ...] into the extension block of A; with F32
+// hidden rows also the bf16 hi/lo planes of the main product (coords NULL: the
+// split only).
 __global__ void __launch_bounds__(256) edit_coefficients_kernel(const void* __restrict__ hidden, int hidden_kind,
-                                                                int M, int H, const float* __restrict__ basis,
+                                                                int M, int H, const float* __restrict__ coords,
                                                                 const float* __restrict__ delta, int rank,
                                                                 __nv_bfloat16* __restrict__ ext_a, int ext_k,
                                                                 __nv_bfloat16* __restrict__ plane_hi,
                                                                 __nv_bfloat16* __restrict__ plane_lo) {
-    __shared__ float coords[8][kMaxEditRank];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x * 8 + warp;
     if (i >= M) return;
-    const int nv = H >> 3;  // 8-element slices per row
-    auto load8 = [&](int v, float (&h)[8]) {
-        if (hidden_kind == LSX_F32) {
-            const float4* src = reinterpret_cast<const float4*>((const float*)hidden + (size_t)i * H) + 2 * v;
-            const float4 a = __ldg(src), b = __ldg(src + 1);
-            h[0] = a.x; h[1] = a.y; h[2] = a.z; h[3] = a.w;
-            h[4] = b.x; h[5] = b.y; h[6] = b.z; h[7] = b.w;
-        } else {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>((const __nv_bfloat16*)hidden + (size_t)i * H) + v);
-            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(b2[e]);
-                h[2 * e] = f.x;
-                h[2 * e + 1] = f.y;
-            }
-        }
-    };
-    if (plane_hi) {
-        for (int v = lane; v < nv; v += 32) {
-            float h[8];
-            load8(v, h);
+    if (plane_hi && hidden_kind == LSX_F32) {
+        const float4* src = reinterpret_cast<const float4*>((const float*)hidden + (size_t)i * H);
+        for (int v = lane; v < (H >> 3); v += 32) {
+            const float4 a = __ldg(src + 2 * v), b = __ldg(src + 2 * v + 1);
+            const float h[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
             __align__(16) __nv_bfloat16 hi[8], lo[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -1128,44 +1112,12 @@ __global__ void __launch_bounds__(256) edit_coefficients_kernel(const void* __re
             reinterpret_cast<uint4*>(plane_lo + (size_t)i * H)[v] = *reinterpret_cast<const uint4*>(lo);
         }
     }
-    if (rank == 0) return;
-    for (int k0 = 0; k0 < rank; k0 += kRankBlock) {
-        float acc[kRankBlock];
-#pragma unroll
-        for (int k = 0; k < kRankBlock; ++k) acc[k] = 0.f;
-        for (int v = lane; v < nv; v += 32) {
-            float h[8];
-            load8(v, h);
-#pragma unroll
-            for (int k = 0; k < kRankBlock; ++k) {
-                if (k0 + k < rank) {
-                    const float4* u = reinterpret_cast<const float4*>(basis + (size_t)(k0 + k) * H) + 2 * v;
-                    const float4 a = __ldg(u), b = __ldg(u + 1);
-                    float d = acc[k];
-                    d = fmaf(a.x, h[0], d);
-                    d = fmaf(a.y, h[1], d);
-                    d = fmaf(a.z, h[2], d);
-                    d = fmaf(a.w, h[3], d);
-                    d = fmaf(b.x, h[4], d);
-                    d = fmaf(b.y, h[5], d);
-                    d = fmaf(b.z, h[6], d);
-                    d = fmaf(b.w, h[7], d);
-                    acc[k] = d;
-                }
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < kRankBlock; ++k) {
-            const float t = warp_allsum(acc[k]);
-            if (lane == 0 && k0 + k < rank) coords[warp][k0 + k] = t;
-        }
-    }
-    __syncwarp();
+    if (!coords) return;
     __nv_bfloat16* dst = ext_a + (size_t)i * ext_k;
     for (int k = 3 * rank + lane; k < ext_k; k += 32) dst[k] = __float2bfloat16_rn(0.f);
     for (int k = lane; k < rank; k += 32) {
         float c = 0.f;
-        for (int q = 0; q < rank; ++q) c = fmaf(delta[k * rank + q], coords[warp][q], c);
+        for (int q = 0; q < rank; ++q) c = fmaf(delta[k * rank + q], coords[(size_t)q * M + i], c);
         const __nv_bfloat16 hi = __float2bfloat16_rn(c);
         const __nv_bfloat16 lo = __float2bfloat16_rn(c - __bfloat162float(hi));
         dst[k] = hi;
@@ -1316,7 +1268,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 
 struct Layout {
-    size_t ext_k, planes_off, planes_bytes, ext_a_off, ext_b_off, basis_off, delta_off, image_a_off, key_off,
+    size_t ext_k, planes_off, planes_bytes, ext_a_off, ext_b_off, basis_off, delta_off, image_a_off, coords_off, key_off,
         tlog_off, status_off, total;
 };
 
@@ -1336,7 +1288,9 @@ Layout layout_for(size_t vocab, size_t width, size_t rows, size_t rank, bool f32
     L.delta_off = at;
     at = align256(at + rank * rank * 4);
     L.image_a_off = at;
-    at = align256(at + 2 * std::min(rank, (size_t)kImageRanks) * width * 2);
+    at = align256(at + (rank ? std::max(2 * std::min(rank, (size_t)kImageRanks), (size_t)kImageMaxN) : 0) * width * 2);
+    L.coords_off = at;
+    at = align256(at + rows * rank * 4);
     L.key_off = at;
     at = align256(at + rows * 8);
     L.tlog_off = at;
@@ -1432,6 +1386,9 @@ size_t readout_workspace_need(size_t vocab, size_t width, size_t rows, size_t ra
     return layout_for(vocab, width, rows, rank, f32_hidden).total;
 }
 
+int image_f32_enqueue(lsx_ctx* ctx, const void* a, size_t rows, size_t width, const float* dirs, size_t count,
+                      float* out, bool accumulate, __nv_bfloat16* split, int* status);
+
 // One vocabulary shard's outputs: per-row partials instead of margins.
 struct ShardOut {
     size_t vocab_offset;
@@ -1525,11 +1482,26 @@ int readout_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bi
             LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel<kImageExtension>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem),
                      "edit image smem attribute");
-            edit_image_kernel<kImageExtension><<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
+            edit_image_kernel<kImageExtension>
+                <<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
             LSX_CUDA(cudaGetLastError(), "edit image");
         }
-        edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, dbasis, ddelta, (int)rank,
-                                                             ext_a, (int)L.ext_k, plane_hi, plane_lo);
+        // Edit coordinates U h of every row ([rank, M] f32) on the tensor cores: the
+        // rows (bf16, or the hi and lo planes of f32 rows) against U as exact
+        // three-term bf16 directions.
+        float* coords = (float*)(ws + L.coords_off);
+        __nv_bfloat16* split = (__nv_bfloat16*)(ws + L.image_a_off);
+        if (f32_hidden) {
+            edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, nullptr, nullptr, 0,
+                                                                 nullptr, 0, plane_hi, plane_lo);
+            LSX_CUDA(cudaGetLastError(), "hidden split");
+            LSX_TRY(image_f32_enqueue(ctx, plane_hi, rows, width, dbasis, rank, coords, false, split, status));
+            LSX_TRY(image_f32_enqueue(ctx, plane_lo, rows, width, dbasis, rank, coords, true, split, status));
+        } else {
+            LSX_TRY(image_f32_enqueue(ctx, hidden, rows, width, dbasis, rank, coords, false, split, status));
+        }
+        edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, coords, ddelta, (int)rank,
+                                                             ext_a, (int)L.ext_k, nullptr, nullptr);
         LSX_CUDA(cudaGetLastError(), "edit coefficients");
     } else if (f32_hidden) {
         edit_coefficients_kernel<<<(M + 7) / 8, 256, 0, s>>>(hidden, hidden_kind, M, H, nullptr, nullptr, 0, nullptr,
@@ -1604,29 +1576,21 @@ size_t head_images_scratch(size_t count, size_t width) {
     return align256(count * width * 4) + align256((size_t)kImageMaxN * width * 2) + 256;
 }
 
-// out[k, :] = W u_k (f32) for the f32 directions dirs_host [count, width]: one
-// tcgen05 pass over W per 32 directions (kImageF32).  W is BF16 [vocab, width].
-// Enqueued on ctx->stream; `scratch` holds head_images_scratch() bytes; the host
-// copy of the directions is taken before return.
-int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, size_t width, const float* dirs_host,
-                        size_t count, float* out, void* scratch) {
-    LSX_ENSURE(weight && weight->kind == LSX_BF16 && weight->count == vocab * width, "the head weight must be BF16");
-    LSX_ENSURE(count > 0 && count <= 4096 && width % 8 == 0 && vocab <= 2147483647ull, "check the head image sizes");
-    uint8_t* b = (uint8_t*)scratch;
-    float* dirs = (float*)b;
-    __nv_bfloat16* rows = (__nv_bfloat16*)(b + align256(count * width * 4));
-    int* status = (int*)(b + align256(count * width * 4) + align256((size_t)kImageMaxN * width * 2));
+// out[k, :] (=|+=) A u_k in f32 for the f32 directions dirs [count, width] (device):
+// one tcgen05 pass over A (BF16 [rows, width]) per 32 directions (kImageF32);
+// `split` holds kImageMaxN x width bf16 for the split directions.  Enqueued only.
+int image_f32_enqueue(lsx_ctx* ctx, const void* a, size_t rows, size_t width, const float* dirs, size_t count,
+                      float* out, bool accumulate, __nv_bfloat16* split, int* status) {
+    LSX_ENSURE(count > 0 && width % 8 == 0 && rows > 0 && rows <= 2147483647ull, "check the image sizes");
     cudaStream_t s = ctx->stream;
-    LSX_CUDA(cudaMemcpyAsync(dirs, dirs_host, count * width * 4, cudaMemcpyHostToDevice, s), "direction upload");
-    LSX_CUDA(cudaMemsetAsync(status, 0, 8, s), "status clear");
     CUtensorMap mw;
-    LSX_TRY(make_map(&mw, weight->data, width, vocab, width * 2, kImageM));
-    const int V = (int)vocab, H = (int)width;
+    LSX_TRY(make_map(&mw, a, width, rows, width * 2, kImageM));
+    const int V = (int)rows, H = (int)width;
     const int n_tiles = (V + kImageM - 1) / kImageM;
     constexpr int kDirs = kImageMaxN / 4;  // directions per pass
     for (int k0 = 0; k0 < (int)count; k0 += kDirs) {
         const int kc = std::min(kDirs, (int)count - k0);
-        direction_split_kernel<<<std::min(ctx->sm_count, (kc * H + 255) / 256), 256, 0, s>>>(dirs, H, k0, kc, rows);
+        direction_split_kernel<<<std::min(ctx->sm_count, (kc * H + 255) / 256), 256, 0, s>>>(dirs, H, k0, kc, split);
         LSX_CUDA(cudaGetLastError(), "direction split");
         ImageParams q{};
         q.V = V;
@@ -1637,22 +1601,42 @@ int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, si
         q.k0 = k0;
         q.kc = kc;
         q.out = out;
+        q.accumulate = accumulate ? 1 : 0;
         q.status = status;
         const int stage_bytes = kImageM * RK * 2 + q.np * RK * 2;
         q.stages = std::min(8, (int)((200u << 10) / stage_bytes));
         const size_t ismem = (size_t)q.stages * stage_bytes + 1024 + (2 * q.stages + 4) * 8 + 16;
         CUtensorMap mu;
-        LSX_TRY(make_map(&mu, rows, width, 4 * (size_t)kc, width * 2, (uint32_t)q.np));
+        LSX_TRY(make_map(&mu, split, width, 4 * (size_t)kc, width * 2, (uint32_t)q.np));
         LSX_CUDA(cudaFuncSetAttribute((const void*)edit_image_kernel<kImageF32>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ismem),
-                 "head image smem attribute");
+                 "image smem attribute");
         edit_image_kernel<kImageF32><<<std::min(n_tiles, ctx->sm_count), kImageThreads, ismem, s>>>(mw, mu, q);
-        LSX_CUDA(cudaGetLastError(), "head images");
+        LSX_CUDA(cudaGetLastError(), "f32 image");
     }
+    return LSX_OK;
+}
+
+// out[k, :] = W u_k (f32) for the f32 directions dirs_host [count, width]: one
+// tcgen05 pass over W per 32 directions (kImageF32).  W is BF16 [vocab, width].
+// Runs on ctx->stream and waits for it; `scratch` holds head_images_scratch() bytes.
+int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, size_t width, const float* dirs_host,
+                        size_t count, float* out, void* scratch) {
+    LSX_ENSURE(weight && weight->kind == LSX_BF16 && weight->count == vocab * width, "the head weight must be BF16");
+    LSX_ENSURE(count > 0 && count <= 4096 && width % 8 == 0 && vocab <= 2147483647ull, "check the head image sizes");
+    uint8_t* b = (uint8_t*)scratch;
+    float* dirs = (float*)b;
+    __nv_bfloat16* split = (__nv_bfloat16*)(b + align256(count * width * 4));
+    int* status = (int*)(b + align256(count * width * 4) + align256((size_t)kImageMaxN * width * 2));
+    cudaStream_t s = ctx->stream;
+    LSX_CUDA(cudaMemcpyAsync(dirs, dirs_host, count * width * 4, cudaMemcpyHostToDevice, s), "direction upload");
+    LSX_CUDA(cudaMemsetAsync(status, 0, 8, s), "status clear");
+    LSX_TRY(image_f32_enqueue(ctx, weight->data, vocab, width, dirs, count, out, false, split, status));
     int host_status[2] = {0, 0};
     LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
     LSX_CUDA(cudaStreamSynchronize(s), "head images");
-    if (host_status[0] != 0) return fail(LSX_E_CUDA, "head image kernel reported status " + std::to_string(host_status[0]));
+    if (host_status[0] != 0)
+        return fail(LSX_E_CUDA, "head image kernel reported status " + std::to_string(host_status[0]));
     return LSX_OK;
 }
 
