@@ -404,12 +404,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "score8b", "readout_vocab",
-                                           "plane"],
+                                           "plane", "attribution"],
                     default="all",
                     help="all: the headline line; decode/readout/gemv: one leg only (with --profile); "
                          "long4b: Qwen3-4B decode after a long prompt; score8b: Qwen3-8B teacher-forced scoring; "
                          "readout_vocab: the validation workload with the lm_head split by rows over the GPUs; "
-                         "plane: the plane search's constraint loop (GPU-screened) against the oracle's host loop")
+                         "plane: the plane search's constraint loop (GPU-screened) against the oracle's host loop; "
+                         "attribution: the integrated-softmax credits over the vocabulary")
     ap.add_argument("--prompt", type=int, default=4096, help="long4b: prompt length")
     ap.add_argument("--cases", type=int, default=64, help="score8b: cases timed (of the 1024-case job)")
     ap.add_argument("--batch", type=int, default=64, help="score8b: cases per lsx_model_score_batch call "
@@ -429,6 +430,8 @@ def main():
         return vocab_readout(args, rank, local, world)
     if args.workload == "plane":
         return plane_bench(args, local)
+    if args.workload == "attribution":
+        return attribution_bench(args, local)
     if args.profile:
         return profile_run(args, local)
     if args.warmup < 3:
@@ -640,6 +643,47 @@ def plane_bench(args, local, points: int = 64):
                              "mask downloads and the host merge)"},
         "cpu_baseline": {"value": constraints / cpu, "unit": "constraints/s", "cores": 1, "kind": "port",
                          "sample": "the whole loop once (oracle restatement, sequential as the reference)"},
+        "clocks": clocks.summary(),
+    }))
+
+
+def attribution_bench(args, local, points: int = 64, panels: int = 64):
+    """integrated_probabilities (src/attribution.rs:79-123) over the Qwen3-0.6B
+    vocabulary: `points` points with seeded before/after logits, `panels` Simpson
+    panels, through lsx_integrated_credits with host arrays (uploads and the credit
+    download inside the timing).  Unit: softmax evaluations (points x (panels + 1) x
+    vocabulary exponentials) per second; the oracle's sequential f64 loop on one
+    point is the CPU baseline."""
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import attribution
+    from oracle import binding as oracle
+    gpu = lsx.Gpu(local)
+    rng = np.random.default_rng(7)
+    V, P = VOCAB, points
+    before = (rng.standard_normal((P, V)) * 3).astype(np.float32)
+    after = (before + rng.standard_normal((P, V)).astype(np.float32) * 0.5).astype(np.float32)
+    targets = rng.integers(0, V, P).astype(np.uint32)
+    weights = np.full(P, 1.0 / P)
+    for _ in range(max(3, args.warmup)):
+        attribution.integrated_credits(gpu, before, after, targets, weights, panels)
+    with ClockSampler(local) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            credits, _, _ = attribution.integrated_credits(gpu, before, after, targets, weights, panels)
+        dt = (time.perf_counter() - t0) / args.steps
+    evals = P * (panels + 1) * V
+    t1 = time.perf_counter()
+    ref, _ = oracle.integrated_credits(before[:1], after[:1], targets[:1], weights[:1], panels)
+    cpu = time.perf_counter() - t1
+    print(json.dumps({
+        "metric": "integrated-softmax evaluations/s (src/attribution.rs:79-123)",
+        "value": evals / dt, "unit": "exp/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "dtype": "f64",
+        "data": "synthetic: seeded before/after logits over the Qwen3-0.6B vocabulary",
+        "config": {"workload": f"{P} points x {panels} panels x {V} vocabulary rows",
+                   "timing": "wall clock around lsx_integrated_credits with host arrays (2 x 39 MB uploaded)"},
+        "cpu_baseline": {"value": (panels + 1) * V / cpu, "unit": "exp/s", "cores": 1, "kind": "port",
+                         "sample": "one point (oracle, sequential f64 as the reference)"},
         "clocks": clocks.summary(),
     }))
 

@@ -336,6 +336,21 @@ int lsx_plane_feasible(lsx_ctx* ctx, lsx_feasible* set, const float* wu, const f
                        const float* logits, const uint32_t* targets, const double* hu, const double* hv,
                        size_t points, double margin, double guard);
 
+/* ------------------------------------------------------------ attribution -- */
+/* integrated_probabilities (src/attribution.rs:79-123) with the losses analyze needs
+   (src/attribution.rs:49-78), on the GPU in f64.  For point p (before/after logits
+   rows of [points x vocab] f32, target, weight >= 0) the softmax along the chord
+   z(t) = (1 - t) before + t after is integrated by Simpson's rule over `panels`
+   (even) panels; credits_out[j] = -sum_p weight_p (after_pj - before_pj) integral_pj.
+   For the `row_count` rows given, gradients_out[p * row_count + r] = integral_p at
+   rows[r] (may be NULL).  losses_out (may be NULL) is [points x (2 + row_count)]:
+   loss(before_p), loss(after_p), then restored_loss(after_p, rows[r], before_p[rows[r]],
+   target_p).  Host arrays; sums over the vocabulary are reassociated, so results
+   match the sequential loop to f64 rounding. */
+int lsx_integrated_credits(lsx_ctx* ctx, const float* before, const float* after, const uint32_t* targets,
+                           const double* weights, size_t points, size_t vocab, size_t panels, double* credits_out,
+                           const uint32_t* rows, size_t row_count, double* gradients_out, double* losses_out);
+
 /* ---------------------------------------------------- synthetic checkpoints -- */
 /* Seeded N(0, std^2) values rounded to `kind` (BF16 or F32): element i of stream
    `stream` under `seed` is a pure function of (seed, stream, i), so any slice can

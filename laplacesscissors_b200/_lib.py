@@ -114,6 +114,7 @@ SIGNATURES = {
     "lsx_feasible_intervals": (SZ, [P, DP, SZ]),
     "lsx_feasible_work": (I, [P, C.POINTER(C.c_uint64)]),
     "lsx_plane_feasible": (I, [P, P, FP, FP, SZ, FP, UP, DP, DP, SZ, D, D]),
+    "lsx_integrated_credits": (I, [P, P, P, UP, DP, SZ, SZ, SZ, DP, UP, SZ, DP, DP]),
     "lsx_synth_normal": (I, [U64, U64, U64, SZ, D, I, P]),
     "lsx_synth_uniform_u32": (I, [U64, U64, U64, SZ, U32, UP]),
 }

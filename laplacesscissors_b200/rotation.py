@@ -91,6 +91,11 @@ class SubspaceRotation:
         delta = (self.transform - np.eye(self.rank)) @ self.coordinates(h)
         return h + delta @ self.basis
 
+    def delta_row(self, row) -> np.ndarray:  # src/response.rs:78-90
+        x = self.coordinates(row)
+        delta = (self.transform.T - np.eye(self.rank)) @ x
+        return delta @ self.basis
+
     def subspace(self) -> "SubspaceRotation":
         return self
 

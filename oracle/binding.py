@@ -86,6 +86,8 @@ def _load() -> C.CDLL:
         "lsxo_feasible_nearest": (I, [C.POINTER(FeasibleStruct), C.POINTER(D)]),
         "lsxo_feasible_intervals": (SZ, [C.POINTER(FeasibleStruct), V, SZ]),
         "lsxo_plane_feasible": (I, [C.POINTER(FeasibleStruct), V, V, SZ, V, V, V, V, SZ, D, D]),
+        "lsxo_restored_loss": (D, [V, SZ, SZ, F, C.c_uint32]),
+        "lsxo_integrated_credits": (None, [V, V, V, V, SZ, SZ, SZ, V, V]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -454,3 +456,22 @@ class Feasible:
         if lib.lsxo_plane_feasible(C.byref(self._s), ptr(wu), ptr(wv), wu.size, ptr(z), ptr(t), ptr(hu), ptr(hv),
                                    t.size, float(margin), float(guard)) != 0:
             raise ValueError("finite quadratic coefficients are required")
+
+
+# ------------------------------------------------------------ attribution ---
+def restored_loss(z, row: int, original: float, target: int) -> float:
+    z = f32(z)
+    return float(lib.lsxo_restored_loss(ptr(z), z.size, int(row), float(original), int(target)))
+
+
+def integrated_credits(before, after, targets, weights, panels: int, gradients: bool = False):
+    """src/attribution.rs:79-123: (credits [vocab], integrals [points, vocab] or None)."""
+    b, a = f32(before), f32(after)
+    points, vocab = b.shape
+    t = np.ascontiguousarray(targets, dtype=np.uint32)
+    w = np.ascontiguousarray(weights, dtype=np.float64)
+    credits = np.empty(vocab, dtype=np.float64)
+    grads = np.empty((points, vocab), dtype=np.float64) if gradients else None
+    lib.lsxo_integrated_credits(ptr(b), ptr(a), ptr(t), ptr(w), points, vocab, int(panels), ptr(credits),
+                                ptr(grads))
+    return credits, grads

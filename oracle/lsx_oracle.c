@@ -671,3 +671,49 @@ int lsxo_plane_feasible(lsxo_feasible* f, const float* wu, const float* wv, size
     }
     return 0;
 }
+
+
+/* ------------------------------------------------------------ attribution --
+ * src/attribution.rs:61-123, in the reference's f64 order (sequential sums,
+ * -ffp-contract=off). */
+double lsxo_restored_loss(const float* z, size_t n, size_t row, float original, uint32_t target) {
+    double maximum = -INFINITY;
+    for (size_t j = 0; j < n; ++j) maximum = fmax_rs(maximum, (double)(j == row ? original : z[j]));
+    double total = 0.0;
+    for (size_t j = 0; j < n; ++j) total += exp((double)(j == row ? original : z[j]) - maximum);
+    return maximum + log(total) - (double)(row == target ? original : z[target]);
+}
+
+void lsxo_integrated_credits(const float* before, const float* after, const uint32_t* targets,
+                             const double* weights, size_t points, size_t vocab, size_t panels, double* credits,
+                             double* gradients) {
+    double* integral = (double*)malloc(vocab * sizeof(double));
+    double* prob = (double*)malloc(vocab * sizeof(double));
+    for (size_t j = 0; j < vocab; ++j) credits[j] = 0.0;
+    for (size_t p = 0; p < points; ++p) {
+        const float* b = before + p * vocab;
+        const float* a = after + p * vocab;
+        for (size_t j = 0; j < vocab; ++j) integral[j] = 0.0;
+        for (size_t k = 0; k <= panels; ++k) {
+            const double t = (double)k / (double)panels;
+            double maximum = -INFINITY;
+            for (size_t j = 0; j < vocab; ++j) {
+                prob[j] = (double)b[j] * (1. - t) + (double)a[j] * t;
+                maximum = fmax_rs(maximum, prob[j]);
+            }
+            double total = 0.0;
+            for (size_t j = 0; j < vocab; ++j) {
+                prob[j] = exp(prob[j] - maximum);
+                total += prob[j];
+            }
+            const double weight = (k == 0 || k == panels ? 1. : (k % 2 == 0 ? 2. : 4.)) / (3. * (double)panels);
+            for (size_t j = 0; j < vocab; ++j)
+                integral[j] += weight * (prob[j] / total - (j == targets[p] ? 1. : 0.));
+        }
+        for (size_t j = 0; j < vocab; ++j)
+            credits[j] -= weights[p] * ((double)a[j] - (double)b[j]) * integral[j];
+        if (gradients) memcpy(gradients + p * vocab, integral, vocab * sizeof(double));
+    }
+    free(integral);
+    free(prob);
+}

@@ -147,6 +147,15 @@ int lsxo_plane_feasible(lsxo_feasible* f, const float* wu, const float* wv, size
                         const uint32_t* targets, const double* hu, const double* hv, size_t points, double margin,
                         double guard);
 
+/* restored_loss (src/attribution.rs:61-78): loss of z with z[row] replaced by `original`. */
+double lsxo_restored_loss(const float* z, size_t n, size_t row, float original, uint32_t target);
+/* integrated_probabilities (src/attribution.rs:79-123), sequential f64 as the
+   reference: credits [vocab] and, when non-NULL, the per-point integrals
+   gradients [points x vocab]. */
+void lsxo_integrated_credits(const float* before, const float* after, const uint32_t* targets,
+                             const double* weights, size_t points, size_t vocab, size_t panels, double* credits,
+                             double* gradients);
+
 /* Version string of the oracle build. */
 const char* lsxo_version(void);
 
