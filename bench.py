@@ -425,7 +425,7 @@ def main():
     if args.workload == "long4b":
         return long_decode(args, local)
     if args.workload == "score8b":
-        return scoring(args, local)
+        return scoring(args, rank, local, world)
     if args.workload == "readout_vocab":
         return vocab_readout(args, rank, local, world)
     if args.workload == "plane":
@@ -788,7 +788,7 @@ def decoder_flops_per_token(cfg: dict) -> int:
     return 2 * cfg["layers"] * (H * (q + 2 * kv) + q * H + 3 * H * I)
 
 
-def scoring(args, local):
+def scoring(args, rank, local, world):
     """Qwen3-8B (36 layers, hidden 4096, 32/8 heads, I 12288, untied lm_head)
     teacher-forced case scoring: cases of 64 random prompt ids and 8 random
     answer ids + EOS.  --batch > 0: lsx_model_score_batch over --batch cases at a
@@ -798,7 +798,9 @@ def scoring(args, local):
     reference).  --cases of the 1024-case job are timed end to end (host arrays in,
     losses and argmaxes out)."""
     if args.batch > 0:
-        return scoring_batched(args, local)
+        return scoring_batched(args, rank, local, world)
+    if rank != 0:  # the token-by-token form is a single-GPU measurement
+        return
     import laplacesscissors_b200 as lsx
     from laplacesscissors_b200 import synth
     gpu = lsx.Gpu(local)
@@ -845,13 +847,21 @@ def scoring(args, local):
     }))
 
 
-def scoring_batched(args, local):
+def scoring_batched(args, rank, local, world):
+    """Batched scoring; with several ranks (torchrun) each rank scores its own
+    --cases cases of the job (cases are independent: case sharding, weak scaling)
+    and the time is the maximum over ranks."""
     import laplacesscissors_b200 as lsx
     from laplacesscissors_b200 import synth
+    dist = Dist(world, local)
     gpu = lsx.Gpu(local)
     cfg = synth.QWEN3_8B
     eos, V, P, n = 151645, cfg["vocab"], 64, 9
+    if rank == 0:
+        model_checkpoint("QWEN3_8B")  # one writer; the other ranks read it after the barrier
+    dist.barrier()
     model = lsx.Model.load(model_checkpoint("QWEN3_8B"), gpu, 80)
+    first_case = 100 + rank * args.cases
 
     def batch(first, count):
         prompts = np.stack([synth.uniform_u32(7, 1000 + i, P, V) for i in range(first, first + count)])
@@ -862,19 +872,24 @@ def scoring_batched(args, local):
     for i in range(max(1, args.warmup)):
         model.score_batch(*batch(10_000 + i * B, B))
     gpu.synchronize()
-    inputs = [batch(100 + i, min(B, args.cases - i)) for i in range(0, args.cases, B)]
+    inputs = [batch(first_case + i, min(B, args.cases - i)) for i in range(0, args.cases, B)]
+    dist.barrier()
     with ClockSampler(gpu.device) as clocks:
         t0 = time.perf_counter()
         for pr, tg in inputs:
             model.score_batch(pr, tg)
-        dt = time.perf_counter() - t0
+        dt = dist.max(time.perf_counter() - t0)
+    dist.close()
+    if rank != 0:
+        return
     tokens = P + n - 1
     flops_case = decoder_flops_per_token(cfg) * tokens + 2 * n * V * cfg["hidden"]
-    tflops = args.cases * flops_case / dt / 1e12
+    tflops = world * args.cases * flops_case / dt / 1e12
     peaks = measured_peaks()
     print(json.dumps({
         "metric": "teacher-forced scoring cases/s (Qwen3-8B, 64-token prompt + 9 scored targets)",
-        "value": args.cases / dt, "unit": "cases/s", "n_gpus": 1, "steps": args.cases, "warmup": args.warmup,
+        "value": world * args.cases / dt, "unit": "cases/s", "n_gpus": world, "steps": args.cases,
+        "warmup": args.warmup, "scaling": "weak (case shards)",
         "ms_per_step": dt / args.cases * 1e3, "higher_is_better": True,
         "dtype": "bf16 weights; f32 activations entering the tensor cores as two bf16 terms (f32 accumulate); "
                  "f64 loss",
@@ -882,12 +897,12 @@ def scoring_batched(args, local):
         "config": {"workload": "Qwen3-8B teacher-forced scoring, 64 prompt + 8 answer + EOS per case",
                    "cases_timed": args.cases, "cases_per_call": B, "job_cases": 1024, "fed_tokens_per_case": tokens,
                    "timing": "wall clock around lsx_model_score_batch calls (host buffers in and out)"},
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": tflops / peaks["bf16_tflops"],
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / (world * peaks["bf16_tflops"]),
                      "scope": f"algorithmic {flops_case / 1e12:.3f} TFLOP per case (2 x decoder parameters x 72 "
                               "fed tokens + the lm_head on 9 rows); the two-term activations double the "
                               "tensor-core work, so 0.5 of peak is this path's ceiling"},
-        "job_seconds_estimate": 1024 / (args.cases / dt),
+        "job_seconds_estimate": 1024 / (world * args.cases / dt),
         "clocks": clocks.summary(),
     }))
 
