@@ -109,6 +109,13 @@ cudaError_t launch_rotate(cudaStream_t s, const float* h, const float* u, const 
                           size_t width, float* out);
 cudaError_t launch_all_finite(cudaStream_t s, const float* x, size_t n, int* flag);
 
+// ---- large host <-> device copies through the context's pinned staging (runtime.cu) ----
+// staged_upload: enqueued on ctx->stream; returns once the host data has been
+// consumed.  staged_download: returns once the host holds the data (synchronises
+// ctx->stream).  Copies below 8 MiB go directly.
+int staged_upload(lsx_ctx* ctx, void* dst, const void* src, size_t bytes);
+int staged_download(lsx_ctx* ctx, void* dst, const void* src, size_t bytes);
+
 // ---- head images on the tensor cores (readout.cu) ----
 size_t head_images_scratch(size_t count, size_t width);
 int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, size_t width, const float* dirs_host,

@@ -1416,9 +1416,7 @@ int lsx_model_generate(lsx_model* m, const uint32_t* prompt, size_t prompt_lengt
         LSX_K(cudaMemcpyAsync(tokens_out, m->d_tokens, n * 4, cudaMemcpyDeviceToHost, s), "token download");
         if (hidden_frames)
             LSX_K(cudaMemcpyAsync(hidden_frames, m->d_frames, n * H * 4, cudaMemcpyDeviceToHost, s), "frames");
-        if (logits_frames)
-            LSX_K(cudaMemcpyAsync(logits_frames, m->d_frames + maximum * H, n * V * 4, cudaMemcpyDeviceToHost, s),
-                  "frames");
+        if (logits_frames) LSX_TRY(staged_download(m->ctx, logits_frames, m->d_frames + maximum * H, n * V * 4));
         LSX_K(cudaStreamSynchronize(s), "generate");
         if (m->host_state->nonfinite) return fail(LSX_E_NONFINITE, "check the finiteness of the model outputs");
         *generated = n;
@@ -1503,10 +1501,10 @@ int lsx_model_score(lsx_model* m, const uint32_t* prompt, size_t prompt_length, 
                 e = cudaMemcpyAsync(argmax_out, m->d_tokens, count * 4, cudaMemcpyDeviceToHost, s);
             if (e == cudaSuccess && hidden_frames)
                 e = cudaMemcpyAsync(hidden_frames, m->d_frames, count * H * 4, cudaMemcpyDeviceToHost, s);
-            if (e == cudaSuccess && logits_frames)
-                e = cudaMemcpyAsync(logits_frames, m->d_frames + count * H, count * V * 4, cudaMemcpyDeviceToHost, s);
             if (e == cudaSuccess) e = cudaStreamSynchronize(s);
             if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("score", e));
+            if (rc == LSX_OK && logits_frames)
+                rc = staged_download(m->ctx, logits_frames, m->d_frames + count * H, count * V * 4);
         }
         device_release(m->ctx, block);
         if (rc != LSX_OK) return rc;

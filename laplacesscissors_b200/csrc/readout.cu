@@ -1789,8 +1789,9 @@ int lsx_readout_margin(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor*
     cudaStream_t s = ctx->stream;
     int status[2] = {0, 0};
     int rc = LSX_OK;
-    cudaError_t e = cudaMemcpyAsync(d_hidden, hidden, hbytes, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d_targets, targets, rows * 4, cudaMemcpyHostToDevice, s);
+    rc = staged_upload(ctx, d_hidden, hidden, hbytes);
+    cudaError_t e = cudaSuccess;
+    if (rc == LSX_OK) e = cudaMemcpyAsync(d_targets, targets, rows * 4, cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) rc = fail(LSX_E_CUDA, cuda_message("readout upload", e));
     if (rc == LSX_OK)
         rc = readout_margin_enqueue(ctx, weight, bias, vocab, width, d_hidden, hidden_kind, rows, d_targets, rotation,

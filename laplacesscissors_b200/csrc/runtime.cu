@@ -4,6 +4,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -113,6 +114,89 @@ int lsx_ctx::staging(size_t bytes, void** out) {
     *out = pinned;
     return LSX_OK;
 }
+
+namespace lsx {
+namespace {
+
+constexpr size_t kStageChunk = size_t(4) << 20;  // bytes per staged piece (two in flight)
+
+// memcpy with the host's threads (pageable source or destination, pinned other side).
+void parallel_copy(void* dst, const void* src, size_t bytes) {
+    constexpr size_t kPiece = size_t(256) << 10;
+    const long long pieces = (long long)((bytes + kPiece - 1) / kPiece);
+#pragma omp parallel for schedule(static) if (pieces > 1)
+    for (long long i = 0; i < pieces; ++i) {
+        const size_t off = (size_t)i * kPiece;
+        std::memcpy((uint8_t*)dst + off, (const uint8_t*)src + off, std::min(kPiece, bytes - off));
+    }
+}
+
+}  // namespace
+
+int staged_upload(lsx_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    if (bytes < 2 * kStageChunk) {
+        LSX_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream), "host to device copy");
+        return LSX_OK;
+    }
+    void* pin = nullptr;
+    LSX_TRY(ctx->staging(2 * kStageChunk, &pin));
+    cudaEvent_t done[2];
+    LSX_CUDA(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming), "staging event");
+    LSX_CUDA(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming), "staging event");
+    cudaError_t e = cudaSuccess;
+    size_t i = 0;
+    for (size_t off = 0; off < bytes && e == cudaSuccess; off += kStageChunk, ++i) {
+        const size_t len = std::min(kStageChunk, bytes - off);
+        uint8_t* half = (uint8_t*)pin + (i & 1) * kStageChunk;
+        if (i >= 2) e = cudaEventSynchronize(done[i & 1]);  // that half's previous copy has left it
+        if (e != cudaSuccess) break;
+        parallel_copy(half, (const uint8_t*)src + off, len);
+        e = cudaMemcpyAsync((uint8_t*)dst + off, half, len, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(done[i & 1], ctx->stream);
+    }
+    // the staging buffer is free again once the last copies have left it
+    if (e == cudaSuccess) e = cudaEventSynchronize(done[(i - 1) & 1]);
+    if (e == cudaSuccess && i >= 2) e = cudaEventSynchronize(done[i & 1]);
+    cudaEventDestroy(done[0]);
+    cudaEventDestroy(done[1]);
+    if (e != cudaSuccess) return fail(LSX_E_CUDA, cuda_message("staged host to device copy", e));
+    return LSX_OK;
+}
+
+int staged_download(lsx_ctx* ctx, void* dst, const void* src, size_t bytes) {
+    if (bytes < 2 * kStageChunk) {
+        LSX_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "device to host copy");
+        LSX_CUDA(cudaStreamSynchronize(ctx->stream), "device to host copy");
+        return LSX_OK;
+    }
+    void* pin = nullptr;
+    LSX_TRY(ctx->staging(2 * kStageChunk, &pin));
+    cudaEvent_t done[2];
+    LSX_CUDA(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming), "staging event");
+    LSX_CUDA(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming), "staging event");
+    const size_t n = (bytes + kStageChunk - 1) / kStageChunk;
+    auto issue = [&](size_t i) {
+        const size_t off = i * kStageChunk, len = std::min(kStageChunk, bytes - off);
+        cudaError_t r = cudaMemcpyAsync((uint8_t*)pin + (i & 1) * kStageChunk, (const uint8_t*)src + off, len,
+                                        cudaMemcpyDeviceToHost, ctx->stream);
+        return r == cudaSuccess ? cudaEventRecord(done[i & 1], ctx->stream) : r;
+    };
+    cudaError_t e = issue(0);
+    for (size_t i = 0; i < n && e == cudaSuccess; ++i) {
+        if (i + 1 < n) e = issue(i + 1);  // the next piece lands while this one is copied out
+        if (e == cudaSuccess) e = cudaEventSynchronize(done[i & 1]);
+        if (e != cudaSuccess) break;
+        const size_t off = i * kStageChunk;
+        parallel_copy((uint8_t*)dst + off, (uint8_t*)pin + (i & 1) * kStageChunk, std::min(kStageChunk, bytes - off));
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaEventDestroy(done[0]);
+    cudaEventDestroy(done[1]);
+    if (e != cudaSuccess) return fail(LSX_E_CUDA, cuda_message("staged device to host copy", e));
+    return LSX_OK;
+}
+
+}  // namespace lsx
 
 using namespace lsx;
 

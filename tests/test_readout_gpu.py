@@ -174,3 +174,33 @@ def test_compact_readout_matches_oracle(gpu, oracle):
     bad[2][7] = np.inf
     with pytest.raises(ValueError):
         diagnosis.CompactReadout(gpu, images, bad, coordinates).evaluate(gpu, q, diagnosis.Deadline(60.0))
+
+
+def test_host_entry_large_upload_matches_device_entry(gpu):
+    """Host rows above the staging threshold (10.6 MB of f32, three pieces, the
+    last one partial) give the same margins as the device-pointer entry."""
+    import ctypes as C
+
+    import torch
+
+    from laplacesscissors_b200._lib import F32, check, lib
+    V, H, n = 4099, 1024, 2600
+    w, _, targets = problem(V, H, n)
+    hidden = synth.normal_f32(8, 1, n * H).reshape(n, H)
+    weight = gpu.upload_raw(w, BF16)
+    margin, amax, tl = diagnosis.readout_margin(gpu, weight, None, V, H, hidden, targets)
+    dev = torch.device("cuda", gpu.device)
+    h = torch.from_numpy(hidden).to(dev)
+    t = torch.from_numpy(targets.astype(np.uint32).view(np.int32)).to(dev)
+    ws = torch.empty(lib.lsx_readout_workspace_bytes(V, H, n, None), dtype=torch.uint8, device=dev)
+    out = torch.empty(n * 16, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
+    base = out.data_ptr()
+    check(lib.lsx_readout_margin_device(gpu.handle, weight.handle, None, V, H, C.c_void_p(h.data_ptr()), F32, n,
+                                        C.c_void_p(t.data_ptr()), None, C.c_void_p(base), C.c_void_p(base + n * 8),
+                                        C.c_void_p(base + n * 12), C.c_void_p(ws.data_ptr()), ws.numel()))
+    gpu.synchronize()
+    raw = out.cpu().numpy()
+    assert np.array_equal(margin, raw[: n * 8].view(np.float64))
+    assert np.array_equal(amax, raw[n * 8: n * 12].view(np.uint32))
+    assert np.array_equal(tl, raw[n * 12:].view(np.float32))
