@@ -742,6 +742,8 @@ def long_decode(args, local):
     model = lsx.Model.load(model_checkpoint("QWEN3_4B"), gpu, P + args.warmup + args.steps + 8)
     prompt = synth.prompt_tokens(7, P, cfg["vocab"])
     stream, event = cuda_timer(gpu)
+    model.generate(prompt, 1)  # warm-up: buffers, tensor maps and kernel modules
+    model.reset()
     t0 = time.perf_counter()
     tokens, _, _ = model.generate(prompt, 1)
     prefill_s = time.perf_counter() - t0
@@ -774,7 +776,8 @@ def long_decode(args, local):
                      "scope": f"{step_bytes / 1e9:.3f} GB per step (weights + f32 KV at the mean context)"},
         "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s,
                     "tflops": decoder_flops_per_token(cfg) * (P - 1) / prefill_s / 1e12,
-                    "note": "lsx_model_generate wall clock: the first P - 1 tokens in one batched forward "
+                    "note": "lsx_model_generate wall clock after one warm-up call: the first P - 1 tokens in one "
+                            "batched forward "
                             "(tcgen05 GEMMs, causal attention, KV cache filled), the last through the decode "
                             "engine; LSX_PREFILL_MIN=0 feeds the prompt token by token as the reference"},
         "clocks": clocks.summary(),

@@ -92,6 +92,32 @@ __global__ void rms_planes_kernel(const float* __restrict__ x, const int* __rest
     __shared__ float red[32];
     const size_t r = blockIdx.x;
     const float* xr = x + (size_t)(rows ? rows[r] : (int)r) * H;
+    if ((H & 3) == 0 && !out) {  // 16-byte loads, 8-byte plane stores
+        const float4* x4 = reinterpret_cast<const float4*>(xr);
+        const float4* g4 = reinterpret_cast<const float4*>(gain);
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < (H >> 2); i += blockDim.x) {
+            const float4 v = x4[i];
+            ss = fmaf(v.x, v.x, ss);
+            ss = fmaf(v.y, v.y, ss);
+            ss = fmaf(v.z, v.z, ss);
+            ss = fmaf(v.w, v.w, ss);
+        }
+        const float inverse = rsqrtf(block_sum(ss, red) / (float)H + eps);
+        for (int i = threadIdx.x; i < (H >> 2); i += blockDim.x) {
+            const float4 v = x4[i], g = g4[i];
+            const float y[4] = {v.x * inverse * g.x, v.y * inverse * g.y, v.z * inverse * g.z, v.w * inverse * g.w};
+            __align__(8) __nv_bfloat16 h4[4], l4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                h4[e] = __float2bfloat16_rn(y[e]);
+                l4[e] = __float2bfloat16_rn(y[e] - __bfloat162float(h4[e]));
+            }
+            *reinterpret_cast<uint2*>(hi + r * H + 4 * i) = *reinterpret_cast<const uint2*>(h4);
+            *reinterpret_cast<uint2*>(lo + r * H + 4 * i) = *reinterpret_cast<const uint2*>(l4);
+        }
+        return;
+    }
     float ss = 0.f;
     for (int i = threadIdx.x; i < H; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
     const float inverse = rsqrtf(block_sum(ss, red) / (float)H + eps);
@@ -262,10 +288,167 @@ __global__ void causal_attention_kernel(const float* __restrict__ qkv, int M, in
     for (int j = 0; j < DPL; ++j) split_store(hi, lo, o + lane + 32 * j, acc[j] / l);
 }
 
+// The same attention with the keys and values staged in shared memory: a block
+// takes one case, one KV group and kQT consecutive query rows (one warp per row);
+// each kKT-key tile of the group's K and V is loaded once and serves every warp,
+// and each warp carries all R query heads of the group, so a tile is read once per
+// warp instead of once per (row, head) from L2.  Per (row, head) the arithmetic is
+// that of causal_attention_kernel (the same key batches in the same order), so the
+// outputs are identical.
+constexpr int kQT = 8;   // query rows per block
+constexpr int kKT = 32;  // keys per staged tile (a multiple of the 8-key batch)
+
+template <int DPL, int R>
+__global__ void __launch_bounds__(32 * kQT, 1) causal_attention_tiled_kernel(const float* __restrict__ qkv, int M,
+                                                                          int T, int QH, int KVH, float scale,
+                                                                          __nv_bfloat16* __restrict__ hi,
+                                                                          __nv_bfloat16* __restrict__ lo) {
+    constexpr int D = DPL * 32;
+    constexpr int PB = 8, LPV = 32 / PB;
+    __shared__ float ks[kKT * D], vs[kKT * D];
+    const int qtiles = (T + kQT - 1) / kQT;
+    int bid = blockIdx.x;
+    const int qt = bid % qtiles;
+    bid /= qtiles;
+    const int g = bid % KVH, c = bid / KVH;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = qt * kQT + warp;  // query position within the case
+    const bool active = t < T;
+    const int first = c * T;
+    const size_t stride = (size_t)(QH + 2 * KVH) * D;
+    const float* kbase = qkv + (size_t)QH * D + (size_t)g * D;
+    const float* vbase = kbase + (size_t)KVH * D;
+    float q[R][DPL], mx[R], l[R], acc[R][DPL];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        mx[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            q[i][j] = active ? qkv[(size_t)(first + t) * stride + (size_t)(g * R + i) * D + lane + 32 * j] : 0.f;
+            acc[i][j] = 0.f;
+        }
+    }
+    const int my_b = lane / LPV;
+    const int kv_end = min(T, qt * kQT + kQT);  // keys the block's last row needs
+    for (int k0 = 0; k0 < kv_end; k0 += kKT) {
+        __syncthreads();  // every warp is done with the previous tile
+        for (int i = threadIdx.x; i < kKT * D; i += blockDim.x) {
+            const int sk = k0 + i / D, col = i % D;
+            const size_t row = (size_t)(first + (sk < T ? sk : T - 1)) * stride + col;
+            ks[i] = kbase[row];
+            vs[i] = vbase[row];
+        }
+        __syncthreads();
+        if (!active) continue;
+        for (int s0 = k0; s0 < k0 + kKT && s0 <= t; s0 += PB) {
+            float kv[PB][DPL], vv[PB][DPL];
+#pragma unroll
+            for (int b = 0; b < PB; ++b) {
+                const int sk = (s0 + b <= t ? s0 + b : t) - k0;
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) {
+                    kv[b][j] = ks[sk * D + lane + 32 * j];
+                    vv[b][j] = vs[sk * D + lane + 32 * j];
+                }
+            }
+            const bool valid = s0 + my_b <= t;
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                float sc[PB];
+#pragma unroll
+                for (int b = 0; b < PB; ++b) {
+                    float x = 0.f;
+#pragma unroll
+                    for (int j = 0; j < DPL; ++j) x = fmaf(q[i][j], kv[b][j], x);
+                    sc[b] = x;
+                }
+#pragma unroll
+                for (int cnt = PB, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+                    const bool up = (lane & off) != 0;
+#pragma unroll
+                    for (int e = 0; e < cnt / 2; ++e) {
+                        const float keep = up ? sc[e + cnt / 2] : sc[e];
+                        const float send = up ? sc[e] : sc[e + cnt / 2];
+                        sc[e] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                    }
+                }
+                for (int off = LPV / 2; off > 0; off >>= 1) sc[0] += __shfl_xor_sync(0xffffffffu, sc[0], off);
+                const float sv = valid ? sc[0] * scale : -INFINITY;
+                float mb = sv;
+                for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+                const float mn = fmaxf(mx[i], mb);
+                const float carry = expf(mx[i] - mn);
+                const float p = valid ? expf(sv - mn) : 0.f;
+                float ps = (lane % LPV) == 0 ? p : 0.f;
+                for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+                l[i] = l[i] * carry + ps;
+#pragma unroll
+                for (int j = 0; j < DPL; ++j) acc[i][j] *= carry;
+#pragma unroll
+                for (int b = 0; b < PB; ++b) {
+                    const float pb = __shfl_sync(0xffffffffu, p, b * LPV);
+#pragma unroll
+                    for (int j = 0; j < DPL; ++j) acc[i][j] = fmaf(pb, vv[b][j], acc[i][j]);
+                }
+                mx[i] = mn;
+            }
+        }
+    }
+    if (!active) return;
+    const int m = first + t;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const size_t o = (size_t)m * QH * D + (size_t)(g * R + i) * D;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) split_store(hi, lo, o + lane + 32 * j, acc[i][j] / l[i]);
+    }
+}
+
+// Tiled attention when the group ratio has an instantiation (q and the
+// accumulators of all R heads stay in registers); false otherwise.
+template <int DPL>
+bool launch_attention_tiled(cudaStream_t s, const float* qkv, int M, int T, int QH, int KVH, float scale,
+                            __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const int R = QH / KVH;
+    const int blocks = (M / T) * KVH * ((T + kQT - 1) / kQT);
+    if (M % T != 0 || QH % KVH != 0) return false;
+    if (R == 1) causal_attention_tiled_kernel<DPL, 1><<<blocks, 32 * kQT, 0, s>>>(qkv, M, T, QH, KVH, scale, hi, lo);
+    else if (R == 2) causal_attention_tiled_kernel<DPL, 2><<<blocks, 32 * kQT, 0, s>>>(qkv, M, T, QH, KVH, scale, hi, lo);
+    else if (R == 4 && DPL <= 4)
+        causal_attention_tiled_kernel<DPL, 4><<<blocks, 32 * kQT, 0, s>>>(qkv, M, T, QH, KVH, scale, hi, lo);
+    else return false;
+    return true;
+}
+
 // A planes of act(gate) * up from the interleaved [g0 u0 g1 u1 ...] rows.
+// Four features per thread (two 16-byte loads, 8-byte plane stores) when I % 4 == 0.
 __global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, int I, int kind,
                                     __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t step = (size_t)gridDim.x * blockDim.x;
+    if ((I & 3) == 0) {
+        const size_t quads = total >> 2;
+        const int per_row = I >> 2;
+        for (size_t q = (size_t)blockIdx.x * blockDim.x + threadIdx.x; q < quads; q += step) {
+            const size_t m = q / per_row;
+            const int f = (int)(q - m * per_row) * 4;
+            const float4* src = reinterpret_cast<const float4*>(gu + m * 2 * I + 2 * f);
+            const float4 a = src[0], b = src[1];  // (g0 u0 g1 u1) (g2 u2 g3 u3)
+            const float v[4] = {act_fn(a.x, kind) * a.y, act_fn(a.z, kind) * a.w, act_fn(b.x, kind) * b.y,
+                                act_fn(b.z, kind) * b.w};
+            __align__(8) __nv_bfloat16 h4[4], l4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                h4[e] = __float2bfloat16_rn(v[e]);
+                l4[e] = __float2bfloat16_rn(v[e] - __bfloat162float(h4[e]));
+            }
+            const size_t o = m * I + f;
+            *reinterpret_cast<uint2*>(hi + o) = *reinterpret_cast<const uint2*>(h4);
+            *reinterpret_cast<uint2*>(lo + o) = *reinterpret_cast<const uint2*>(l4);
+        }
+        return;
+    }
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
         const size_t m = i / I, f = i % I;
         const float2 v = *reinterpret_cast<const float2*>(gu + m * 2 * I + 2 * f);
         split_store(hi, lo, i, act_fn(v.x, kind) * v.y);
@@ -489,13 +672,15 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
         if (D == 128) {
             qk_rope_kernel<4><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
                                                                          Ly.k_gain, c.qk_eps, rope);
-            causal_attention_kernel<4><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, c.scale,
-                                                                                  hi, lo);
+            if (!launch_attention_tiled<4>(s, work, M, (int)T, QH, KVH, c.scale, hi, lo))
+                causal_attention_kernel<4><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH,
+                                                                                      c.scale, hi, lo);
         } else if (D == 64) {
             qk_rope_kernel<2><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
                                                                          Ly.k_gain, c.qk_eps, rope);
-            causal_attention_kernel<2><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, c.scale,
-                                                                                  hi, lo);
+            if (!launch_attention_tiled<2>(s, work, M, (int)T, QH, KVH, c.scale, hi, lo))
+                causal_attention_kernel<2><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH,
+                                                                                      c.scale, hi, lo);
         } else {
             qk_rope_kernel<8><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
                                                                          Ly.k_gain, c.qk_eps, rope);
