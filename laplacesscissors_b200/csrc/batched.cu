@@ -405,6 +405,232 @@ __global__ void __launch_bounds__(32 * kQT, 1) causal_attention_tiled_kernel(con
     }
 }
 
+// ---- tensor-core attention for head_dim 128 -------------------------------
+// Flash-style causal attention on mma.sync (bf16 inputs, f32 accumulation): a
+// block takes one case, one KV group and 16 query positions, one warp per query
+// head of the group.  f32 operands enter as two bf16 terms (hi + lo, 16
+// significant bits), and each product is formed as hi.hi + hi.lo + lo.hi, so S =
+// Q K^T and O = P V keep about 16 bits like the batched GEMMs.  K and V^T tiles of
+// kFaKeys keys are staged in shared memory once per block (split into hi/lo) and
+// serve every warp; S stays in registers and becomes the A operand of P V
+// directly (the m16n8 accumulator layout is the m16k16 operand layout).  The
+// online softmax (running row maximum and sum, rescaled output) follows
+// kernels/ops.py:88-99 per key tile.
+constexpr int kFaD = 128;
+constexpr int kFaKeys = 64;
+constexpr int kFaKStride = kFaD + 8;     // bf16 per staged K row (padding: conflict-free fragment loads)
+constexpr int kFaVStride = kFaKeys + 8;  // bf16 per staged V^T row
+
+__device__ __forceinline__ uint32_t pack_bf16x2(__nv_bfloat16 lo_half, __nv_bfloat16 hi_half) {
+    return (uint32_t)__bfloat16_as_ushort(lo_half) | ((uint32_t)__bfloat16_as_ushort(hi_half) << 16);
+}
+// (x, y) -> packed bf16 hi terms and lo terms
+__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat16 hx = __float2bfloat16_rn(x), hy = __float2bfloat16_rn(y);
+    hi = pack_bf16x2(hx, hy);
+    lo = pack_bf16x2(__float2bfloat16_rn(x - __bfloat162float(hx)), __float2bfloat16_rn(y - __bfloat162float(hy)));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(256, 1) causal_attention_mma_kernel(const float* __restrict__ qkv, int M, int T,
+                                                                     int QH, int KVH, float scale,
+                                                                     __nv_bfloat16* __restrict__ hi,
+                                                                     __nv_bfloat16* __restrict__ lo) {
+    extern __shared__ __align__(16) __nv_bfloat16 fa_smem[];
+    __nv_bfloat16* k_hi = fa_smem;                        // [kFaKeys][kFaKStride]
+    __nv_bfloat16* k_lo = k_hi + kFaKeys * kFaKStride;
+    __nv_bfloat16* v_hi = k_lo + kFaKeys * kFaKStride;    // V^T [kFaD][kFaVStride]
+    __nv_bfloat16* v_lo = v_hi + kFaD * kFaVStride;
+    const int R = QH / KVH;
+    const int qtiles = (T + 15) / 16;
+    int bid = blockIdx.x;
+    const int qt = bid % qtiles;
+    bid /= qtiles;
+    const int g = bid % KVH, c = bid / KVH;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = g * R + warp;
+    const int first = c * T, q0 = qt * 16;
+    const int r = lane >> 2, cq = (lane & 3) * 2;  // fragment row and column pair
+    const size_t stride = (size_t)(QH + 2 * KVH) * kFaD;
+    const float* kbase = qkv + (size_t)QH * kFaD + (size_t)g * kFaD;
+    const float* vbase = kbase + (size_t)KVH * kFaD;
+
+    // Q fragments (hi, lo) for the 16 query rows of head h: 8 k-steps of 16 dims.
+    uint32_t qa_hi[8][4], qa_lo[8][4];
+    {
+        const int ra = min(q0 + r, T - 1), rb = min(q0 + r + 8, T - 1);
+        const float* qa = qkv + (size_t)(first + ra) * stride + (size_t)h * kFaD;
+        const float* qb = qkv + (size_t)(first + rb) * stride + (size_t)h * kFaD;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const int d0 = kk * 16 + cq;
+            const float2 x0 = *reinterpret_cast<const float2*>(qa + d0);
+            const float2 x1 = *reinterpret_cast<const float2*>(qb + d0);
+            const float2 x2 = *reinterpret_cast<const float2*>(qa + d0 + 8);
+            const float2 x3 = *reinterpret_cast<const float2*>(qb + d0 + 8);
+            split2(x0.x, x0.y, qa_hi[kk][0], qa_lo[kk][0]);
+            split2(x1.x, x1.y, qa_hi[kk][1], qa_lo[kk][1]);
+            split2(x2.x, x2.y, qa_hi[kk][2], qa_lo[kk][2]);
+            split2(x3.x, x3.y, qa_hi[kk][3], qa_lo[kk][3]);
+        }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows r and r + 8
+    const int q_a = q0 + r, q_b = q0 + r + 8;
+    const int key_end = min(T, q0 + 16);
+    for (int k0 = 0; k0 < key_end; k0 += kFaKeys) {
+        __syncthreads();  // the previous tile is no longer read
+        for (int i = threadIdx.x; i < kFaKeys * (kFaD / 2); i += blockDim.x) {
+            const int key = i / (kFaD / 2), d = (i % (kFaD / 2)) * 2;
+            const int src = first + min(k0 + key, T - 1);
+            const float2 kv = *reinterpret_cast<const float2*>(kbase + (size_t)src * stride + d);
+            const float2 vv = *reinterpret_cast<const float2*>(vbase + (size_t)src * stride + d);
+            uint32_t kh, kl;
+            split2(kv.x, kv.y, kh, kl);
+            *reinterpret_cast<uint32_t*>(k_hi + key * kFaKStride + d) = kh;
+            *reinterpret_cast<uint32_t*>(k_lo + key * kFaKStride + d) = kl;
+            const __nv_bfloat16 v0 = __float2bfloat16_rn(vv.x), v1 = __float2bfloat16_rn(vv.y);
+            v_hi[d * kFaVStride + key] = v0;
+            v_hi[(d + 1) * kFaVStride + key] = v1;
+            v_lo[d * kFaVStride + key] = __float2bfloat16_rn(vv.x - __bfloat162float(v0));
+            v_lo[(d + 1) * kFaVStride + key] = __float2bfloat16_rn(vv.y - __bfloat162float(v1));
+        }
+        __syncthreads();
+        if (warp >= R) continue;
+        // S = Q K^T over this tile: 8 n-tiles of 8 keys.
+        float sc[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+            const int key = nt * 8 + r;  // B fragment column (key) of this lane
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const int d0 = kk * 16 + cq;
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + key * kFaKStride + d0);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + key * kFaKStride + d0 + 8);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + key * kFaKStride + d0);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + key * kFaKStride + d0 + 8);
+                mma_bf16(sc[nt], qa_lo[kk], bh0, bh1);
+                mma_bf16(sc[nt], qa_hi[kk], bl0, bl1);
+                mma_bf16(sc[nt], qa_hi[kk], bh0, bh1);
+            }
+        }
+        // causal mask, scale, running maxima of rows r and r + 8
+        float tile_a = -INFINITY, tile_b = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int key = k0 + nt * 8 + cq + e;
+                sc[nt][e] = key <= q_a && key < T ? sc[nt][e] * scale : -INFINITY;
+                sc[nt][2 + e] = key <= q_b && key < T ? sc[nt][2 + e] * scale : -INFINITY;
+                tile_a = fmaxf(tile_a, sc[nt][e]);
+                tile_b = fmaxf(tile_b, sc[nt][2 + e]);
+            }
+        }
+        tile_a = fmaxf(tile_a, __shfl_xor_sync(0xffffffffu, tile_a, 1));
+        tile_a = fmaxf(tile_a, __shfl_xor_sync(0xffffffffu, tile_a, 2));
+        tile_b = fmaxf(tile_b, __shfl_xor_sync(0xffffffffu, tile_b, 1));
+        tile_b = fmaxf(tile_b, __shfl_xor_sync(0xffffffffu, tile_b, 2));
+        const float mn_a = fmaxf(m_a, tile_a), mn_b = fmaxf(m_b, tile_b);
+        const float carry_a = expf(m_a - mn_a), carry_b = expf(m_b - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
+        float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                sc[nt][e] = expf(sc[nt][e] - mn_a);
+                sc[nt][2 + e] = expf(sc[nt][2 + e] - mn_b);
+                sum_a += sc[nt][e];
+                sum_b += sc[nt][2 + e];
+            }
+        }
+        l_a = l_a * carry_a + sum_a;
+        l_b = l_b * carry_b + sum_b;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= carry_a;
+            o[n][1] *= carry_a;
+            o[n][2] *= carry_b;
+            o[n][3] *= carry_b;
+        }
+        // O += P V: P's accumulator tiles (2j, 2j + 1) form the A operand of k-step j.
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t pa_hi[4], pa_lo[4];
+            split2(sc[2 * j][0], sc[2 * j][1], pa_hi[0], pa_lo[0]);
+            split2(sc[2 * j][2], sc[2 * j][3], pa_hi[1], pa_lo[1]);
+            split2(sc[2 * j + 1][0], sc[2 * j + 1][1], pa_hi[2], pa_lo[2]);
+            split2(sc[2 * j + 1][2], sc[2 * j + 1][3], pa_hi[3], pa_lo[3]);
+#pragma unroll
+            for (int n = 0; n < 16; ++n) {
+                const int d = n * 8 + r;  // B fragment column (dim) of this lane
+                const int kb = j * 16 + cq;
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + d * kFaVStride + kb);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + d * kFaVStride + kb + 8);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + d * kFaVStride + kb);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + d * kFaVStride + kb + 8);
+                mma_bf16(o[n], pa_lo, bh0, bh1);
+                mma_bf16(o[n], pa_hi, bl0, bl1);
+                mma_bf16(o[n], pa_hi, bh0, bh1);
+            }
+        }
+    }
+    if (warp >= R) return;
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+        const int d = n * 8 + cq;
+        if (q_a < T) {
+            const size_t at = (size_t)(first + q_a) * QH * kFaD + (size_t)h * kFaD + d;
+            uint32_t hh, ll;
+            split2(o[n][0] / l_a, o[n][1] / l_a, hh, ll);
+            *reinterpret_cast<uint32_t*>(hi + at) = hh;
+            *reinterpret_cast<uint32_t*>(lo + at) = ll;
+        }
+        if (q_b < T) {
+            const size_t at = (size_t)(first + q_b) * QH * kFaD + (size_t)h * kFaD + d;
+            uint32_t hh, ll;
+            split2(o[n][2] / l_b, o[n][3] / l_b, hh, ll);
+            *reinterpret_cast<uint32_t*>(hi + at) = hh;
+            *reinterpret_cast<uint32_t*>(lo + at) = ll;
+        }
+    }
+}
+
+constexpr size_t kFaSmem = (size_t)(2 * kFaKeys * kFaKStride + 2 * kFaD * kFaVStride) * 2;
+
+// Tensor-core attention when head_dim is 128 and a group has at most eight query heads.
+bool launch_attention_mma(cudaStream_t s, const float* qkv, int M, int T, int QH, int KVH, int D, float scale,
+                          __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    if (D != kFaD || QH % KVH != 0 || QH / KVH > 8 || M % T != 0) return false;
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute((const void*)causal_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kFaSmem) != cudaSuccess)
+            return false;
+        configured = true;
+    }
+    const int R = QH / KVH;
+    const int blocks = (M / T) * KVH * ((T + 15) / 16);
+    causal_attention_mma_kernel<<<blocks, 32 * std::max(R, 4), kFaSmem, s>>>(qkv, M, T, QH, KVH, scale, hi, lo);
+    return true;
+}
+
 // Tiled attention when the group ratio has an instantiation (q and the
 // accumulators of all R heads stay in registers); false otherwise.
 template <int DPL>
@@ -672,7 +898,8 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
         if (D == 128) {
             qk_rope_kernel<4><<<qk_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH, Ly.q_gain,
                                                                          Ly.k_gain, c.qk_eps, rope);
-            if (!launch_attention_tiled<4>(s, work, M, (int)T, QH, KVH, c.scale, hi, lo))
+            if (!launch_attention_mma(s, work, M, (int)T, QH, KVH, D, c.scale, hi, lo) &&
+                !launch_attention_tiled<4>(s, work, M, (int)T, QH, KVH, c.scale, hi, lo))
                 causal_attention_kernel<4><<<at_blocks, 32 * warps_per_block, 0, s>>>(work, M, (int)T, QH, KVH,
                                                                                       c.scale, hi, lo);
         } else if (D == 64) {
