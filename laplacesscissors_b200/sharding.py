@@ -99,18 +99,25 @@ def shard_partials(logits: np.ndarray, targets: np.ndarray, v0: int) -> tuple[np
 def merge_partials_(keys, target_logit, group=None) -> None:
     """In-place max-merge of vocabulary-shard partials across `group`: `keys` is an
     int64 tensor holding the bits of the packed unsigned keys, `target_logit` f32.
-    The keys are compared as unsigned 64-bit integers, so the sign bit is flipped
-    around a signed all-reduce MAX.  Runs on the tensors' device (NCCL for CUDA
-    tensors, gloo on CPU) and on the current stream."""
+    One all-reduce MAX over [keys | target logits] as signed int64: the keys with
+    their sign bit flipped (so signed order is their unsigned order), the target
+    logits as their f32 total-order keys (non-negative, so the maximum key is the
+    maximum logit).  Runs on the tensors' device (NCCL for CUDA tensors, gloo on
+    CPU) and on the current stream."""
     import torch
     import torch.distributed as dist
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return
+    n = keys.numel()
     flip = torch.tensor(-(1 << 63), dtype=torch.int64, device=keys.device)
-    keys.bitwise_xor_(flip)
-    dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
-    keys.bitwise_xor_(flip)
-    dist.all_reduce(target_logit, op=dist.ReduceOp.MAX, group=group)
+    bits = target_logit.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    order = torch.where(bits >= 0x80000000, bits ^ 0xFFFFFFFF, bits | 0x80000000)
+    both = torch.cat([keys ^ flip, order])
+    dist.all_reduce(both, op=dist.ReduceOp.MAX, group=group)
+    keys.copy_(both[:n] ^ flip)
+    order = both[n:]
+    bits = torch.where(order >= 0x80000000, order & 0x7FFFFFFF, order ^ 0xFFFFFFFF)
+    target_logit.copy_(bits.to(torch.int32).view(torch.float32))
 
 
 def merge_vocab_partials(keys: np.ndarray, target_logit: np.ndarray, targets: np.ndarray, group=None):
