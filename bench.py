@@ -856,13 +856,22 @@ def scoring_batched(args, rank, local, world):
     and the time is the maximum over ranks."""
     import laplacesscissors_b200 as lsx
     from laplacesscissors_b200 import synth
+    # One writer for the 16 GB checkpoint, before the process group exists (writing it
+    # takes longer than a collective may wait); the other ranks wait for its marker.
+    marker = Path(tempfile.gettempdir()) / "lsx-bench-qwen3_8b-seed7.complete"
+    if rank == 0:
+        model_checkpoint("QWEN3_8B")
+        marker.touch()
+    else:
+        t_wait = time.monotonic()
+        while not marker.exists():
+            if time.monotonic() - t_wait > 1800:
+                raise RuntimeError("the checkpoint writer did not finish")
+            time.sleep(1.0)
     dist = Dist(world, local)
     gpu = lsx.Gpu(local)
     cfg = synth.QWEN3_8B
     eos, V, P, n = 151645, cfg["vocab"], 64, 9
-    if rank == 0:
-        model_checkpoint("QWEN3_8B")  # one writer; the other ranks read it after the barrier
-    dist.barrier()
     model = lsx.Model.load(model_checkpoint("QWEN3_8B"), gpu, 80)
     first_case = 100 + rank * args.cases
 
