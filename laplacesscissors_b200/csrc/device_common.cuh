@@ -88,21 +88,6 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return p;
 }
 
-// L2 policy for data that should outlive streamed data in L2.
-__device__ __forceinline__ uint64_t l2_evict_last_policy() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-
-// Prefetch `bytes` (a multiple of 16, 16-byte aligned) of this GPU's memory into
-// L2 with a cache-policy hint; no shared-memory destination, nothing to wait for.
-__device__ __forceinline__ void l2_prefetch_hint(const void* gmem_src, uint32_t bytes, uint64_t policy) {
-    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(gmem_src), "r"(bytes),
-                 "l"(policy)
-                 : "memory");
-}
-
 // bulk_load with an L2 cache-policy hint.
 __device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
                                                uint64_t policy) {

@@ -90,7 +90,6 @@ struct PArgs {
     int slots;
     int slot_bytes;
     int inflight;  // chunks the producer keeps in flight at most (0: every free slot)
-    int head_prefetch;  // head chunks per CTA warmed into L2 during the layers of each step
     SmemLayout sm;
 };
 
@@ -1178,25 +1177,11 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             int lslot = 0;
             uint32_t lphase = 0;
             long long landed = 0;
-            const uint64_t keep = l2_evict_last_policy();
             for (int step = 0; step < a.steps && go; ++step) {
                 for (int oi = 0; oi <= 4 * a.L && go; ++oi) {
                     const int op = oi < 4 * a.L ? (oi & 3) : kOpHead;
                     const OpDesc d = ops[op];
                     const __nv_bfloat16* w = op_weight(a, layers[oi < 4 * a.L ? oi >> 2 : 0], op);
-                    if (oi < 4 * a.L && a.head_prefetch > 0) {
-                        // HBM idles during the layers' exchanges: warm L2 with the first
-                        // head chunks of this CTA, spread over the layer ops, so part of
-                        // the lm_head read at the end of the step hits L2.
-                        const OpDesc hd = ops[kOpHead];
-                        const int total = min(a.head_prefetch, hd.nch);
-                        const int j0 = (oi * total) / (4 * a.L), j1 = ((oi + 1) * total) / (4 * a.L);
-                        for (int j = j0; j < j1; ++j) {
-                            const int r0 = hd.lo + (j << hd.shift);
-                            const int nr = min(1 << hd.shift, hd.hi - r0);
-                            l2_prefetch_hint(a.head + (size_t)r0 * hd.K, (uint32_t)nr * (uint32_t)hd.K * 2u, keep);
-                        }
-                    }
                     for (int ch = 0; ch < d.nch; ++ch) {
                         if (wrapped) {
                             // wait until the consumers released this slot's previous chunk
@@ -1651,14 +1636,6 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
     // LSX_DECODE_INFLIGHT overrides.
     inflight_ = std::min(6, slots_ - 1);
     if (const char* v = std::getenv("LSX_DECODE_INFLIGHT")) inflight_ = std::max(0, std::min(std::atoi(v), slots_ - 1));
-    // Head chunks per CTA warmed into L2 during each step's layers
-    // (LSX_DECODE_HEAD_PREFETCH_MB: megabytes of lm_head over the whole grid).
-    head_prefetch_ = 0;
-    if (const char* v = std::getenv("LSX_DECODE_HEAD_PREFETCH_MB")) {
-        const double mb = std::max(0.0, std::atof(v));
-        const double chunk = (double)std::max(1, slot_bytes);
-        head_prefetch_ = (int)(mb * 1048576.0 / ((double)grid_ * chunk));
-    }
     layer_count_ = (int)layers.size();
     smem_ = (size_t)layout_for(c, slots_, slot_bytes, grid_, layers.size()).total;
     PKernel k = kernel_for(c);
@@ -1708,7 +1685,6 @@ int PersistentDecoder::run(int steps) {
     a.slots = slots_;
     a.slot_bytes = slot_bytes_for(c);
     a.inflight = inflight_;
-    a.head_prefetch = head_prefetch_;
     a.sm = layout_for(c, slots_, a.slot_bytes, grid_, (size_t)layer_count_);
     void* args[] = {&a};
     LSX_CUDA(cudaLaunchCooperativeKernel((const void*)kernel_for(c), dim3(grid_), dim3(kThreads), args, smem_,

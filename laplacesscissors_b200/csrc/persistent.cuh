@@ -33,7 +33,6 @@ private:
     size_t smem_ = 0;
     int slots_ = 0;
     int inflight_ = 0;
-    int head_prefetch_ = 0;  // head chunks per CTA warmed into L2 during each step's layers
     int ns_ = 0, split_min_ = 0;  // split attention: slots per KV group, first position + 1
     int grid_ = 0;
     int layer_count_ = 0;
