@@ -535,7 +535,7 @@ def vocab_readout(args, rank, local, world):
 
     import laplacesscissors_b200 as lsx
     from laplacesscissors_b200 import DeviceRotation
-    from laplacesscissors_b200._lib import BF16, lib
+    from laplacesscissors_b200._lib import BF16, check, lib
     from laplacesscissors_b200.sharding import vocab_shard, vocab_sharded_margin
     args.warmup = max(args.warmup, 3)
     dist = Dist(world, local)
@@ -570,6 +570,28 @@ def vocab_readout(args, rank, local, world):
         stop.record(stream)
         stop.synchronize()
     ms = dist.max(start.elapsed_time(stop)) / args.steps
+    # The shard's kernels alone (no collective, no merge), to separate compute from exchange.
+    import ctypes as C
+    keys = torch.empty(READOUT_ROWS, dtype=torch.int64, device=dev)
+    tlog = torch.empty(READOUT_ROWS, dtype=torch.float32, device=dev)
+
+    def shard_only():
+        check(lib.lsx_readout_shard_device(gpu.handle, shard.handle, None, v0, v1 - v0, HIDDEN,
+                                           C.c_void_p(d_hidden.data_ptr()), BF16, READOUT_ROWS,
+                                           C.c_void_p(d_targets.data_ptr()), rot.handle,
+                                           C.c_void_p(keys.data_ptr()), C.c_void_p(tlog.data_ptr()),
+                                           C.c_void_p(ws.data_ptr()), ws.numel()))
+
+    for _ in range(args.warmup):
+        shard_only()
+    gpu.synchronize()
+    start2, stop2 = event(), event()
+    start2.record(stream)
+    for _ in range(args.steps):
+        shard_only()
+    stop2.record(stream)
+    stop2.synchronize()
+    shard_ms = dist.max(start2.elapsed_time(stop2)) / args.steps
     if rank == 0:
         tflops = 2.0 * READOUT_ROWS * VOCAB * HIDDEN / (ms / 1e3) / 1e12
         print(json.dumps({
@@ -579,8 +601,9 @@ def vocab_readout(args, rank, local, world):
             "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate",
             "data": "synthetic: lm_head N(0, 0.02) seed 7, 4096 RMSNorm'd rows, rank-16 Givens edit",
             "config": {"workload": "4096 rows x lm_head [151936, 1024], rank-16 edit, vocab-sharded",
-                       "vocab_rows_per_gpu": VOCAB // world, "collective": "2 NCCL all-reduce MAX per step",
+                       "vocab_rows_per_gpu": VOCAB // world, "collective": "1 NCCL all-reduce MAX per step",
                        "l2": "lm_head shard read once per step"},
+            "shard_kernels_ms": shard_ms,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": tflops / (world * peaks["bf16_tflops"]),
                          "scope": f"whole validation over {world} GPU(s), {peaks['source']} burst peak x GPUs"},
