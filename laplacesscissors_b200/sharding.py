@@ -146,8 +146,8 @@ def vocab_sharded_margin(gpu, weight_shard, bias_shard, vocab_offset: int, shard
 
     This rank holds lm_head rows [vocab_offset, vocab_offset + shard_vocab)
     (`weight_shard`, a BF16 Tensor) and scores every hidden row against them with
-    lsx_readout_shard_device; one NCCL all-reduce MAX of the packed competitor keys
-    and one of the target logits combine the shards, and lsx_readout_merge_device
+    lsx_readout_shard_device; one NCCL all-reduce MAX over the packed competitor
+    keys and the target logits (merge_partials_) combines the shards, and lsx_readout_merge_device
     turns the merged partials into margins and first argmaxes.  All work is ordered
     on the library's stream.  `hidden_ptr` / `targets_ptr` are device addresses
     ([rows, width] of `hidden_kind`; global target ids as u32).  Returns device
