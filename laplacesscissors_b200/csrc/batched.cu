@@ -618,12 +618,11 @@ constexpr size_t kFaSmem = (size_t)(2 * kFaKeys * kFaKStride + 2 * kFaD * kFaVSt
 bool launch_attention_mma(cudaStream_t s, const float* qkv, int M, int T, int QH, int KVH, int D, float scale,
                           __nv_bfloat16* hi, __nv_bfloat16* lo) {
     if (D != kFaD || QH % KVH != 0 || QH / KVH > 8 || M % T != 0) return false;
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute((const void*)causal_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kFaSmem) != cudaSuccess)
-            return false;
-        configured = true;
+    // set on every call: the attribute belongs to the current device
+    if (cudaFuncSetAttribute((const void*)causal_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kFaSmem) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
     }
     const int R = QH / KVH;
     const int blocks = (M / T) * KVH * ((T + 15) / 16);
