@@ -209,6 +209,17 @@ int lsx_model_score(lsx_model* model, const uint32_t* prompt, size_t prompt_leng
                     size_t count, const lsx_rotation* rotation, double* nll_out, uint32_t* argmax_out,
                     float* hidden_frames, float* logits_frames);
 
+/* Greedy generation of `batch` independent sequences at once (batch > 1 decode; the
+   reference decodes one sequence at a time, diagnosis::generate_frames,
+   src/diagnosis.rs:106-149, so a batch equals that many separate generations):
+   prompts [batch x prompt_length] (prompt_length >= 2), tokens_out [batch x maximum].
+   The first prompt_length - 1 tokens of every sequence go through one batched
+   forward into per-sequence KV caches; then each step feeds one row per sequence
+   through the tensor-core GEMMs (each weight read once for the whole batch) and an
+   attention over each sequence's own cache.  No stop tokens, no frames; does not
+   touch the model's own cursor or cache. */
+int lsx_model_generate_batch(lsx_model* model, const uint32_t* prompts, size_t batch, size_t prompt_length,
+                             size_t maximum, uint32_t* tokens_out);
 /* lsx_model_score over `cases` independent cases of equal shape at once (the
    per-case loop of scaling::evaluate, src/scaling.rs:181-216, batched): prompts
    [cases x prompt_length], targets [cases x count].  Per scored position:

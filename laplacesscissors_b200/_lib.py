@@ -98,6 +98,7 @@ SIGNATURES = {
     "lsx_model_head": (I, [P, PP, PP]),
     "lsx_model_generate": (I, [P, UP, SZ, SZ, UP, SZ, P, UP, C.POINTER(SZ), C.POINTER(I), FP, FP]),
     "lsx_model_score": (I, [P, UP, SZ, UP, SZ, P, DP, UP, FP, FP]),
+    "lsx_model_generate_batch": (I, [P, UP, SZ, SZ, SZ, UP]),
     "lsx_model_score_batch": (I, [P, UP, SZ, SZ, UP, SZ, P, DP, UP, DP, FP]),
     "lsx_readout_margin": (I, [P, P, P, SZ, SZ, P, I, SZ, UP, P, DP, UP, FP]),
     "lsx_readout_margin_device": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P, P, P, SZ]),

@@ -682,13 +682,153 @@ __global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, 
 
 // Appends every row's k (after QK-norm and RoPE) and v to the f32 KV cache at
 // position = row (kernels/ops.py:69-73 for a whole prompt).
+// Row m = c T + t goes to position pos0 + t of case c's cache (case_stride floats
+// apart; one case: case_stride is unused).
 __global__ void kv_store_kernel(const float* __restrict__ qkv, size_t total, int QH, int KVH, int D,
-                                float* __restrict__ keys, float* __restrict__ values) {
+                                float* __restrict__ keys, float* __restrict__ values, int T, int pos0,
+                                size_t case_stride) {
     const size_t kw = (size_t)KVH * D, stride = (size_t)(QH + 2 * KVH) * D;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const size_t m = i / kw, e = i % kw;
-        keys[i] = qkv[m * stride + (size_t)QH * D + e];
-        values[i] = qkv[m * stride + (size_t)(QH + KVH) * D + e];
+        const size_t c = m / T, t = m % T;
+        const size_t dst = c * case_stride + (pos0 + t) * kw + e;
+        keys[dst] = qkv[m * stride + (size_t)QH * D + e];
+        values[dst] = qkv[m * stride + (size_t)(QH + KVH) * D + e];
+    }
+}
+
+// ---- batched decode: one new row per sequence, attention over its cache ----
+// Block (case c, KV group g, split s) takes positions [s chunk, (s + 1) chunk) of
+// 0 .. pos of case c's cache; warp w the positions start + w, start + w + 8, ...; each
+// warp carries the R query heads of the group (the K and V rows are read once for
+// all of them) with a running softmax per head (kernels/ops.py:88-99), the warps'
+// states merge in shared memory, and the block writes per head a partial state
+// (max, sum, unnormalised output[D]) for cached_attention_merge_kernel.
+constexpr int kDecWarps = 8;
+
+template <int DPL, int R>
+__global__ void __launch_bounds__(32 * kDecWarps) cached_attention_part_kernel(
+    const float* __restrict__ qkv, const float* __restrict__ keys, const float* __restrict__ values, int QH, int KVH,
+    int pos, size_t case_stride, int splits, float scale, float* __restrict__ part) {
+    constexpr int D = DPL * 32;
+    __shared__ float st[kDecWarps][R][D + 2];
+    const int s = blockIdx.x % splits, g = (blockIdx.x / splits) % KVH, c = blockIdx.x / (splits * KVH);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = pos + 1, chunk = (n + splits - 1) / splits;
+    const int t0 = s * chunk, t1 = min(n, t0 + chunk);
+    const size_t kw = (size_t)KVH * D;
+    const float* kb = keys + (size_t)c * case_stride + (size_t)g * D;
+    const float* vb = values + (size_t)c * case_stride + (size_t)g * D;
+    const float* qrow = qkv + (size_t)c * (QH + 2 * KVH) * D;
+    float q[R][DPL], m[R], l[R], acc[R][DPL];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            q[i][j] = qrow[(size_t)(g * R + i) * D + lane + 32 * j];
+            acc[i][j] = 0.f;
+        }
+    }
+    for (int t = t0 + warp; t < t1; t += kDecWarps) {
+        float k[DPL], v[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            k[j] = __ldcs(kb + (size_t)t * kw + lane + 32 * j);
+            v[j] = __ldcs(vb + (size_t)t * kw + lane + 32 * j);
+        }
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            float x = 0.f;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) x = fmaf(q[i][j], k[j], x);
+            for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+            const float sv = x * scale;
+            const float mn = fmaxf(m[i], sv);
+            const float carry = expf(m[i] - mn), p = expf(sv - mn);
+            l[i] = l[i] * carry + p;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[i][j] = fmaf(p, v[j], acc[i][j] * carry);
+            m[i] = mn;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        if (lane == 0) {
+            st[warp][i][0] = m[i];
+            st[warp][i][1] = l[i];
+        }
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) st[warp][i][2 + lane + 32 * j] = acc[i][j];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < R * (D + 2); idx += blockDim.x) {
+        const int i = idx / (D + 2), e = idx % (D + 2);
+        float M = -INFINITY;
+        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, st[w][i][0]);
+        float val;
+        if (e == 0) {
+            val = M;
+        } else {
+            val = 0.f;
+            for (int w = 0; w < kDecWarps; ++w)
+                if (st[w][i][0] != -INFINITY) val = fmaf(st[w][i][e], expf(st[w][i][0] - M), val);
+        }
+        part[(((size_t)c * QH + g * R + i) * splits + s) * (D + 2) + e] = val;
+    }
+}
+
+// Per (case, query head): merges the splits' partial states and writes the output as
+// the bf16 hi/lo A planes of the o projection, row c.
+template <int DPL>
+__global__ void cached_attention_merge_kernel(const float* __restrict__ part, int QH, int splits,
+                                              __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    constexpr int D = DPL * 32;
+    const int c = blockIdx.x / QH, h = blockIdx.x % QH;
+    const float* p = part + ((size_t)c * QH + h) * splits * (D + 2);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float M = -INFINITY;
+        for (int s = 0; s < splits; ++s) M = fmaxf(M, p[(size_t)s * (D + 2)]);
+        float L = 0.f, O = 0.f;
+        for (int s = 0; s < splits; ++s) {
+            const float* q = p + (size_t)s * (D + 2);
+            if (q[0] == -INFINITY) continue;
+            const float ex = expf(q[0] - M);
+            L = fmaf(q[1], ex, L);
+            O = fmaf(q[2 + d], ex, O);
+        }
+        split_store(hi, lo, ((size_t)c * QH + h) * D + d, O / L);
+    }
+}
+
+// First argmax of each logit row (src/diagnosis.rs:58-70) into tokens[row] and
+// history[row]; a non-finite logit raises status[1].
+__global__ void __launch_bounds__(1024) row_argmax_tokens_kernel(const float* __restrict__ logits, int V,
+                                                                 uint32_t* __restrict__ tokens,
+                                                                 uint32_t* __restrict__ history, int* status) {
+    __shared__ unsigned long long kbest[32];
+    const float* z = logits + (size_t)blockIdx.x * V;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
+    unsigned long long best = 0ull;
+    bool bad = false;
+    for (int j = tid; j < V; j += blockDim.x) {
+        const unsigned long long k = pack_arg(z[j], (uint32_t)j);
+        best = k > best ? k : best;
+        bad |= !isfinite(z[j]);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
+        best = b2 > best ? b2 : best;
+    }
+    if (lane == 0) kbest[warp] = best;
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&status[1], 1);
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < warps; ++w) best = kbest[w] > best ? kbest[w] : best;
+        const uint32_t token = 0xffffffffu - (uint32_t)(best & 0xffffffffull);
+        tokens[blockIdx.x] = token;
+        history[blockIdx.x] = token;
     }
 }
 
@@ -749,6 +889,7 @@ __global__ void __launch_bounds__(1024) row_scores_kernel(const float* __restric
 
 BatchedScorer::~BatchedScorer() {
     if (block_) cudaFree(block_);
+    if (batch_cache_) cudaFree(batch_cache_);
 }
 
 bool BatchedScorer::eligible(const FusedConfig& c, std::string* why) {
@@ -826,6 +967,149 @@ int BatchedScorer::prefill(const uint32_t* tokens, size_t n) {
     return run(tokens, 1, n, 0, 0, nullptr, nullptr, Outputs{}, true);
 }
 
+template <int DPL>
+static bool launch_cached_attention(cudaStream_t s, const float* qkv, const float* keys, const float* values, int B,
+                                    int QH, int KVH, int pos, size_t case_stride, int splits, float scale,
+                                    float* part, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const int R = QH / KVH;
+    const int blocks = B * KVH * splits, threads = 32 * kDecWarps;
+    if (R == 1)
+        cached_attention_part_kernel<DPL, 1><<<blocks, threads, 0, s>>>(qkv, keys, values, QH, KVH, pos, case_stride,
+                                                                        splits, scale, part);
+    else if (R == 2)
+        cached_attention_part_kernel<DPL, 2><<<blocks, threads, 0, s>>>(qkv, keys, values, QH, KVH, pos, case_stride,
+                                                                        splits, scale, part);
+    else if (R == 4 && DPL <= 4)
+        cached_attention_part_kernel<DPL, 4><<<blocks, threads, 0, s>>>(qkv, keys, values, QH, KVH, pos, case_stride,
+                                                                        splits, scale, part);
+    else
+        return false;
+    cached_attention_merge_kernel<DPL><<<B * QH, 128, 0, s>>>(part, QH, splits, hi, lo);
+    return true;
+}
+
+int BatchedScorer::generate_batch(const uint32_t* prompts, size_t batch, size_t P, size_t maximum,
+                                  uint32_t* tokens_out) {
+    const FusedConfig& c = config_;
+    LSX_ENSURE(prompts && tokens_out && batch > 0 && batch <= 1024 && P >= 2 && maximum > 0,
+               "check the batched generation shape");
+    for (size_t i = 0; i < batch * P; ++i) LSX_ENSURE(prompts[i] < (uint32_t)c.vocab, "check the prompt token range");
+    const int H = c.hidden, D = c.head_dim, QH = c.qheads, KVH = c.kvheads, I = c.intermediate, V = c.vocab;
+    const int R = QH / KVH, dpl = D / 32;
+    LSX_ENSURE(R == 1 || R == 2 || (R == 4 && dpl <= 4), "batched generation: unsupported group ratio");
+    const size_t cap = P + maximum, kw = (size_t)KVH * D, B = batch;
+    const size_t case_stride = cap * kw, layer_stride = 2 * B * case_stride;
+    const int splits = std::max(1, std::min(32, (2 * ctx_->sm_count + (int)(B * KVH) - 1) / (int)(B * KVH)));
+    const size_t part_floats = B * QH * (size_t)splits * (D + 2);
+    const size_t need = (layer_stride * layers_.size() + part_floats) * 4 + maximum * B * 4 + 256;
+    cudaStream_t s = ctx_->stream;
+    LSX_CUDA(cudaStreamSynchronize(s), "batched generation");
+    if (need > batch_cache_bytes_) {
+        if (batch_cache_) cudaFree(batch_cache_);
+        batch_cache_ = nullptr;
+        batch_cache_bytes_ = 0;
+        LSX_CUDA(cudaMalloc(&batch_cache_, need), "batched generation caches");
+        batch_cache_bytes_ = need;
+    }
+    float* part = batch_cache_ + layer_stride * layers_.size();
+    uint32_t* history = (uint32_t*)(part + part_floats);
+
+    // the prompts less their last token: one batched forward into the sequences' caches
+    std::vector<uint32_t> head_tokens(B * (P - 1));
+    for (size_t b = 0; b < B; ++b)
+        for (size_t t = 0; t + 1 < P; ++t) head_tokens[b * (P - 1) + t] = prompts[b * P + t];
+    batch_keys_ = batch_cache_;
+    batch_case_stride_ = case_stride;
+    batch_layer_stride_ = layer_stride;
+    const int rc = run(head_tokens.data(), B, P - 1, 0, 0, nullptr, nullptr, Outputs{}, true);
+    batch_keys_ = nullptr;
+    LSX_TRY(rc);
+
+    // decode: one row per sequence and step, the whole loop on the device
+    LSX_TRY(reserve(B, B, cap));
+    const Layout& L = layout_;
+    uint8_t* base = (uint8_t*)block_;
+    float* x = (float*)(base + L.x);
+    float* work = (float*)(base + L.work);
+    const size_t widest = std::max((size_t)H, std::max((size_t)QH * D, (size_t)I));
+    __nv_bfloat16* hi = (__nv_bfloat16*)(base + L.planes);
+    __nv_bfloat16* lo = hi + B * widest;
+    float* logits = (float*)(base + L.logits);
+    float2* rope = (float2*)(base + L.rope);
+    uint32_t* d_tokens = (uint32_t*)(base + L.tokens);
+    int* status = (int*)(base + L.status);
+    const int half = D / 2, qkvw = (QH + 2 * KVH) * D;
+    std::vector<float2> table(cap * half);
+    for (size_t p = 0; p < cap; ++p)
+        for (int i = 0; i < half; ++i) {
+            const double angle = (double)p * std::pow(c.theta, -2.0 * i / (double)c.rotary);
+            table[p * half + i] = make_float2((float)std::cos(angle), (float)std::sin(angle));
+        }
+    std::vector<uint32_t> last(B);
+    for (size_t b = 0; b < B; ++b) last[b] = prompts[b * P + P - 1];
+    LSX_CUDA(cudaMemcpyAsync(rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice, s),
+             "rope upload");
+    LSX_CUDA(cudaMemcpyAsync(d_tokens, last.data(), B * 4, cudaMemcpyHostToDevice, s), "token upload");
+    LSX_CUDA(cudaMemsetAsync(status, 0, 16, s), "status clear");
+    LSX_CUDA(cudaStreamSynchronize(s), "batched generation upload");  // host tables go out of scope
+    const int M = (int)B;
+    const int qk_blocks = (M * (QH + KVH) + 7) / 8;
+    const int kv_blocks = (int)((B * kw + 255) / 256);
+    for (size_t step = 0; step < maximum; ++step) {
+        const int pos = (int)(P - 1 + step);
+        embed_rows_kernel<<<M, 256, 0, s>>>(c.embedding, c.embedding_kind, c.embedding_scale, d_tokens, H, x);
+        LSX_CUDA(cudaGetLastError(), "embedding rows");
+        for (size_t li = 0; li < layers_.size(); ++li) {
+            const FusedLayer& Ly = layers_[li];
+            float* bk = batch_cache_ + li * layer_stride;
+            float* bv = bk + layer_stride / 2;
+            rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.input_gain, c.eps, hi, lo);
+            LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wqkv, qkvw, Ly.bqkv, work, qkvw, false, status));
+            const float2* rp = rope + (size_t)pos * half;
+            bool ok;
+            if (D == 128) {
+                qk_rope_kernel<4><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
+                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride);
+                ok = launch_cached_attention<4>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
+                                                hi, lo);
+            } else if (D == 64) {
+                qk_rope_kernel<2><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
+                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride);
+                ok = launch_cached_attention<2>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
+                                                hi, lo);
+            } else {
+                qk_rope_kernel<8><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
+                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride);
+                ok = launch_cached_attention<8>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
+                                                hi, lo);
+            }
+            LSX_ENSURE(ok, "batched generation: unsupported group ratio");
+            LSX_CUDA(cudaGetLastError(), "batched decode attention");
+            LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));
+            rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.post_gain, c.eps, hi, lo);
+            LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wgu, 2 * I, Ly.bgu, work, 2 * I, false, status));
+            const size_t feats = (size_t)M * I;
+            gated_planes_kernel<<<(int)std::min<size_t>((feats + 255) / 256, 148 * 16), 256, 0, s>>>(
+                work, feats, I, c.activation, hi, lo);
+            LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
+        }
+        rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, c.final_gain, c.eps, hi, lo);
+        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, c.head, V, c.head_bias, logits, V, false, status));
+        row_argmax_tokens_kernel<<<M, 1024, 0, s>>>(logits, V, d_tokens, history + step * B, status);
+        LSX_CUDA(cudaGetLastError(), "batched decode step");
+    }
+    std::vector<uint32_t> hist(maximum * B);
+    int host_status[2] = {0, 0};
+    LSX_CUDA(cudaMemcpyAsync(hist.data(), history, hist.size() * 4, cudaMemcpyDeviceToHost, s), "token download");
+    LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
+    LSX_CUDA(cudaStreamSynchronize(s), "batched generation");
+    if (host_status[0] != 0) return fail(LSX_E_CUDA, "batched generation: a device wait timed out");
+    if (host_status[1] != 0) return fail(LSX_E_NONFINITE, "check the finiteness of the model outputs");
+    for (size_t b = 0; b < B; ++b)
+        for (size_t k = 0; k < maximum; ++k) tokens_out[b * maximum + k] = hist[k * B + b];
+    return LSX_OK;
+}
+
 int BatchedScorer::score(const uint32_t* tokens, size_t cases, size_t T, size_t first, size_t count,
                          const uint32_t* targets, const lsx_rotation* rotation, const Outputs& out) {
     LSX_ENSURE(cases > 0 && T > 0 && count > 0 && first + count <= T && targets, "check the case shape");
@@ -886,7 +1170,8 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
     embed_rows_kernel<<<M, 256, 0, s>>>(c.embedding, c.embedding_kind, c.embedding_scale, d_tokens, H, x);
     LSX_CUDA(cudaGetLastError(), "embedding rows");
     const int warps_per_block = 8;
-    for (const FusedLayer& Ly : layers_) {
+    for (size_t li = 0; li < layers_.size(); ++li) {
+        const FusedLayer& Ly = layers_[li];
         rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.input_gain, c.eps, hi, lo);
         LSX_CUDA(cudaGetLastError(), "input norm");
         LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wqkv, qkvw, Ly.bqkv, work, qkvw, false, status));
@@ -916,8 +1201,15 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
         LSX_CUDA(cudaGetLastError(), "attention");
         if (write_cache) {
             const size_t kv = (size_t)M * KVH * D;
-            kv_store_kernel<<<(int)std::min<size_t>((kv + 255) / 256, 148 * 16), 256, 0, s>>>(work, kv, QH, KVH, D,
-                                                                                             Ly.keys, Ly.values);
+            if (batch_keys_) {  // per-sequence caches of generate_batch
+                float* bk = batch_keys_ + li * batch_layer_stride_;
+                float* bv = bk + batch_layer_stride_ / 2;
+                kv_store_kernel<<<(int)std::min<size_t>((kv + 255) / 256, 148 * 16), 256, 0, s>>>(
+                    work, kv, QH, KVH, D, bk, bv, (int)T, 0, batch_case_stride_);
+            } else {
+                kv_store_kernel<<<(int)std::min<size_t>((kv + 255) / 256, 148 * 16), 256, 0, s>>>(
+                    work, kv, QH, KVH, D, Ly.keys, Ly.values, (int)T, 0, 0);
+            }
             LSX_CUDA(cudaGetLastError(), "KV append");
         }
         LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));

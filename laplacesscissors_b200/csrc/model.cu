@@ -1539,6 +1539,18 @@ int lsx_model_score(lsx_model* m, const uint32_t* prompt, size_t prompt_length, 
 // Teacher-forced scoring of many equal-length cases at once (the per-case loop of
 // src/scaling.rs:181-216 batched over cases): every case's prompt and targets but
 // the last go through the decoder together, one tensor-core GEMM per projection.
+int lsx_model_generate_batch(lsx_model* m, const uint32_t* prompts, size_t batch, size_t prompt_length,
+                             size_t maximum, uint32_t* tokens_out) {
+    LSX_ENSURE(m && prompts && tokens_out, "invalid argument");
+    LSX_ENSURE(batch > 0 && prompt_length >= 2 && maximum > 0,
+               "give at least one sequence, two prompt tokens and one generated token");
+    for (size_t i = 0; i < batch * prompt_length; ++i) LSX_ENSURE(prompts[i] < m->graph.vocab, "check the token range");
+    if (!m->fused) return fail(LSX_E_UNSUPPORTED, "batched generation needs the fused weight layout");
+    cudaSetDevice(m->ctx->device);
+    LSX_TRY(ensure_batched(m));
+    return m->batched->generate_batch(prompts, batch, prompt_length, maximum, tokens_out);
+}
+
 int lsx_model_score_batch(lsx_model* m, const uint32_t* prompts, size_t cases, size_t prompt_length,
                           const uint32_t* targets, size_t count, const lsx_rotation* rotation, double* nll_out,
                           uint32_t* argmax_out, double* margin_out, float* logits_out) {

@@ -188,6 +188,14 @@ class Model:
         check(lib.lsx_model_head_image(self._h, _dp(v), _fp(out)))
         return out
 
+    def generate_batch(self, prompts, maximum: int) -> np.ndarray:
+        """Greedy generation of several equal-length prompts at once
+        (lsx_model_generate_batch): prompts [batch, P] -> tokens [batch, maximum]."""
+        p = np.ascontiguousarray(np.atleast_2d(prompts), dtype=np.uint32)
+        out = np.empty((p.shape[0], int(maximum)), dtype=np.uint32)
+        check(lib.lsx_model_generate_batch(self._h, _up(p), p.shape[0], p.shape[1], int(maximum), _up(out)))
+        return out
+
     def head_images(self, gpu: Gpu, vectors) -> np.ndarray:
         """head_image for every row of `vectors` [count, hidden] in one tensor-core
         pass over the lm_head per 32 directions; returns [count, vocab] f32."""
