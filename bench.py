@@ -763,10 +763,10 @@ def long_decode_batch(args, local, batch: int = 16):
     from laplacesscissors_b200 import synth
     gpu = lsx.Gpu(local)
     cfg = synth.QWEN3_4B
-    P, K = args.prompt, max(4, args.steps)
+    P, K = args.prompt, max(32, args.steps)
     model = lsx.Model.load(model_checkpoint("QWEN3_4B"), gpu, 64)
     prompts = np.stack([synth.prompt_tokens(7 + b, P, cfg["vocab"]) for b in range(batch)])
-    model.generate_batch(prompts, 2)  # warm-up: buffers, caches, kernel modules
+    model.generate_batch(prompts, 1 + K)  # warm-up: buffers, caches (largest), kernel modules
     t0 = time.perf_counter()
     model.generate_batch(prompts, 1)
     t_one = time.perf_counter() - t0

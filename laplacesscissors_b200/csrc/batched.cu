@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <vector>
 
 #include "batched.cuh"
@@ -731,12 +732,28 @@ __global__ void __launch_bounds__(32 * kDecWarps) cached_attention_part_kernel(
             acc[i][j] = 0.f;
         }
     }
+    // the next position's K and V rows are loaded while the current one is used
+    float kn[DPL], vn[DPL];
+    if (t0 + warp < t1) {
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            kn[j] = __ldcs(kb + (size_t)(t0 + warp) * kw + lane + 32 * j);
+            vn[j] = __ldcs(vb + (size_t)(t0 + warp) * kw + lane + 32 * j);
+        }
+    }
     for (int t = t0 + warp; t < t1; t += kDecWarps) {
         float k[DPL], v[DPL];
 #pragma unroll
         for (int j = 0; j < DPL; ++j) {
-            k[j] = __ldcs(kb + (size_t)t * kw + lane + 32 * j);
-            v[j] = __ldcs(vb + (size_t)t * kw + lane + 32 * j);
+            k[j] = kn[j];
+            v[j] = vn[j];
+        }
+        if (t + kDecWarps < t1) {
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) {
+                kn[j] = __ldcs(kb + (size_t)(t + kDecWarps) * kw + lane + 32 * j);
+                vn[j] = __ldcs(vb + (size_t)(t + kDecWarps) * kw + lane + 32 * j);
+            }
         }
 #pragma unroll
         for (int i = 0; i < R; ++i) {
@@ -999,7 +1016,10 @@ int BatchedScorer::generate_batch(const uint32_t* prompts, size_t batch, size_t 
     LSX_ENSURE(R == 1 || R == 2 || (R == 4 && dpl <= 4), "batched generation: unsupported group ratio");
     const size_t cap = P + maximum, kw = (size_t)KVH * D, B = batch;
     const size_t case_stride = cap * kw, layer_stride = 2 * B * case_stride;
-    const int splits = std::max(1, std::min(32, (2 * ctx_->sm_count + (int)(B * KVH) - 1) / (int)(B * KVH)));
+    // about eight attention blocks per SM at any batch: each warp's cache walk is
+    // latency-bound, so parallel blocks carry the bandwidth
+    int splits = std::max(1, std::min(64, (8 * ctx_->sm_count + (int)(B * KVH) - 1) / (int)(B * KVH)));
+    if (const char* v = std::getenv("LSX_BATCH_ATTENTION_SPLITS")) splits = std::max(1, std::min(64, std::atoi(v)));
     const size_t part_floats = B * QH * (size_t)splits * (D + 2);
     const size_t need = (layer_stride * layers_.size() + part_floats) * 4 + maximum * B * 4 + 256;
     cudaStream_t s = ctx_->stream;
