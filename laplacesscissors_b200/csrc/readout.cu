@@ -60,6 +60,10 @@ struct ReadoutParams {
     // store mode: out[M, ldo] (=|+=) A B^T + bias, columns [0, V)
     float* out;
     int ldo, accumulate;
+    // store mode, split over K: ksplits > 1 writes K-slice s's product to
+    // partial + s * M * V (row stride V, no bias), summed by split_reduce_kernel
+    int ksplits;
+    float* partial;
 };
 
 enum { kModeMargin = 0, kModeStore = 2 };
@@ -585,7 +589,9 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
     const uint32_t rank = cluster_rank();  // 0: leader
     const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
     const int m_pairs = (p.M + kPairRows - 1) / kPairRows;
-    const int total = m_pairs * p.n_tiles;
+    const int ksplits = (MODE == kModeStore && p.ksplits > 1) ? p.ksplits : 1;
+    const int base_tiles = m_pairs * p.n_tiles;
+    const int total = base_tiles * ksplits;
     const int k_total = p.k_blocks + p.ext_blocks;
 
     if (threadIdx.x == 0) {
@@ -620,9 +626,11 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             bool ok = true;
             const uint32_t full0 = map_to_rank(smem_u32(&full[0]), 0);
             for (int tile = pair; tile < total && ok; tile += pairs) {
-                const int m0 = (tile % m_pairs) * kPairRows + (int)rank * RM;
-                const int n0 = (tile / m_pairs) * RN + (int)rank * kHalfN;
-                for (int kb = 0; kb < k_total; ++kb) {
+                const int ks = tile / base_tiles, bt = tile - ks * base_tiles;
+                const int m0 = (bt % m_pairs) * kPairRows + (int)rank * RM;
+                const int n0 = (bt / m_pairs) * RN + (int)rank * kHalfN;
+                const int kb0 = ks * k_total / ksplits, kb1 = (ks + 1) * k_total / ksplits;
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
                         ok = false;
                         break;
@@ -669,7 +677,9 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * RN);
-                for (int kb = 0; kb < k_total; ++kb) {
+                const int ks = tile / base_tiles;
+                const int kb0 = ks * k_total / ksplits, kb1 = (ks + 1) * k_total / ksplits;
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!wait_or_abort(&full[stage], phase, abort_flag)) {
                         ok = false;
                         break;
@@ -683,7 +693,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
                         const uint64_t adesc = smem_desc_sw128(sa + pl * kTileBytesA);
 #pragma unroll
                         for (int k = 0; k < RK / 16; ++k) {
-                            const uint32_t accumulate = (kb | pl | k) != 0;
+                            const uint32_t accumulate = ((kb - kb0) | pl | k) != 0;
                             tc_mma_pair(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdescPair,
                                         accumulate);
                         }
@@ -715,8 +725,9 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
         uint32_t acc_phase = 0;
         bool nonfinite = false;
         for (int tile = pair; tile < total; tile += pairs) {
-            const int m0 = (tile % m_pairs) * kPairRows + (int)rank * RM;
-            const int n0 = (tile / m_pairs) * RN;
+            const int ks = tile / base_tiles, bt = tile - ks * base_tiles;
+            const int m0 = (bt % m_pairs) * kPairRows + (int)rank * RM;
+            const int n0 = (bt / m_pairs) * RN;
             const bool ok = wait_or_abort(&tmem_full[acc], acc_phase, abort_flag);
             if (__any_sync(0xffffffffu, !ok)) {
                 if (lane == 0) {
@@ -730,7 +741,17 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
             const bool live = row < p.M;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * RN);
             if (MODE == kModeStore) {
-                store_tile(taddr, row, live, n0, p, nonfinite);
+                if (ksplits > 1) {  // this K slice's product, plain, into its partial plane
+                    ReadoutParams q = p;
+                    q.out = p.partial + (size_t)ks * p.M * p.V;
+                    q.ldo = p.V;
+                    q.accumulate = 0;
+                    q.bias = nullptr;
+                    bool unused = false;
+                    store_tile(taddr, row, live, n0, q, unused);
+                } else {
+                    store_tile(taddr, row, live, n0, p, nonfinite);
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(tmem_empty0 + (uint32_t)(acc * 8));
@@ -779,6 +800,26 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
     cluster_sync();  // the pair's MMAs and epilogues are done with both CTAs' memory
     tc_fence_after();
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem_base) : "memory");
+}
+
+// Sum of the K slices of a split store GEMM, in slice order: out[m, n] (=|+=)
+// sum_s partial[s, m, n] (+ bias[n]); a non-finite result raises status[1].
+__global__ void split_reduce_kernel(const float* __restrict__ partial, int ksplits, int M, int N,
+                                    const float* __restrict__ bias, float* __restrict__ out, int ldo, int accumulate,
+                                    int* status) {
+    const size_t total = (size_t)M * N, plane = total;
+    bool bad = false;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / N), n = (int)(i - (size_t)m * N);
+        float v = partial[i];
+        for (int sl = 1; sl < ksplits; ++sl) v += partial[(size_t)sl * plane + i];
+        if (bias) v += bias[n];
+        float* o = out + (size_t)m * ldo + n;
+        if (accumulate) v = *o + v;
+        bad |= !isfinite(v);
+        *o = v;
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(&status[1], 1);
 }
 
 // ------------------------------------------------------------ prep kernels --
@@ -1320,7 +1361,7 @@ cudaError_t launch_pair(lsx_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& 
     cudaError_t e = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int m_pairs = (p.M + kPairRows - 1) / kPairRows;
-    const int total = m_pairs * p.n_tiles;
+    const int total = m_pairs * p.n_tiles * (MODE == kModeStore && p.ksplits > 1 ? p.ksplits : 1);
     const int pairs = std::max(1, std::min(total, ctx->sm_count / 2));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
@@ -1368,6 +1409,29 @@ int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bflo
         // CTA pairs (cta_group::2): each CTA loads half of the weight tile
         CUtensorMap mbh;
         LSX_TRY(make_map(&mbh, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, kHalfN));
+        // Few rows (a batched decode step): too few output tiles to occupy the
+        // pairs, so the K loop is split over otherwise idle pairs and the slices'
+        // products are summed in order afterwards.
+        const int pairs = ctx->sm_count / 2;
+        const int tiles = ((M + kPairRows - 1) / kPairRows) * p.n_tiles;
+        const int ksplits = tiles * 2 <= pairs ? std::min(std::min(pairs / tiles, p.k_blocks / 4), 16) : 1;
+        if (ksplits > 1) {
+            const size_t bytes = (size_t)ksplits * M * N * 4;
+            void* part = nullptr;
+            LSX_TRY(device_alloc(ctx, bytes, &part));
+            p.ksplits = ksplits;
+            p.partial = (float*)part;
+            cudaError_t e = launch_pair<2, 4, kModeStore>(ctx, ma, ma2, mbh, ma, mbh, p);
+            if (e == cudaSuccess) {
+                const size_t total = (size_t)M * N;
+                split_reduce_kernel<<<(int)std::min<size_t>((total + 255) / 256, 4096), 256, 0, ctx->stream>>>(
+                    (const float*)part, ksplits, M, N, bias, out, ldo, accumulate ? 1 : 0, status);
+                e = cudaGetLastError();
+            }
+            device_release(ctx, part);  // stream-ordered: later users of the block run after the reduce
+            LSX_CUDA(e, "split GEMM launch");
+            return LSX_OK;
+        }
         LSX_CUDA((launch_pair<2, 4, kModeStore>(ctx, ma, ma2, mbh, ma, mbh, p)), "GEMM launch");
         return LSX_OK;
     }
