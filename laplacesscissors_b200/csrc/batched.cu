@@ -684,113 +684,191 @@ __global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, 
 // Appends every row's k (after QK-norm and RoPE) and v to the f32 KV cache at
 // position = row (kernels/ops.py:69-73 for a whole prompt).
 // Row m = c T + t goes to position pos0 + t of case c's cache (case_stride floats
-// apart; one case: case_stride is unused).
+// apart; one case: case_stride is unused); element d of KV group g of position p
+// sits at g group_stride + p pos_stride + d. The engine's cache is position-major
+// (group_stride D, pos_stride KVH D); the caches of batched generation are
+// group-major (group_stride capacity D, pos_stride D).
 __global__ void kv_store_kernel(const float* __restrict__ qkv, size_t total, int QH, int KVH, int D,
                                 float* __restrict__ keys, float* __restrict__ values, int T, int pos0,
-                                size_t case_stride) {
+                                size_t case_stride, size_t group_stride, size_t pos_stride) {
     const size_t kw = (size_t)KVH * D, stride = (size_t)(QH + 2 * KVH) * D;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const size_t m = i / kw, e = i % kw;
         const size_t c = m / T, t = m % T;
-        const size_t dst = c * case_stride + (pos0 + t) * kw + e;
+        const size_t dst = c * case_stride + (e / D) * group_stride + (pos0 + t) * pos_stride + e % D;
         keys[dst] = qkv[m * stride + (size_t)QH * D + e];
         values[dst] = qkv[m * stride + (size_t)(QH + KVH) * D + e];
     }
 }
 
 // ---- batched decode: one new row per sequence, attention over its cache ----
+// The caches are group-major: case c's KV group g holds its positions' D-float rows
+// contiguously (group_stride = case_stride / KVH floats apart), so a block's walk
+// reads one contiguous stretch of memory.
 // Block (case c, KV group g, split s) takes positions [s chunk, (s + 1) chunk) of
-// 0 .. pos of case c's cache; warp w the positions start + w, start + w + 8, ...; each
-// warp carries the R query heads of the group (the K and V rows are read once for
-// all of them) with a running softmax per head (kernels/ops.py:88-99), the warps'
-// states merge in shared memory, and the block writes per head a partial state
-// (max, sum, unnormalised output[D]) for cached_attention_merge_kernel.
-constexpr int kDecWarps = 8;
+// 0 .. pos of case c's cache. Each half-warp is one walker: walker w of the block
+// takes positions start + w, start + w + walkers, ...; a lane owns D / 16
+// consecutive elements of a row, so one 4-step butterfly reduces two positions'
+// dot products at once. Each walker carries the R query heads of the group (the K
+// and V rows are read once for all of them) with a running softmax per head
+// (kernels/ops.py:88-99); the walkers' states merge in shared memory, and the block
+// writes per head a partial state (max, sum, unnormalised output[D]) for
+// cached_attention_merge_kernel.
+//
+// A warp keeps its next positions' K and V rows in flight with cp.async into its
+// own ring in shared memory; a lane copies and reads back only its own elements,
+// so the ring needs no cross-lane synchronisation.
+template <int DPL>
+struct AttentionWalk {
+    static constexpr int kWarps = DPL == 8 ? 4 : 8;
+    // ring slots of two positions per warp: 96 KB of ring per block (dynamic shared
+    // memory), so each warp has ten or more rows of K and V in flight
+    static constexpr int kDepth = 98304 / (kWarps * 16 * DPL * 32);
+};
 
 template <int DPL, int R>
-__global__ void __launch_bounds__(32 * kDecWarps) cached_attention_part_kernel(
+constexpr size_t attention_walk_smem() {
+    constexpr int D = DPL * 32, W = AttentionWalk<DPL>::kWarps;
+    constexpr size_t ring = (size_t)W * AttentionWalk<DPL>::kDepth * 4 * D, state = (size_t)2 * W * R * (D + 2);
+    return 4 * (ring > state ? ring : state);
+}
+
+// this lane's E floats of one row, global -> shared, asynchronously
+template <int E>
+__device__ __forceinline__ void lane_row_async(float* dst, const float* src) {
+    static_assert(E % 4 == 0, "16-byte copies");
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+#pragma unroll
+    for (int j = 0; j < E; j += 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 4 * j), "l"(src + j) : "memory");
+}
+
+__device__ __forceinline__ void async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int E>
+__device__ __forceinline__ void lane_row_load(const float* src, float (&x)[E]) {
+#pragma unroll
+    for (int j = 0; j < E; j += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(src + j);
+        x[j] = t.x;
+        x[j + 1] = t.y;
+        x[j + 2] = t.z;
+        x[j + 3] = t.w;
+    }
+}
+
+template <int DPL, int R>
+__global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attention_part_kernel(
     const float* __restrict__ qkv, const float* __restrict__ keys, const float* __restrict__ values, int QH, int KVH,
     int pos, size_t case_stride, int splits, float scale, float* __restrict__ part) {
-    constexpr int D = DPL * 32;
-    __shared__ float st[kDecWarps][R][D + 2];
+    constexpr int D = DPL * 32, E = D / 16, W = AttentionWalk<DPL>::kWarps, S = AttentionWalk<DPL>::kDepth;
+    constexpr int kWalkers = 2 * W;
+    extern __shared__ __align__(16) float smem[];  // attention_walk_smem<DPL, R>() bytes
     const int s = blockIdx.x % splits, g = (blockIdx.x / splits) % KVH, c = blockIdx.x / (splits * KVH);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+    const int walker = 2 * warp + half;
     const int n = pos + 1, chunk = (n + splits - 1) / splits;
     const int t0 = s * chunk, t1 = min(n, t0 + chunk);
-    const size_t kw = (size_t)KVH * D;
-    const float* kb = keys + (size_t)c * case_stride + (size_t)g * D;
-    const float* vb = values + (size_t)c * case_stride + (size_t)g * D;
+    const size_t group = (size_t)c * case_stride + (size_t)g * (case_stride / KVH);
+    const float* kb = keys + group + hl * E;
+    const float* vb = values + group + hl * E;
     const float* qrow = qkv + (size_t)c * (QH + 2 * KVH) * D;
-    float q[R][DPL], m[R], l[R], acc[R][DPL];
+    // ring slot: [K of the two halves' positions | V of the same], D floats each
+    float* ring = smem + warp * (S * 4 * D) + half * D + hl * E;
+    float q[R][E], m[R], l[R], acc[R][E];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
         m[i] = -INFINITY;
         l[i] = 0.f;
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-            q[i][j] = qrow[(size_t)(g * R + i) * D + lane + 32 * j];
+        for (int j = 0; j < E; ++j) {
+            q[i][j] = qrow[(size_t)(g * R + i) * D + hl * E + j];
             acc[i][j] = 0.f;
         }
     }
-    // the next position's K and V rows are loaded while the current one is used
-    float kn[DPL], vn[DPL];
-    if (t0 + warp < t1) {
+    const int first = t0 + walker;
+    const int count = first < t1 ? (t1 - first + kWalkers - 1) / kWalkers : 0;
+    const int trips = max(count, __shfl_xor_sync(0xffffffffu, count, 16));  // uniform over the warp
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-            kn[j] = __ldcs(kb + (size_t)(t0 + warp) * kw + lane + 32 * j);
-            vn[j] = __ldcs(vb + (size_t)(t0 + warp) * kw + lane + 32 * j);
+    for (int i = 0; i < S - 1; ++i) {
+        if (i < count) {
+            const size_t row = (size_t)(first + i * kWalkers) * D;
+            lane_row_async<E>(ring + i * 4 * D, kb + row);
+            lane_row_async<E>(ring + i * 4 * D + 2 * D, vb + row);
         }
+        async_commit();
     }
-    for (int t = t0 + warp; t < t1; t += kDecWarps) {
-        float k[DPL], v[DPL];
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-            k[j] = kn[j];
-            v[j] = vn[j];
+    int rd = 0, wr = S - 1;  // ring slots of position i and of position i + S - 1
+    for (int i = 0; i < trips; ++i) {
+        if (i + S - 1 < count) {
+            const size_t row = (size_t)(first + (i + S - 1) * kWalkers) * D;
+            lane_row_async<E>(ring + wr * 4 * D, kb + row);
+            lane_row_async<E>(ring + wr * 4 * D + 2 * D, vb + row);
         }
-        if (t + kDecWarps < t1) {
+        async_commit();
+        async_wait<S - 1>();  // position i's rows have landed
+        const bool live = i < count;  // the same in all lanes of a half
+        const int slot = rd;
+        rd = rd + 1 == S ? 0 : rd + 1;
+        wr = wr + 1 == S ? 0 : wr + 1;
+        float k[E], v[E];
+        lane_row_load<E>(ring + slot * 4 * D, k);
+        lane_row_load<E>(ring + slot * 4 * D + 2 * D, v);
 #pragma unroll
-            for (int j = 0; j < DPL; ++j) {
-                kn[j] = __ldcs(kb + (size_t)(t + kDecWarps) * kw + lane + 32 * j);
-                vn[j] = __ldcs(vb + (size_t)(t + kDecWarps) * kw + lane + 32 * j);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
+        for (int h = 0; h < R; ++h) {
             float x = 0.f;
 #pragma unroll
-            for (int j = 0; j < DPL; ++j) x = fmaf(q[i][j], k[j], x);
-            for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-            const float sv = x * scale;
-            const float mn = fmaxf(m[i], sv);
-            const float carry = expf(m[i] - mn), p = expf(sv - mn);
-            l[i] = l[i] * carry + p;
+            for (int j = 0; j < E; ++j) x = fmaf(q[h][j], k[j], x);
+            for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+            // the butterfly leaves the same sum in every lane of the half
+            if (live) {
+                const float sv = x * scale;
+                if (sv > m[h]) {
+                    const float carry = expf(m[h] - sv);
+                    l[h] *= carry;
 #pragma unroll
-            for (int j = 0; j < DPL; ++j) acc[i][j] = fmaf(p, v[j], acc[i][j] * carry);
-            m[i] = mn;
+                    for (int j = 0; j < E; ++j) acc[h][j] *= carry;
+                    m[h] = sv;
+                }
+                const float p = expf(sv - m[h]);
+                l[h] += p;
+#pragma unroll
+                for (int j = 0; j < E; ++j) acc[h][j] = fmaf(p, v[j], acc[h][j]);
+            }
         }
     }
+    async_wait<0>();
+    __syncthreads();  // every warp is done with its ring: the states reuse the space
+    float* st = smem;  // [walker][R][D + 2]
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-        if (lane == 0) {
-            st[warp][i][0] = m[i];
-            st[warp][i][1] = l[i];
+        float* w = st + (walker * R + i) * (D + 2);
+        if (hl == 0) {
+            w[0] = m[i];
+            w[1] = l[i];
         }
 #pragma unroll
-        for (int j = 0; j < DPL; ++j) st[warp][i][2 + lane + 32 * j] = acc[i][j];
+        for (int j = 0; j < E; ++j) w[2 + hl * E + j] = acc[i][j];
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < R * (D + 2); idx += blockDim.x) {
         const int i = idx / (D + 2), e = idx % (D + 2);
         float M = -INFINITY;
-        for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, st[w][i][0]);
+        for (int w = 0; w < kWalkers; ++w) M = fmaxf(M, st[(w * R + i) * (D + 2)]);
         float val;
         if (e == 0) {
             val = M;
         } else {
             val = 0.f;
-            for (int w = 0; w < kDecWarps; ++w)
-                if (st[w][i][0] != -INFINITY) val = fmaf(st[w][i][e], expf(st[w][i][0] - M), val);
+            for (int w = 0; w < kWalkers; ++w) {
+                const float* ws = st + (w * R + i) * (D + 2);
+                if (ws[0] != -INFINITY) val = fmaf(ws[e], expf(ws[0] - M), val);
+            }
         }
         part[(((size_t)c * QH + g * R + i) * splits + s) * (D + 2) + e] = val;
     }
@@ -989,18 +1067,24 @@ static bool launch_cached_attention(cudaStream_t s, const float* qkv, const floa
                                     int QH, int KVH, int pos, size_t case_stride, int splits, float scale,
                                     float* part, __nv_bfloat16* hi, __nv_bfloat16* lo) {
     const int R = QH / KVH;
-    const int blocks = B * KVH * splits, threads = 32 * kDecWarps;
+    const int blocks = B * KVH * splits, threads = 32 * AttentionWalk<DPL>::kWarps;
+    auto launch = [&](auto kernel, size_t smem) {
+        if (cudaFuncSetAttribute((const void*)kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return false;
+        kernel<<<blocks, threads, smem, s>>>(qkv, keys, values, QH, KVH, pos, case_stride, splits, scale, part);
+        return true;
+    };
+    bool ok;
     if (R == 1)
-        cached_attention_part_kernel<DPL, 1><<<blocks, threads, 0, s>>>(qkv, keys, values, QH, KVH, pos, case_stride,
-                                                                        splits, scale, part);
+        ok = launch(cached_attention_part_kernel<DPL, 1>, attention_walk_smem<DPL, 1>());
     else if (R == 2)
-        cached_attention_part_kernel<DPL, 2><<<blocks, threads, 0, s>>>(qkv, keys, values, QH, KVH, pos, case_stride,
-                                                                        splits, scale, part);
+        ok = launch(cached_attention_part_kernel<DPL, 2>, attention_walk_smem<DPL, 2>());
     else if (R == 4 && DPL <= 4)
-        cached_attention_part_kernel<DPL, 4><<<blocks, threads, 0, s>>>(qkv, keys, values, QH, KVH, pos, case_stride,
-                                                                        splits, scale, part);
+        ok = launch(cached_attention_part_kernel<DPL, 4>, attention_walk_smem<DPL, 4>());
     else
         return false;
+    if (!ok) return false;
     cached_attention_merge_kernel<DPL><<<B * QH, 128, 0, s>>>(part, QH, splits, hi, lo);
     return true;
 }
@@ -1015,6 +1099,7 @@ int BatchedScorer::generate_batch(const uint32_t* prompts, size_t batch, size_t 
     const int R = QH / KVH, dpl = D / 32;
     LSX_ENSURE(R == 1 || R == 2 || (R == 4 && dpl <= 4), "batched generation: unsupported group ratio");
     const size_t cap = P + maximum, kw = (size_t)KVH * D, B = batch;
+    // per layer: keys, then values, each [batch][kvheads][capacity][head_dim]
     const size_t case_stride = cap * kw, layer_stride = 2 * B * case_stride;
     // about eight attention blocks per SM at any batch: each warp's cache walk is
     // latency-bound, so parallel blocks carry the bandwidth
@@ -1089,21 +1174,24 @@ int BatchedScorer::generate_batch(const uint32_t* prompts, size_t batch, size_t 
             bool ok;
             if (D == 128) {
                 qk_rope_kernel<4><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
-                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride);
+                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride,
+                                                          cap * D, D);
                 ok = launch_cached_attention<4>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
                                                 hi, lo);
             } else if (D == 64) {
                 qk_rope_kernel<2><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
-                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride);
+                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride,
+                                                          cap * D, D);
                 ok = launch_cached_attention<2>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
                                                 hi, lo);
             } else {
                 qk_rope_kernel<8><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
-                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride);
+                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride,
+                                                          cap * D, D);
                 ok = launch_cached_attention<8>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
                                                 hi, lo);
             }
-            LSX_ENSURE(ok, "batched generation: unsupported group ratio");
+            LSX_ENSURE(ok, "batched generation: attention launch (group ratio, shared memory)");
             LSX_CUDA(cudaGetLastError(), "batched decode attention");
             LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));
             rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.post_gain, c.eps, hi, lo);
@@ -1225,10 +1313,10 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
                 float* bk = batch_keys_ + li * batch_layer_stride_;
                 float* bv = bk + batch_layer_stride_ / 2;
                 kv_store_kernel<<<(int)std::min<size_t>((kv + 255) / 256, 148 * 16), 256, 0, s>>>(
-                    work, kv, QH, KVH, D, bk, bv, (int)T, 0, batch_case_stride_);
+                    work, kv, QH, KVH, D, bk, bv, (int)T, 0, batch_case_stride_, batch_case_stride_ / KVH, D);
             } else {
                 kv_store_kernel<<<(int)std::min<size_t>((kv + 255) / 256, 148 * 16), 256, 0, s>>>(
-                    work, kv, QH, KVH, D, Ly.keys, Ly.values, (int)T, 0, 0);
+                    work, kv, QH, KVH, D, Ly.keys, Ly.values, (int)T, 0, 0, D, (size_t)KVH * D);
             }
             LSX_CUDA(cudaGetLastError(), "KV append");
         }
