@@ -129,12 +129,20 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- workload ----
-def build_checkpoint(rank: int, layers: int = 28) -> Path:
+def build_checkpoint(rank: int = 0, layers: int = 28) -> Path:
+    """The Qwen3-0.6B-architecture checkpoint of the decode workload (seed 7),
+    written once per machine (every rank shares it)."""
     from laplacesscissors_b200 import synth
-    d = Path(tempfile.gettempdir()) / f"lsx-bench-qwen3-0.6b-seed7-l{layers}-r{rank}"
-    if not (d / "model.safetensors").exists():
-        synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(synth.QWEN3_0_6B, layers=layers)), seed=7)
-    return d
+    return synth.cached_checkpoint("QWEN3_0_6B", layers=layers) if layers != 28 else \
+        synth.cached_checkpoint("QWEN3_0_6B")
+
+
+def decode_config(world: int) -> dict:
+    """`config` of the headline line (both arms print the same)."""
+    return {"workload": "Qwen3-0.6B bs1 greedy decode, 24-token prompt + 32 tokens",
+            "decode_steps_per_step": STEPS_PER_GENERATION, "batch": 1, "kv_cache": "f32",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "weights 1.19 GB per token > 126 MB L2 (no flush needed)"}
 
 
 def readout_inputs(rank: int = 0, world: int = 1):
@@ -156,23 +164,24 @@ def cpu_threads():
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
-def cpu_decode_rate(ckpt: Path, seconds: float = 15.0):
-    """Oracle decode of the same checkpoint and prompt on the host cores."""
-    from laplacesscissors_b200 import synth
+def cpu_decode_rate(ckpt: Path, generations: int = 1):
+    """The oracle's decode of the same checkpoint and prompt on the host cores: the
+    whole 55-step generation (prompt token by token, then greedy), `generations`
+    times.  Inputs come from the oracle's own generator (no library code runs)."""
     from oracle import binding as oracle
+    from oracle import synth as osynth
     threads = cpu_threads()
     m = oracle.OracleModel(ckpt, 64, threads=threads)
-    prompt = synth.prompt_tokens(7, PROMPT, VOCAB)
-    m.advance(int(prompt[0]))  # warm-up
+    prompt = osynth.prompt_tokens(7, PROMPT, VOCAB)
     m.cursor = 0
+    m.advance(int(prompt[0]))  # warm-up: pages the weights in
     t0 = time.perf_counter()
-    n = 0
-    while n < STEPS_PER_GENERATION and (n < 3 or time.perf_counter() - t0 < seconds):
-        tok = int(prompt[n]) if n < PROMPT else int(np.argmax(z))
-        _, z = m.advance(tok)
-        n += 1
+    for _ in range(generations):
+        m.cursor = 0
+        m.generate(prompt, GENERATE)
     dt = time.perf_counter() - t0
-    return n / dt, threads, f"first {n} decode steps of the generation (oracle, f64 reductions)"
+    return generations * STEPS_PER_GENERATION / dt, threads, \
+        f"{generations} whole generation(s) of 55 decode steps (oracle, f64 reductions, {threads} threads)"
 
 
 def cpu_readout_rate(w, hidden, targets, edit, seconds: float = 15.0):
@@ -991,38 +1000,46 @@ def scoring_batched(args, rank, local, world):
 
 
 def reference_arm(args, rank, world):
-    """The reference's CPU path on the host cores (oracle restatement), rank 0 only."""
+    """The reference's CPU path on the host cores, rank 0 only: the oracle's
+    restatement of the reference's CPU forward (tests/qwen_reference.rs:39-202 with
+    the KV cache of Model::decode), running the headline workload itself -- one
+    bench step is the whole 55-step generation of the 24-token prompt -- on the
+    same checkpoint bytes, built by the oracle's own generator.  Nothing of this
+    repository's library is loaded."""
     if rank != 0:
         return
-    ckpt = build_checkpoint(0)
-    from laplacesscissors_b200 import synth
     from oracle import binding as oracle
+    from oracle import synth as osynth
+    ckpt = osynth.cached_checkpoint(osynth.QWEN3_0_6B, "qwen3_0_6b")
     threads = cpu_threads()
     m = oracle.OracleModel(ckpt, 64, threads=threads)
-    prompt = synth.prompt_tokens(7, PROMPT, VOCAB)
-    per_step = 4  # decode steps per bench step: a bounded sample of the generation
+    prompt = osynth.prompt_tokens(7, PROMPT, VOCAB)
 
-    def one(step):
+    def one():
         m.cursor = 0
-        for i in range(per_step):
-            m.advance(int(prompt[i]))
+        return m.generate(prompt, GENERATE)[0]
 
-    for i in range(args.warmup):
-        one(i)
+    for _ in range(args.warmup):
+        one()
     t0 = time.perf_counter()
-    for i in range(args.steps):
-        one(i)
+    for _ in range(args.steps):
+        tokens = one()
     dt = time.perf_counter() - t0
-    v = args.steps * per_step / dt
+    v = args.steps * STEPS_PER_GENERATION / dt
+    sample = (f"the whole generation ({STEPS_PER_GENERATION} oracle decode steps) per bench step on {threads} "
+              "host threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 weights, f32 activations, f64 reductions", "data": "synthetic",
-        "config": {"workload": "Qwen3-0.6B bs1 greedy decode, 24-token prompt + 32 tokens",
-                   "sample": f"{per_step} decode steps per bench step"},
-        "cpu_baseline": {"kind": "port", "cores": threads, "value": v,
-                         "sample": f"{per_step} oracle decode steps per bench step on {threads} threads"},
+        "vs_baseline": None, "dtype": "bf16 weights, f32 activations and KV (f32 accumulate)",
+        "data": "synthetic: random-init Qwen3-0.6B architecture (seed 7), 24 random prompt ids",
+        "config": decode_config(world),
+        "cpu_baseline": {"kind": "port", "cores": threads, "value": v, "unit": "tok/s", "sample": sample},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "first_tokens": [int(t) for t in tokens[:8]],
+        "note": "the reference's Rust crate cannot be built here (no cargo); its GPU kernels are timed on the "
+                "GPU by the repo arm's triton_baseline object.  One CPU process on the host cores whatever the "
+                "GPU count (rank 0 alone runs)",
     }))
 
 

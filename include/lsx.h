@@ -250,13 +250,24 @@ int lsx_readout_margin(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor*
                        const uint32_t* targets, const lsx_rotation* rotation, double* margin_out,
                        uint32_t* argmax_out, float* target_logit_out);
 /* Same computation on device-resident inputs and outputs (no host copies, no
-   synchronisation).  workspace must hold lsx_readout_workspace_bytes() bytes. */
+   synchronisation).  workspace must hold lsx_readout_workspace_bytes() bytes.  The
+   kernels' status (a device wait that gave up; non-finite scores, which the
+   reference rejects, src/model.rs:680-683) stays in the workspace: read it with
+   lsx_readout_status. */
 int lsx_readout_margin_device(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias,
                               size_t vocab, size_t width, const void* hidden, lsx_dtype hidden_kind,
                               size_t rows, const uint32_t* targets, const lsx_rotation* rotation,
                               double* margin_out, uint32_t* argmax_out, float* target_logit_out,
                               void* workspace, size_t workspace_bytes);
 size_t lsx_readout_workspace_bytes(size_t vocab, size_t width, size_t rows, const lsx_rotation* rotation);
+/* Status of the last readout call that used `workspace` (lsx_readout_margin_device,
+   lsx_readout_shard_device), or, with workspace NULL, of the last
+   lsx_readout_margin_fixed call on the context's device: waits for the context's
+   stream, then returns LSX_E_CUDA when a kernel's bounded device wait gave up,
+   LSX_E_NONFINITE when a score was not finite (Model::readout's rejection,
+   src/model.rs:680-683), else LSX_OK.  The host-buffer entries check this
+   themselves. */
+int lsx_readout_status(lsx_ctx* ctx, const void* workspace);
 /* CompactReadout::evaluate (src/diagnosis.rs:643-665) fused with minimum_margin,
    other and argmax (src/diagnosis.rs:58-80, 490-492): for observation o the scores
    z_o = image c_o + baseline_o are reduced on the device, never stored, to
@@ -300,14 +311,15 @@ int lsx_readout_merge_device(lsx_ctx* ctx, const uint64_t* other_key, const floa
 /* The device-pointer readout margin without an edit, for callers that must not
    allocate device memory (their memory is already fully committed, or an
    allocation at that point would be illegal or would stall other work).  It has
-   no counterpart in the reference, which allocates per call (src/gpu.rs:204-216).
+   no counterpart in the reference.
    Scratch is a fixed 4 MiB area inside the library's device image, one per device:
    calls needing more (bf16 hidden: about 12 bytes per row; F32 hidden: a further
    4 x width bytes per row) fail with LSX_E_ARGUMENT and enqueue nothing.  No
    scratch word needs to start at zero.  Calls that may overlap on one device share
-   that scratch and race: order them on one stream.  The first call on a device
-   looks the scratch up (which may load the library's device code): make it before
-   any stream capture begins. */
+   that scratch and race: order them on one stream.  The kernels' status words stay
+   in the scratch until the next call on the device: lsx_readout_status(ctx, NULL)
+   reports them.  The first call on a device looks the scratch up (which may load
+   the library's device code): make it before any stream capture begins. */
 int lsx_readout_margin_fixed(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias,
                              size_t vocab, size_t width, const void* hidden, lsx_dtype hidden_kind,
                              size_t rows, const uint32_t* targets, double* margin_out,

@@ -103,6 +103,7 @@ SIGNATURES = {
     "lsx_readout_margin": (I, [P, P, P, SZ, SZ, P, I, SZ, UP, P, DP, UP, FP]),
     "lsx_readout_margin_device": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P, P, P, SZ]),
     "lsx_readout_workspace_bytes": (SZ, [SZ, SZ, SZ, P]),
+    "lsx_readout_status": (I, [P, P]),
     "lsx_readout_margin_fixed": (I, [P, P, P, SZ, SZ, P, I, SZ, P, P, P, P]),
     "lsx_compact_margin": (I, [P, P, P, SZ, SZ, SZ, FP, UP, DP, UP, UP]),
     "lsx_readout_shard_device": (I, [P, P, P, SZ, SZ, SZ, P, I, SZ, P, P, P, P, P, SZ]),

@@ -49,6 +49,13 @@ struct DecodeState {
     unsigned int attn_counter[64];
     unsigned int epoch;  // last publication epoch of the persistent engine's tagged buffers
     unsigned int pad2;
+    // Failure-path test hook of the persistent engine (0 in normal runs): CTA
+    // hold_cta - 1 skips publishing its argmax partial at step hold_step, and every
+    // exchange wait gives up after spin_limit clock cycles instead of about two
+    // seconds, so the other CTAs' waits expire and the kernel records a status.
+    int hold_cta;
+    int hold_step;
+    long long spin_limit;
 };
 
 struct FusedLayer {

@@ -955,6 +955,22 @@ int run_fused(lsx_model* m, int steps) {
     cudaStream_t s = m->ctx->stream;
     DecodeState* dev = m->persistent ? m->persistent->state() : m->decoder->state();
     m->host_state->epoch = m->epoch;
+    // Failure-path test hook of the persistent engine: LSX_DECODE_FAULT_TEST =
+    // "cta,step,cycles" makes CTA `cta` withhold its argmax partial at `step` and
+    // caps every exchange wait at `cycles` clock cycles, so the run ends with a
+    // device status instead of output (no fault: only bounded waits expire).
+    m->host_state->hold_cta = 0;
+    m->host_state->hold_step = 0;
+    m->host_state->spin_limit = 0;
+    if (const char* v = getenv("LSX_DECODE_FAULT_TEST")) {
+        int cta = -1, step = 0;
+        long long cycles = 0;
+        if (sscanf(v, "%d,%d,%lld", &cta, &step, &cycles) == 3 && cta >= 0 && step >= 0 && cycles > 0) {
+            m->host_state->hold_cta = cta + 1;
+            m->host_state->hold_step = step;
+            m->host_state->spin_limit = cycles;
+        }
+    }
     LSX_K(cudaMemcpyAsync(dev, m->host_state, sizeof(DecodeState), cudaMemcpyHostToDevice, s), "state upload");
     if (m->persistent) LSX_TRY(m->persistent->run(steps));
     else LSX_TRY(m->decoder->enqueue_steps(steps));

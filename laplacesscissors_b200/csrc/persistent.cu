@@ -56,6 +56,11 @@ constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kCompute = kWarps * 32;
 constexpr long long kSpin = 4000000000ll;     // ~2 s at B200 clocks
 
+// Clock cycles an exchange wait may spin before it gives up: kSpin, or the
+// failure-path test hook's shorter limit (DecodeState::spin_limit).  Set by thread 0
+// before the block's first barrier.
+__shared__ long long s_spin;
+
 enum { kOpQkv = 0, kOpO = 1, kOpGu = 2, kOpDown = 3, kOpHead = 4, kOps = 5 };
 
 // This CTA's share of one GEMV op.
@@ -173,7 +178,7 @@ __device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch
             }
             if (start == 0) {
                 start = clock64();
-            } else if (clock64() - start > kSpin || aborted(st)) {
+            } else if (clock64() - start > s_spin || aborted(st)) {
                 ok = false;
                 break;
             }
@@ -229,7 +234,7 @@ __device__ bool poll_segments(const unsigned long long* s0, int n0, float* d0, c
                 if ((uint32_t)(v[j] >> 32) != epoch) v[j] = ld_relaxed(src[j]);
             if (start == 0) {
                 start = clock64();
-            } else if (clock64() - start > kSpin || aborted(st)) {
+            } else if (clock64() - start > s_spin || aborted(st)) {
                 ok = false;
                 break;
             }
@@ -1150,6 +1155,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
         }
         *s_stop = 0;
         *s_issued = 0;
+        s_spin = a.state->spin_limit > 0 ? a.state->spin_limit : kSpin;
         const int qkv_rows = (a.QH + 2 * a.KVH) * a.D;
         ops[kOpQkv] = make_op(qkv_rows, 1, a.H, c, G, a.slot_bytes, a.slots);
         ops[kOpO] = make_op(a.H, 1, a.QH * a.D, c, G, a.slot_bytes, a.slots);
@@ -1164,6 +1170,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
     const int first_frame = P - 1 - st->frame_back;  // step of the first recorded frame
     const int pos0 = st->position;
     const uint32_t base = st->epoch;
+    const int hold_cta = st->hold_cta - 1, hold_step = st->hold_step;
     const uint32_t per_step = 5u * (uint32_t)a.L + 1u;
 
     if (warp == kWarps) {  // ---------------------------------- producer warp
@@ -1194,7 +1201,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                                 }
                                 if (start == 0) {
                                     start = clock64();
-                                } else if (clock64() - start > kSpin) {
+                                } else if (clock64() - start > s_spin) {
                                     raise_abort(st, kDeviceTimeoutWeights);
                                     go = false;
                                     break;
@@ -1411,7 +1418,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             const unsigned long long wbest = warp_max_u64(e.best);
             if (lane == 0) rb[warp] = wbest;
             if (!compute_and(!e.bad) && tid == 0) atomicOr(&st->nonfinite, 1);
-            if (tid == 0) {
+            if (tid == 0 && !(c == hold_cta && step == hold_step)) {
                 unsigned long long b = 0ull;
                 for (int i = 0; i < kWarps; ++i) b = rb[i] > b ? rb[i] : b;
                 st_relaxed(a.t_arg + c, arg_word(b, e_head));
@@ -1425,7 +1432,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 while ((uint32_t)(v & 0x1FFFull) != (e_head & 0x1FFFu)) {
                     v = ld_relaxed(src);
                     if (start == 0) start = clock64();
-                    else if (clock64() - start > kSpin || aborted(st)) {
+                    else if (clock64() - start > s_spin || aborted(st)) {
                         ok = false;
                         break;
                     }
@@ -1623,7 +1630,9 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
     // Shared memory: ring slots first, then x, scratch, owned residual rows,
     // barriers and the tables.  As many slots as fit, at most 16.
     const int slot_bytes = slot_bytes_for(c);
-    const size_t limit = ctx->smem_optin;
+    cudaFuncAttributes fattr{};
+    LSX_CUDA(cudaFuncGetAttributes(&fattr, (const void*)kernel_for(c)), "persistent kernel attributes");
+    const size_t limit = ctx->smem_optin - fattr.sharedSizeBytes;  // the static s_spin word included
     slots_ = 0;
     for (int s = 16; s >= 2; --s)
         if ((size_t)layout_for(c, s, slot_bytes, grid_, layers.size()).total <= limit) {

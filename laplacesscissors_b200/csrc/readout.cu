@@ -1313,10 +1313,14 @@ struct Layout {
         tlog_off, status_off, total;
 };
 
+// The two status words sit at the start of every layout, so lsx_readout_status can
+// read them from any workspace without knowing the sizes of the call that used it.
 Layout layout_for(size_t vocab, size_t width, size_t rows, size_t rank, bool f32_hidden) {
     Layout L{};
     L.ext_k = rank ? ((3 * rank + RK - 1) / RK) * RK : 0;
     size_t at = 0;
+    L.status_off = at;
+    at = align256(at + 16);
     L.planes_off = at;
     L.planes_bytes = f32_hidden ? rows * width * 2 : 0;
     at = align256(at + 2 * L.planes_bytes);
@@ -1336,8 +1340,6 @@ Layout layout_for(size_t vocab, size_t width, size_t rows, size_t rank, bool f32
     at = align256(at + rows * 8);
     L.tlog_off = at;
     at = align256(at + rows * 4);
-    L.status_off = at;
-    at = align256(at + 16);
     L.total = at;
     return L;
 }
@@ -1704,6 +1706,8 @@ int head_images_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, size_t vocab, si
     return LSX_OK;
 }
 
+int fixed_scratch_address(lsx_ctx* ctx, void** out);
+
 int readout_margin_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bias, size_t vocab, size_t width,
                            const void* hidden, int hidden_kind, size_t rows, const uint32_t* targets,
                            const lsx_rotation* rotation, double* margin, uint32_t* argmax, float* target_logit,
@@ -1808,6 +1812,23 @@ int lsx_compact_margin(lsx_ctx* ctx, const lsx_tensor* image, const lsx_tensor* 
     device_release(ctx, block);
     if (e != cudaSuccess) return fail(LSX_E_CUDA, cuda_message("compact readout", e));
     if (status[1] != 0) return fail(LSX_E_NONFINITE, "check the finite scores of the compact readout");
+    return LSX_OK;
+}
+
+int lsx_readout_status(lsx_ctx* ctx, const void* workspace) {
+    LSX_ENSURE(ctx, "invalid argument");
+    LSX_CUDA(cudaSetDevice(ctx->device), "select device");
+    const void* words = workspace;
+    if (!words) {
+        void* fixed = nullptr;
+        LSX_TRY(fixed_scratch_address(ctx, &fixed));
+        words = fixed;
+    }
+    int status[2] = {0, 0};
+    LSX_CUDA(cudaMemcpyAsync(status, words, 8, cudaMemcpyDeviceToHost, ctx->stream), "readout status download");
+    LSX_CUDA(cudaStreamSynchronize(ctx->stream), "readout status");
+    if (status[0] != 0) return fail(LSX_E_CUDA, "readout kernel reported status " + std::to_string(status[0]));
+    if (status[1] != 0) return fail(LSX_E_NONFINITE, "check the finiteness of the readout scores");
     return LSX_OK;
 }
 

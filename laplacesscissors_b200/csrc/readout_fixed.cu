@@ -13,10 +13,13 @@
 //    F32 hidden states) exceeds it is rejected with LSX_E_ARGUMENT before anything
 //    is enqueued.
 //  - Nothing in the scratch has to start at zero: every call's first kernel writes
-//    each word the later kernels read.
+//    each word the later kernels read, the two status words included.
 //  - The scratch is shared by every call on the same device.  Two calls whose work
 //    can overlap on the GPU (different streams or contexts of one device, without
 //    ordering between them) race on it and give wrong results; serialise them.
+//  - The kernels' status words (a device wait that gave up, non-finite scores) stay
+//    in the scratch until the next call on the device: lsx_readout_status(ctx, NULL)
+//    waits for the context's stream and reports them.
 //  - The first call on each device looks up the scratch's device address, which
 //    may make the CUDA runtime load this module onto that device.  Make the first
 //    call on each device before any stream capture begins and before any section
@@ -63,6 +66,13 @@ int scratch_for(int device, void** out) {
 }
 
 }  // namespace
+
+// Device address of this device's fixed scratch (the status words sit at its start).
+int fixed_scratch_address(lsx_ctx* ctx, void** out) {
+    LSX_CUDA(cudaSetDevice(ctx->device), "select device");
+    return scratch_for(ctx->device, out);
+}
+
 }  // namespace lsx
 
 using namespace lsx;
@@ -73,9 +83,18 @@ int lsx_readout_margin_fixed(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_t
                              size_t width, const void* hidden, lsx_dtype hidden_kind, size_t rows,
                              const uint32_t* targets, double* margin_out, uint32_t* argmax_out,
                              float* target_logit_out) {
-    LSX_ENSURE(ctx && hidden && targets, "invalid argument");
+    LSX_ENSURE(ctx && weight && hidden && targets, "invalid argument");
     LSX_ENSURE(hidden_kind == LSX_F32 || hidden_kind == LSX_BF16, "hidden states are F32 or BF16");
-    LSX_ENSURE(rows > 0, "check the row count");
+    // The checks readout_enqueue makes, here before the scratch size is computed
+    // from these sizes, so that no product below can wrap.
+    LSX_ENSURE(weight->kind == LSX_BF16, "the readout weight must be a BF16 tensor");
+    LSX_ENSURE(rows > 0 && rows <= 2147483647ull && vocab > 1 && vocab <= 2147483647ull, "check the row count");
+    LSX_ENSURE(width > 0 && width % 8 == 0, "the readout width must be a multiple of 8");
+    size_t cells = 0, plane_bytes = 0;
+    LSX_ENSURE(!__builtin_mul_overflow(vocab, width, &cells) && weight->count == cells,
+               "check the readout weight dimensions");
+    LSX_ENSURE(!__builtin_mul_overflow(rows, width, &cells) && !__builtin_mul_overflow(cells, (size_t)4, &plane_bytes),
+               "check the row count");
     const size_t need = readout_workspace_need(vocab, width, rows, 0, hidden_kind == LSX_F32);
     if (need > kReadoutFixedScratch)
         return fail(LSX_E_ARGUMENT, "lsx_readout_margin_fixed needs " + std::to_string(need) +

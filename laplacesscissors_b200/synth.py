@@ -146,23 +146,61 @@ def make_qwen3_checkpoint(root: str | os.PathLike, config: dict, seed: int = 7, 
                           gain_std: float = 0.0) -> Path:
     """Writes a random-init Qwen3-architecture checkpoint: matrices N(0, std^2) in
     bf16, norm gains 1.0 (plus N(0, gain_std^2) when gain_std > 0), tensor i in
-    sorted-name order drawing stream i of `seed`."""
+    sorted-name order drawing stream i of `seed`.  Tensors are generated and
+    written one at a time, so memory stays at one tensor (the 8B model's 16 GB
+    never sits in host memory at once); the file equals write_safetensors' of the
+    same tensors."""
     root = Path(root)
     root.mkdir(parents=True, exist_ok=True)
     shapes = qwen3_tensor_shapes(config)
-    tensors = {}
-    for stream, name in enumerate(sorted(shapes)):
-        shape = shapes[name]
-        count = int(np.prod(shape))
-        if len(shape) == 1:
-            g = np.ones(count, dtype=np.float32)
-            if gain_std > 0:
-                g = g + normal_f32(seed, stream, count, gain_std)
-            tensors[name] = f32_to_bf16(g).reshape(shape)
-        else:
-            tensors[name] = normal_bf16(seed, stream, count, std).reshape(shape)
-    write_safetensors(root / "model.safetensors", tensors)
+    names = sorted(shapes)
+    header: dict = {}
+    offset = 0
+    for n in names:
+        nbytes = 2 * int(np.prod(shapes[n]))
+        header[n] = {"dtype": "BF16", "shape": list(shapes[n]), "data_offsets": [offset, offset + nbytes]}
+        offset += nbytes
+    blob = json.dumps(header, separators=(",", ":")).encode()
+    blob += b" " * ((8 - len(blob) % 8) % 8)
+    with open(root / "model.safetensors", "wb") as f:
+        f.write(struct.pack("<Q", len(blob)))
+        f.write(blob)
+        for stream, name in enumerate(names):
+            count = int(np.prod(shapes[name]))
+            if len(shapes[name]) == 1:
+                g = np.ones(count, dtype=np.float32)
+                if gain_std > 0:
+                    g = g + normal_f32(seed, stream, count, gain_std)
+                f.write(f32_to_bf16(g).tobytes())
+            else:
+                f.write(normal_bf16(seed, stream, count, std).tobytes())
     (root / "config.json").write_text(json.dumps(config, indent=1))
+    return root
+
+
+def cached_checkpoint(shape: str, seed: int = 7, **overrides) -> Path:
+    """The checkpoint make_qwen3_checkpoint writes for the named shape (QWEN3_0_6B,
+    QWEN3_4B, QWEN3_8B) with `overrides`, kept under the system temporary folder so
+    later runs on the same machine reuse it.  It is written to a private folder and
+    renamed into place when complete, so an interrupted write is never reused."""
+    import shutil
+    import tempfile
+    cfg = dict(globals()[shape], **overrides)
+    tag = "".join(f"-{k}{v}" for k, v in sorted(overrides.items()))
+    root = Path(tempfile.gettempdir()) / f"lsx-bench-{shape.lower()}-seed{seed}{tag}"
+    if (root / "model.safetensors").exists() and (root / "config.json").exists():
+        return root
+    work = Path(tempfile.mkdtemp(prefix=root.name + ".partial-", dir=root.parent))
+    try:
+        make_qwen3_checkpoint(work, qwen3_config(**cfg), seed=seed)
+        try:
+            os.replace(work, root)
+        except OSError:  # another process completed it first
+            if not (root / "config.json").exists():
+                raise
+    finally:
+        if work.exists():
+            shutil.rmtree(work, ignore_errors=True)
     return root
 
 
@@ -186,6 +224,7 @@ def readout_targets(seed: int, rows: int, vocab: int, first: int = 0) -> np.ndar
 
 __all__ = [
     "normal_bf16", "normal_f32", "uniform_u32", "bf16_to_f32", "f32_to_bf16", "write_safetensors",
-    "read_safetensors", "qwen3_config", "qwen3_tensor_shapes", "make_qwen3_checkpoint", "prompt_tokens",
+    "read_safetensors", "qwen3_config", "qwen3_tensor_shapes", "make_qwen3_checkpoint", "cached_checkpoint",
+    "prompt_tokens",
     "readout_hidden", "readout_targets", "QWEN3_0_6B", "QWEN3_4B", "QWEN3_8B",
 ]

@@ -88,6 +88,8 @@ def _load() -> C.CDLL:
         "lsxo_plane_feasible": (I, [C.POINTER(FeasibleStruct), V, V, SZ, V, V, V, V, SZ, D, D]),
         "lsxo_restored_loss": (D, [V, SZ, SZ, F, C.c_uint32]),
         "lsxo_integrated_credits": (None, [V, V, V, V, SZ, SZ, SZ, V, V]),
+        "lsxo_synth_normal": (None, [C.c_uint64, C.c_uint64, C.c_uint64, SZ, D, I, V]),
+        "lsxo_synth_uniform_u32": (None, [C.c_uint64, C.c_uint64, C.c_uint64, SZ, C.c_uint32, V]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -717,3 +717,42 @@ void lsxo_integrated_credits(const float* before, const float* after, const uint
     free(integral);
     free(prob);
 }
+
+/* ------------------------------------------------------------ input generator -- */
+static uint64_t synth_mix(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+#define SYNTH_STEP 0x9E3779B97F4A7C15ull
+
+static uint64_t synth_bits(uint64_t key, uint64_t i) { return synth_mix(key + (i + 1) * SYNTH_STEP); }
+
+static uint16_t synth_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+void lsxo_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, size_t count, double std, int kind,
+                       void* out) {
+    const uint64_t key = synth_mix(seed ^ synth_mix(stream + SYNTH_STEP));
+    const long long n = (long long)count;
+#pragma omp parallel for schedule(static) if (count > (1u << 16))
+    for (long long j = 0; j < n; ++j) {
+        const uint64_t i = offset + (uint64_t)j, pair = i >> 1;
+        const double u1 = (double)((synth_bits(key, 2 * pair) >> 11) + 1) * 0x1.0p-53;
+        const double u2 = (double)(synth_bits(key, 2 * pair + 1) >> 11) * 0x1.0p-53;
+        const double radius = sqrt(-2.0 * log(u1)), angle = 6.283185307179586476925286766559 * u2;
+        const float v = (float)(std * ((i & 1) ? radius * sin(angle) : radius * cos(angle)));
+        if (kind == LSXO_BF16) ((uint16_t*)out)[j] = synth_bf16(v);
+        else ((float*)out)[j] = v;
+    }
+}
+
+void lsxo_synth_uniform_u32(uint64_t seed, uint64_t stream, uint64_t offset, size_t count, uint32_t bound,
+                            uint32_t* out) {
+    const uint64_t key = synth_mix(seed ^ synth_mix(stream + SYNTH_STEP));
+    for (size_t j = 0; j < count; ++j) out[j] = (uint32_t)(((synth_bits(key, offset + j) >> 32) * (uint64_t)bound) >> 32);
+}

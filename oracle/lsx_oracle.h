@@ -156,6 +156,16 @@ void lsxo_integrated_credits(const float* before, const float* after, const uint
                              const double* weights, size_t points, size_t vocab, size_t panels, double* credits,
                              double* gradients);
 
+/* The benchmark inputs' counter-based generator (SplitMix64 finaliser; Box-Muller
+   normals rounded to f32, then to bf16 when kind is LSXO_BF16; uniform integers by
+   multiply-shift), written independently of the library's so that the CPU
+   baseline and the reference arms can build their inputs without it, and so that
+   a test can check the two generators against each other. */
+void lsxo_synth_normal(uint64_t seed, uint64_t stream, uint64_t offset, size_t count, double std, int kind,
+                       void* out);
+void lsxo_synth_uniform_u32(uint64_t seed, uint64_t stream, uint64_t offset, size_t count, uint32_t bound,
+                            uint32_t* out);
+
 /* Version string of the oracle build. */
 const char* lsxo_version(void);
 

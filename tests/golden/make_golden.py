@@ -1,7 +1,8 @@
 """Generates the golden vectors in tests/golden/ from the reference itself.
 
-Runs ONLY in a container that has the reference tree (default
-/root/reference, or $LSX_REFERENCE): it imports the reference's unmodified
+Runs ONLY in a container that has the reference tree, named by the required
+environment variable LSX_REFERENCE (the folder holding the reference's
+kernels/ops.py, src/ and tests/): it imports the reference's unmodified
 kernels/ops.py and executes its Triton kernels with Triton's CPU interpreter
 (TRITON_INTERPRET=1), launched with the constexprs and grids of src/gpu.rs:360-559
 and, for whole-model cases, in the op order of Model::decode (src/model.rs:729-853).
@@ -31,7 +32,9 @@ from pathlib import Path
 os.environ["TRITON_INTERPRET"] = "1"
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REFERENCE = Path(os.environ.get("LSX_REFERENCE", "/root/reference"))
+if not os.environ.get("LSX_REFERENCE"):
+    sys.exit("make_golden.py: set LSX_REFERENCE to the reference tree (the folder holding kernels/ops.py)")
+REFERENCE = Path(os.environ["LSX_REFERENCE"])
 sys.path.insert(0, str(REFERENCE / "kernels"))
 sys.path.insert(0, str(REPO))
 

@@ -43,3 +43,24 @@ def test_wide_shapes_match_oracle(gpu, oracle, shape, vocab):
         close(frames[i].hidden, ref_frames[i][0], 2e-2)
     else:
         assert list(map(int, tokens)) == ref_tokens
+
+
+def test_full_depth_qwen3_4b_matches_oracle(gpu, oracle):
+    """All 36 layers of the Qwen3-4B architecture (hidden 2560, 32/8 heads, I 9728,
+    vocab 151936, tied; random init, seed 7 — the long-context decode workload's
+    checkpoint) through the persistent engine: a 4-token prompt and 4 greedy
+    tokens, the first two steps' tokens, logits and hidden states against the
+    oracle."""
+    d = synth.cached_checkpoint("QWEN3_4B")
+    model = lsx.Model.load(d, gpu, 16)
+    assert model.fused and model.info().persistent
+    prompt = synth.prompt_tokens(7, 4, 151936)
+    tokens, _, frames = model.generate(prompt, 4, frames=True)
+    ref_tokens, ref_frames = oracle.OracleModel(d, 16).generate(prompt, 2)
+    for i, rt in enumerate(ref_tokens):
+        if int(tokens[i]) != rt:
+            assert abs(oracle.minimum_margin(ref_frames[i][1], rt)) < 1e-3, (i, tokens[i], rt)
+            break
+        assert rel_l2(frames[i].logits, ref_frames[i][1]) < 1e-2
+        close(frames[i].logits, ref_frames[i][1], 2e-2)
+        close(frames[i].hidden, ref_frames[i][0], 2e-2)

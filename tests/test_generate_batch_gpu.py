@@ -46,3 +46,45 @@ def test_wide_batch_matches_oracle(gpu, oracle, shape, vocab):
     prompts = np.stack([synth.prompt_tokens(30 + b, 12, vocab) for b in range(4)])
     tokens = model.generate_batch(prompts, 6)
     check_rows(tokens, prompts, oracle.OracleModel(d, 48), oracle, 6)
+
+
+# ---- long contexts: the attention walk's ring wraps and its splits end ragged ----
+
+LONG_P, LONG_MAX = 653, 4  # an odd prompt length: no split ends on a 16-position walker boundary
+
+
+@pytest.fixture(scope="module")
+def long_case(oracle):
+    """Qwen3-4B width (2 layers, vocab 8192), three 653-token prompts, and each
+    prompt's greedy generation by the oracle."""
+    d = synth.cached_checkpoint("QWEN3_4B", seed=13, layers=2, vocab=8192)
+    prompts = np.stack([synth.prompt_tokens(40 + b, LONG_P, 8192) for b in range(3)])
+    ref = oracle.OracleModel(d, LONG_P + LONG_MAX + 4)
+    expected = []
+    for prompt in prompts:
+        ref.cursor = 0
+        expected.append(ref.generate(prompt, LONG_MAX))
+    return d, prompts, expected
+
+
+@pytest.mark.parametrize("splits", [None, "2", "64"])
+def test_long_context_batch_matches_oracle(gpu, oracle, long_case, monkeypatch, splits):
+    """Batched generation after 653-token prompts against each prompt's own greedy
+    generation by the oracle.  With 2 position splits every half-warp walker of
+    cached_attention_part_kernel makes about 21 trips, so its 6-slot cp.async ring
+    wraps three times and the splits end mid-walker; with 64 splits the last splits
+    hold no position at all; the default split count sits between."""
+    d, prompts, expected = long_case
+    if splits is None:
+        monkeypatch.delenv("LSX_BATCH_ATTENTION_SPLITS", raising=False)
+    else:
+        monkeypatch.setenv("LSX_BATCH_ATTENTION_SPLITS", splits)
+    model = lsx.Model.load(d, gpu, LONG_P + LONG_MAX + 4)
+    tokens = model.generate_batch(prompts, LONG_MAX)
+    for b, (ref_tokens, ref_frames) in enumerate(expected):
+        for i, (t, rt) in enumerate(zip(tokens[b], ref_tokens)):
+            if int(t) != rt:
+                assert abs(oracle.minimum_margin(ref_frames[i][1], rt)) < 1e-3, (splits, b, i, t, rt)
+                break
+        else:
+            assert list(map(int, tokens[b])) == ref_tokens, (splits, b)

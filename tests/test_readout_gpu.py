@@ -204,3 +204,49 @@ def test_host_entry_large_upload_matches_device_entry(gpu):
     assert np.array_equal(margin, raw[: n * 8].view(np.float64))
     assert np.array_equal(amax, raw[n * 8: n * 12].view(np.uint32))
     assert np.array_equal(tl, raw[n * 12:].view(np.float32))
+
+
+def test_device_entries_report_status(gpu):
+    """The device-pointer entries leave the kernels' status in the caller's
+    workspace: lsx_readout_status reports non-finite scores (the reference's
+    rejection, src/model.rs:680-683) for lsx_readout_margin_device and
+    lsx_readout_shard_device, and a clean status after a clean call on the same
+    workspace."""
+    import ctypes as C
+
+    import torch
+
+    from laplacesscissors_b200._lib import F32, LsxError, check, lib
+    V, H, n = 1031, 256, 48
+    dev = f"cuda:{gpu.device}"
+    weight = gpu.upload_raw(synth.normal_bf16(6, 0, V * H, 0.02), BF16)
+    clean = synth.normal_f32(6, 9, n * H)
+    bad = clean.copy()
+    bad[7 * H + 3] = np.inf
+    targets = torch.from_numpy(synth.readout_targets(6, n, V).astype(np.int32)).to(dev)
+    ws_bytes = lib.lsx_readout_workspace_bytes(V, H, n, None)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    margin = torch.empty(n, dtype=torch.float64, device=dev)
+    amax = torch.empty(n, dtype=torch.int32, device=dev)
+    keys = torch.empty(n, dtype=torch.int64, device=dev)
+    tlog = torch.empty(n, dtype=torch.float32, device=dev)
+    for rows in (bad, clean):
+        hidden = torch.from_numpy(rows).to(dev)
+        check(lib.lsx_readout_margin_device(gpu.handle, weight.handle, None, V, H, C.c_void_p(hidden.data_ptr()), F32,
+                                            n, C.c_void_p(targets.data_ptr()), None, C.c_void_p(margin.data_ptr()),
+                                            C.c_void_p(amax.data_ptr()), None, C.c_void_p(ws.data_ptr()), ws_bytes))
+        if rows is bad:
+            with pytest.raises(LsxError) as err:
+                check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))
+            assert err.value.status == 4
+        else:
+            check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))
+        check(lib.lsx_readout_shard_device(gpu.handle, weight.handle, None, 0, V, H, C.c_void_p(hidden.data_ptr()),
+                                           F32, n, C.c_void_p(targets.data_ptr()), None, C.c_void_p(keys.data_ptr()),
+                                           C.c_void_p(tlog.data_ptr()), C.c_void_p(ws.data_ptr()), ws_bytes))
+        if rows is bad:
+            with pytest.raises(LsxError) as err:
+                check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))
+            assert err.value.status == 4
+        else:
+            check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))

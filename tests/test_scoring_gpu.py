@@ -185,8 +185,8 @@ def test_batched_single_case_single_target_and_checks(gpu, oracle):
 @pytest.mark.parametrize("shape,vocab", [("QWEN3_0_6B", 151936), ("QWEN3_8B", 8192)])
 def test_batched_scores_wide_shapes(gpu, oracle, shape, vocab):
     """Qwen3-0.6B and Qwen3-8B widths (2 layers): several cases of a 64-token prompt
-    and 9 targets, against the sequential path on every case (losses within 2e-2,
-    the decode tolerance) and the oracle on the first."""
+    and 9 targets, against the sequential path and the oracle on every case (losses
+    within 2e-2, the decode tolerance)."""
     d = Path(tempfile.mkdtemp(prefix=f"lsx-batch-{shape.lower()}-"))
     synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(getattr(synth, shape), layers=2, vocab=vocab)), seed=6)
     model = lsx.Model.load(d, gpu, 80)
@@ -195,9 +195,10 @@ def test_batched_scores_wide_shapes(gpu, oracle, shape, vocab):
     for c in range(len(prompts)):
         seq_nll, seq_amax, _ = model.score(prompts[c], targets[c])
         assert np.all(np.abs(nll[c] - seq_nll) <= 2e-2), (c, nll[c], seq_nll)
-    ref_nll, ref_amax = oracle_scores(oracle, d, prompts[0], targets[0], capacity=80)
-    assert np.all(np.abs(nll[0] - ref_nll) <= 2e-2), (nll[0], ref_nll)
-    check_argmax(amax[0], ref_amax, oracle, d, prompts[0], targets[0], capacity=80)
+    for c in range(len(prompts)):
+        ref_nll, ref_amax = oracle_scores(oracle, d, prompts[c], targets[c], capacity=80)
+        assert np.all(np.abs(nll[c] - ref_nll) <= 2e-2), (c, nll[c], ref_nll)
+        check_argmax(amax[c], ref_amax, oracle, d, prompts[c], targets[c], capacity=80)
 
 
 def test_batched_edited_scores_match_sequential(gpu, golden_tiny):
