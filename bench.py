@@ -9,16 +9,28 @@ through the model) per second, device-timed with CUDA events on the library's
 stream.  `e2e` is the same generation through the C ABI call lsx_model_generate
 with host buffers (prompt upload, token and Frame downloads inside the timing).
 
-Second object `readout`: fused readout-margin validation of 4096 RMSNorm'd bf16
-hidden states against lm_head [151936, 1024] with a rank-16 Givens edit; rows/s.
+Sub-objects of the same line, one per configuration of the survey's measurement
+table:
+  readout         fused readout-margin validation of 4096 RMSNorm'd bf16 hidden
+                  states against lm_head [151936, 1024] with a rank-16 Givens edit
+  gemv            the bf16 GEMV microbenchmark (five shapes)
+  long4b_batch    Qwen3-4B, 16 sequences decoded together after 4096-token prompts
+  score8b         Qwen3-8B teacher-forced scoring, 64 cases per GPU
+  readout_vocab   (N > 1) the validation with the lm_head split by vocabulary rows
+  triton_baseline (N = 1) the reference's own Triton kernels on this GPU, in its
+                  runtime pattern and as a CUDA graph (baseline/triton_reference.py)
+Each carries its roofline, and (N = 1) a CPU baseline from the oracle.
 
 Multi-GPU (torchrun): decode runs as one independent replica per GPU (a batch-1
 stream does not shard); readout validation is row-sharded with a fixed 4096 rows
-per GPU (weak scaling, no data-path collective).  Timing is max over ranks.
+per GPU and every step all-gathers the per-row results to every rank (NCCL);
+scoring is case-sharded; the vocabulary-sharded validation merges its shards with
+one NCCL all-reduce per step.  Timing is the maximum over ranks.
 
 --impl reference times the reference's CPU path (the oracle restatement of
 tests/qwen_reference.rs's CPU forward, KV-cached, f64 reductions) on the host
-cores; the reference's Rust crate cannot be built here.
+cores over the same 55-step generation, with inputs from the oracle's own
+generator; the reference's Rust crate cannot be built here.
 """
 from __future__ import annotations
 
@@ -323,23 +335,35 @@ def run_gemv(gpu, iters: int = 20):
 
 
 def run_readout(gpu, inputs, steps: int, warmup: int, dist, e2e: bool = True):
+    """The validation step on device-resident rows.  With several ranks each step
+    ends with one NCCL all-gather of every rank's per-row results (margin f64,
+    argmax u32, target logit f32: 16 B per row) on the library's stream, so every
+    rank holds the whole validation's results, as verify_cached aggregates one
+    Verification over all rows (src/diagnosis.rs:493-580); the gather alone is
+    timed as well."""
     import ctypes as C
     import torch
 
-    import laplacesscissors_b200 as lsx
     from laplacesscissors_b200 import DeviceRotation
     from laplacesscissors_b200._lib import BF16, check, lib
     w, hidden, targets, edit = inputs
     weight = gpu.upload_raw(w, BF16)
     rot = DeviceRotation.upload_edit(gpu, edit, HIDDEN)
+    dev = f"cuda:{gpu.device}"
     # Device-resident inputs for the device-timed leg.
     d_hidden = gpu.upload_raw(hidden, BF16)
     d_targets = torch.from_numpy(targets.astype(np.int32)).cuda(gpu.device)
-    d_out = torch.empty(READOUT_ROWS * 16, dtype=torch.uint8, device=f"cuda:{gpu.device}")
+    d_out = torch.empty(READOUT_ROWS * 16, dtype=torch.uint8, device=dev)
+    gathered = torch.empty(dist.world * READOUT_ROWS * 16, dtype=torch.uint8, device=dev) if dist.world > 1 else None
     ws_bytes = lib.lsx_readout_workspace_bytes(VOCAB, HIDDEN, READOUT_ROWS, rot.handle)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=f"cuda:{gpu.device}")
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     base = d_out.data_ptr()
     torch.cuda.synchronize(gpu.device)
+    stream, event = cuda_timer(gpu)
+
+    def gather():
+        with torch.cuda.stream(stream):
+            dist.pg.all_gather_into_tensor(gathered, d_out)
 
     def step():
         check(lib.lsx_readout_margin_device(gpu.handle, weight.handle, None, VOCAB, HIDDEN,
@@ -347,10 +371,12 @@ def run_readout(gpu, inputs, steps: int, warmup: int, dist, e2e: bool = True):
                                             C.c_void_p(d_targets.data_ptr()), rot.handle, C.c_void_p(base),
                                             C.c_void_p(base + READOUT_ROWS * 8), C.c_void_p(base + READOUT_ROWS * 12),
                                             C.c_void_p(ws.data_ptr()), ws_bytes))
+        if gathered is not None:
+            gather()
 
-    stream, event = cuda_timer(gpu)
     for _ in range(warmup):
         step()
+    check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))
     gpu.synchronize()
     dist.barrier()
     start, stop = event(), event()
@@ -361,6 +387,21 @@ def run_readout(gpu, inputs, steps: int, warmup: int, dist, e2e: bool = True):
         stop.record(stream)
         stop.synchronize()
     dev_ms = start.elapsed_time(stop)
+    check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))
+    gather_ms = None
+    if gathered is not None:
+        # the collective alone, same message, same stream
+        dist.barrier()
+        g0, g1 = event(), event()
+        g0.record(stream)
+        for _ in range(steps):
+            gather()
+        g1.record(stream)
+        g1.synchronize()
+        gather_ms = g0.elapsed_time(g1) / steps
+        # every rank's block of the gathered results is that rank's own output
+        mine = gathered[dist.rank * READOUT_ROWS * 16:(dist.rank + 1) * READOUT_ROWS * 16]
+        assert torch.equal(mine, d_out)
     dist.barrier()
     from laplacesscissors_b200 import diagnosis
     e2e_s = float("nan")
@@ -373,12 +414,13 @@ def run_readout(gpu, inputs, steps: int, warmup: int, dist, e2e: bool = True):
             diagnosis.readout_margin(gpu, weight, None, VOCAB, HIDDEN, hidden, targets, rot)
         e2e_s = time.perf_counter() - t0
     return {"dev_ms": dev_ms, "e2e_s": e2e_s, "clocks": clocks.summary(), "h2d": hidden.nbytes + targets.nbytes,
-            "d2h": READOUT_ROWS * 16}
+            "d2h": READOUT_ROWS * 16, "gather_ms": gather_ms}
 
 
 class Dist:
     def __init__(self, world: int, local: int):
         self.world = world
+        self.rank = int(os.environ.get("RANK", 0))
         self.pg = None
         if world > 1:
             import torch
@@ -405,6 +447,259 @@ class Dist:
             self.pg.destroy_process_group()
 
 
+def ensure_checkpoints(rank: int, shapes: list[str]) -> dict:
+    """Builds the named checkpoints once per machine before any process group
+    exists (writing the 8B model takes longer than a collective may wait): rank 0
+    writes, the other ranks wait for the completed folders."""
+    from laplacesscissors_b200 import synth
+    out = {}
+    for shape in shapes:
+        if rank == 0:
+            out[shape] = synth.cached_checkpoint(shape)
+        else:
+            root = Path(tempfile.gettempdir()) / f"lsx-bench-{shape.lower()}-seed7"
+            t0 = time.monotonic()
+            while not (root / "config.json").exists():
+                if time.monotonic() - t0 > 1800:
+                    raise RuntimeError(f"checkpoint {root} was not written")
+                time.sleep(1.0)
+            out[shape] = root
+    return out
+
+
+def long_batch_leg(gpu, ckpt: Path, steps: int, prompt: int = 4096, batch: int = 16, cpu: bool = True):
+    """Config 4, bs16: Qwen3-4B, 16 sequences decoded together after a 4096-token
+    prompt each (lsx_model_generate_batch, host buffers).  Decode throughput is
+    batch x K / (t(1 + K steps) - t(1 step)): the two calls share the prefill, so
+    the difference is K decode steps at context 4097..4096 + K.  `value` takes the
+    two times from CUDA events on the library's stream, `e2e` from the host clock
+    around the same calls (prompts in, tokens out)."""
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import synth
+    cfg = synth.QWEN3_4B
+    K = max(8, steps)
+    model = lsx.Model.load(ckpt, gpu, 64)
+    prompts = np.stack([synth.prompt_tokens(7 + b, prompt, cfg["vocab"]) for b in range(batch)])
+    model.generate_batch(prompts, 1 + K)  # warm-up: caches at their largest, modules loaded
+    stream, event = cuda_timer(gpu)
+    times = {}
+    with ClockSampler(gpu.device) as clocks:
+        for n in (1, 1 + K):
+            e0, e1 = event(), event()
+            t0 = time.perf_counter()
+            e0.record(stream)
+            model.generate_batch(prompts, n)
+            e1.record(stream)
+            e1.synchronize()
+            times[n] = (e0.elapsed_time(e1) / 1e3, time.perf_counter() - t0)
+    step_dev = (times[1 + K][0] - times[1][0]) / K
+    step_e2e = (times[1 + K][1] - times[1][1]) / K
+    kv_layers = cfg["layers"] * 2 * cfg["kv_heads"] * cfg["head_dim"] * 4
+    step_bytes = weight_bytes_per_step(cfg) + batch * kv_layers * (prompt + 1 + K / 2)
+    peaks = measured_peaks()
+    achieved = step_bytes / step_dev / 1e9
+    out = {
+        "metric": f"decode tok/s (Qwen3-4B bs{batch} after a {prompt}-token prompt)", "value": batch / step_dev,
+        "unit": "tok/s", "ms_per_step": step_dev * 1e3, "steps": K,
+        "config": {"workload": f"Qwen3-4B bs{batch} greedy decode at context {prompt + 1}..{prompt + K}",
+                   "prompt": prompt, "batch": batch, "kv_cache": "f32",
+                   "timing": "generate_batch(1 + K) minus generate_batch(1): K decode steps after a shared prefill",
+                   "l2": f"weights {weight_bytes_per_step(cfg) / 1e9:.2f} GB per step > L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"],
+                     "scope": f"{step_bytes / 1e9:.2f} GB per step: bf16 weights once + {batch} sequences' f32 KV, "
+                              f"{peaks['source']} peak"},
+        "e2e": {"value": batch / step_e2e, "unit": "tok/s", "h2d_bytes_per_step": int(prompts.nbytes),
+                "d2h_bytes_per_step": int(batch * (1 + K) * 4)},
+        "prefill_and_first_step_seconds": times[1][1],
+        "clocks": clocks.summary(),
+    }
+    if cpu:
+        from oracle import binding as oracle
+        threads = cpu_threads()
+        m = oracle.OracleModel(ckpt, 16, threads=threads)
+        ids = synth.prompt_tokens(7, 4, cfg["vocab"])
+        m.advance(int(ids[0]))  # pages the weights in
+        m.cursor = 0
+        t0 = time.perf_counter()
+        for t in ids:
+            m.advance(int(t))
+        rate = len(ids) / (time.perf_counter() - t0)
+        out["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                               "sample": "4 oracle decode steps of the Qwen3-4B model, one sequence, at context 1-4 "
+                                         "(the reference decodes one sequence at a time; its KV read at context "
+                                         "4096 adds 2.4 GB per step, so this rate is an upper bound)"}
+    return out
+
+
+SCORE_P, SCORE_N, SCORE_EOS = 64, 9, 151645
+
+
+def score_cases(first: int, count: int, vocab: int = 151936):
+    """Cases first .. first + count - 1 of the scoring job: 64 random prompt ids,
+    8 random answer ids + EOS (seeded per case)."""
+    from laplacesscissors_b200 import synth
+    prompts = np.stack([synth.uniform_u32(7, 1000 + i, SCORE_P, vocab) for i in range(first, first + count)])
+    answers = np.stack([synth.uniform_u32(7, 5000 + i, SCORE_N - 1, vocab) for i in range(first, first + count)])
+    return prompts, np.concatenate([answers, np.full((count, 1), SCORE_EOS, np.uint32)], axis=1)
+
+
+def scoring_leg(gpu, ckpt: Path, dist, cases: int = 64, batch: int = 64, cpu: bool = True):
+    """Config 5: Qwen3-8B teacher-forced scoring (lsx_model_score_batch, host
+    arrays in, losses, argmaxes and margins out), `cases` cases per rank, case
+    shards across ranks (weak scaling).  `value` from CUDA events on the library's
+    stream around the calls, `e2e` from the host clock; max over ranks."""
+    import laplacesscissors_b200 as lsx
+    from laplacesscissors_b200 import synth
+    cfg = synth.QWEN3_8B
+    model = lsx.Model.load(ckpt, gpu, 80)
+    rank = dist.rank
+    model.score_batch(*score_cases(10_000, batch))  # warm-up
+    inputs = [score_cases(100 + rank * cases + i, min(batch, cases - i)) for i in range(0, cases, batch)]
+    stream, event = cuda_timer(gpu)
+    gpu.synchronize()
+    dist.barrier()
+    with ClockSampler(gpu.device) as clocks:
+        e0, e1 = event(), event()
+        t0 = time.perf_counter()
+        e0.record(stream)
+        for pr, tg in inputs:
+            model.score_batch(pr, tg)
+        e1.record(stream)
+        e1.synchronize()
+        wall = time.perf_counter() - t0
+    dev_s = dist.max(e0.elapsed_time(e1) / 1e3)
+    wall = dist.max(wall)
+    world = dist.world
+    tokens = SCORE_P + SCORE_N - 1
+    flops_case = decoder_flops_per_token(cfg) * tokens + 2 * SCORE_N * cfg["vocab"] * cfg["hidden"]
+    tflops = world * cases * flops_case / dev_s / 1e12
+    peaks = measured_peaks()
+    out = {
+        "metric": "teacher-forced scoring cases/s (Qwen3-8B, 64-token prompt + 9 scored targets)",
+        "value": world * cases / dev_s, "unit": "cases/s", "ms_per_case": dev_s / cases * 1e3,
+        "scaling": "weak (case shards)" if world > 1 else "single GPU",
+        "config": {"workload": "Qwen3-8B teacher-forced scoring, 64 prompt + 8 answer + EOS per case",
+                   "cases_per_gpu": cases, "cases_per_call": batch, "job_cases": 1024,
+                   "fed_tokens_per_case": tokens,
+                   "timing": "lsx_model_score_batch calls with host arrays, CUDA events on the library stream "
+                             "(value) and the host clock (e2e)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": tflops / (world * peaks["bf16_tflops"]),
+                     "scope": f"algorithmic {flops_case / 1e12:.3f} TFLOP per case (2 x decoder parameters x 72 fed "
+                              "tokens + the lm_head on 9 rows); the f32 activations enter the tensor cores as two "
+                              f"bf16 terms, so 0.5 is this path's ceiling; {peaks['source']} burst peak"},
+        "e2e": {"value": world * cases / wall, "unit": "cases/s",
+                "h2d_bytes_per_step": int(sum(pr.nbytes + tg.nbytes for pr, tg in inputs)),
+                "d2h_bytes_per_step": int(cases * SCORE_N * (8 + 4 + 8))},
+        "job_seconds_estimate": 1024 / (world * cases / wall),
+        "clocks": clocks.summary(),
+    }
+    if cpu and dist.world == 1:
+        from oracle import binding as oracle
+        threads = cpu_threads()
+        m = oracle.OracleModel(ckpt, 16, threads=threads)
+        pr, _ = score_cases(100, 1)
+        m.advance(int(pr[0, 0]))  # pages the weights in
+        m.cursor = 0
+        fed = 6
+        t0 = time.perf_counter()
+        for t in pr[0, :fed]:
+            m.advance(int(t))
+        per_token = (time.perf_counter() - t0) / fed
+        out["cpu_baseline"] = {"value": 1.0 / (per_token * tokens), "unit": "cases/s", "cores": threads,
+                               "kind": "port",
+                               "sample": f"{fed} oracle decode steps of the Qwen3-8B model (one case's first fed "
+                                         f"tokens), scaled to the case's {tokens} fed tokens"}
+    return out
+
+
+def vocab_leg(gpu, dist, steps: int, warmup: int):
+    """The validation workload (4096 rows, rank-16 edit) with the lm_head split by
+    rows over the ranks (strong scaling: one whole validation over N GPUs): each
+    rank scores every row against its vocabulary block into packed int64
+    partials, one NCCL all-reduce MAX merges them, one kernel finalises.  The
+    collective alone is timed as well."""
+    import torch
+
+    from laplacesscissors_b200 import DeviceRotation
+    from laplacesscissors_b200._lib import BF16, lib
+    from laplacesscissors_b200.sharding import vocab_shard, vocab_sharded_margin
+    rank, world = dist.rank, dist.world
+    w, hidden, targets, edit = readout_inputs(0, 1)
+    v0, v1 = vocab_shard(VOCAB, world, rank)
+    shard = gpu.upload_raw(np.ascontiguousarray(w.reshape(VOCAB, HIDDEN)[v0:v1]), BF16)
+    del w
+    rot = DeviceRotation.upload_edit(gpu, edit, HIDDEN)
+    dev = torch.device("cuda", gpu.device)
+    d_hidden = torch.from_numpy(hidden.view(np.int16)).to(dev)
+    d_targets = torch.from_numpy(targets.astype(np.uint32).view(np.int32)).to(dev)
+    ws = torch.empty(lib.lsx_readout_workspace_bytes(v1 - v0, HIDDEN, READOUT_ROWS, rot.handle), dtype=torch.uint8,
+                     device=dev)
+    partials = torch.empty(2 * READOUT_ROWS, dtype=torch.int64, device=dev)
+    outs = (torch.empty(READOUT_ROWS, dtype=torch.float64, device=dev),
+            torch.empty(READOUT_ROWS, dtype=torch.int32, device=dev),
+            torch.empty(READOUT_ROWS, dtype=torch.float32, device=dev))
+    torch.cuda.synchronize(dev)
+
+    def step():
+        vocab_sharded_margin(gpu, shard, None, v0, v1 - v0, HIDDEN, d_hidden.data_ptr(), BF16, READOUT_ROWS,
+                             d_targets.data_ptr(), rot, workspace=ws, partials=partials, outputs=outs)
+
+    stream, event = cuda_timer(gpu)
+    for _ in range(warmup):
+        step()
+    gpu.synchronize()
+    dist.barrier()
+    start, stop = event(), event()
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    stop.record(stream)
+    stop.synchronize()
+    ms = dist.max(start.elapsed_time(stop)) / steps
+    dist.barrier()
+    c0, c1 = event(), event()
+    with torch.cuda.stream(stream):
+        c0.record(stream)
+        for _ in range(steps):
+            dist.pg.all_reduce(partials, op=dist.pg.ReduceOp.MAX)
+        c1.record(stream)
+    c1.synchronize()
+    coll_ms = dist.max(c0.elapsed_time(c1)) / steps
+    peaks = measured_peaks()
+    tflops = 2.0 * READOUT_ROWS * VOCAB * HIDDEN / (ms / 1e3) / 1e12
+    return {
+        "metric": "readout-margin rows/s (lm_head split by vocabulary rows)", "value": READOUT_ROWS / (ms / 1e3),
+        "unit": "rows/s", "ms_per_step": ms, "scaling": "strong",
+        "config": {"workload": "4096 rows x lm_head [151936, 1024], rank-16 edit, vocabulary-sharded",
+                   "vocab_rows_per_gpu": v1 - v0,
+                   "collective": "1 NCCL all-reduce MAX of 64 KiB (int64 [2 x 4096] packed partials) per step"},
+        "collective_ms": coll_ms,
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / (world * peaks["bf16_tflops"]),
+                     "scope": f"whole validation over {world} GPUs, {peaks['source']} burst peak x GPUs"},
+    }
+
+
+def triton_baseline_leg(ckpt: Path, steps: int = 3) -> dict:
+    """The reference's own Triton kernels on this GPU (baseline/triton_reference.py,
+    two subprocesses: the reference's runtime pattern, and its kernels alone in a
+    CUDA graph)."""
+    out = {}
+    script = ROOT / "baseline" / "triton_reference.py"
+    for mode in ("runtime", "graph"):
+        cmd = [sys.executable, str(script), "--mode", mode, "--checkpoint", str(ckpt), "--steps", str(steps),
+               "--warmup", "1"]
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+            line = r.stdout.strip().splitlines()[-1] if r.stdout.strip() else ""
+            out[mode] = json.loads(line) if line else {"unavailable": f"exit {r.returncode}: {r.stderr[-300:]}"}
+        except (subprocess.TimeoutExpired, json.JSONDecodeError) as e:
+            out[mode] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -412,6 +707,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-triton", action="store_true", help="skip the reference's Triton kernels on the GPU")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="decode, readout and GEMV only (no Qwen3-4B / Qwen3-8B sub-objects)")
     ap.add_argument("--workload", choices=["all", "decode", "readout", "gemv", "long4b", "long4b_batch", "score8b",
                                            "readout_vocab",
                                            "plane", "attribution"],
@@ -448,15 +746,24 @@ def main():
         return profile_run(args, local)
     if args.warmup < 3:
         args.warmup = 3
+    full = not args.headline_only
+    shapes = ["QWEN3_0_6B"] + (["QWEN3_4B", "QWEN3_8B"] if full and world == 1 else ["QWEN3_8B"] if full else [])
+    ckpts = ensure_checkpoints(rank, shapes)  # before the process group: the 8B file takes a while
     import laplacesscissors_b200 as lsx
     dist = Dist(world, local)
     gpu = lsx.Gpu(local)
     peaks = measured_peaks()
-    ckpt = build_checkpoint(local)
+    ckpt = ckpts["QWEN3_0_6B"]
+    cpu = not args.no_cpu_baseline and world == 1
     dec = run_decode(gpu, ckpt, args.steps, args.warmup, dist)
     inputs = readout_inputs(rank, world)
     ro = run_readout(gpu, inputs, args.steps, args.warmup, dist)
     gemv = run_gemv(gpu) if rank == 0 else None
+    # sub-objects: config 4 (one GPU), config 5 (case shards), vocabulary shards (N > 1)
+    long4b = long_batch_leg(gpu, ckpts["QWEN3_4B"], 32, cpu=cpu) if full and world == 1 else None
+    del dec["model"]
+    score8b = scoring_leg(gpu, ckpts["QWEN3_8B"], dist, cpu=cpu) if full else None
+    vocab = vocab_leg(gpu, dist, args.steps, args.warmup) if world > 1 else None
     # Kernels of ours per timed generation: one cooperative launch (persistent
     # engine) or the graph's per-step chain; readout: init, edit image, edit
     # coefficients, tcgen05 margin, finalize.
@@ -465,6 +772,7 @@ def main():
     dec_e2e = dist.max(dec["e2e_s"]) / args.steps
     ro_ms = dist.max(ro["dev_ms"]) / args.steps
     ro_e2e = dist.max(ro["e2e_s"]) / args.steps
+    gather_ms = dist.max(ro["gather_ms"]) if ro["gather_ms"] is not None else None
     if rank == 0:
         step_s = dec_ms / 1e3 / STEPS_PER_GENERATION
         bytes_step = decode_bytes_per_step()
@@ -482,10 +790,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16 weights, f32 activations and KV (f32 accumulate)",
             "data": "synthetic: random-init Qwen3-0.6B architecture (seed 7), 24 random prompt ids",
-            "config": {"workload": "Qwen3-0.6B bs1 greedy decode, 24-token prompt + 32 tokens",
-                       "decode_steps_per_step": STEPS_PER_GENERATION, "batch": 1, "kv_cache": "f32",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "l2": "weights 1.19 GB per token > 126 MB L2 (no flush needed)"},
+            "config": decode_config(world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"],
                          "traffic": DECODE_TRAFFIC_PER_LAUNCH if dec["persistent"] else None,
@@ -504,7 +809,9 @@ def main():
                 "ms_per_step": ro_ms,
                 "config": {"workload": "4096 RMSNorm'd bf16 hidden x lm_head [151936, 1024] bf16, rank-16 "
                                        "Givens edit within 3 degrees, target margin + argmax",
-                           "rows_per_gpu": READOUT_ROWS, "scaling": "weak (row shards)",
+                           "rows_per_gpu": READOUT_ROWS,
+                           "scaling": "weak (row shards), results all-gathered every step" if world > 1
+                           else "single GPU",
                            "l2": "lm_head 311 MB > L2"},
                 "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
                              "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
@@ -518,20 +825,51 @@ def main():
                 "clocks": ro["clocks"],
             },
         }
+        if gather_ms is not None:
+            line["readout"]["collective"] = {"op": "NCCL all-gather of 16 B per row (margin f64, argmax u32, "
+                                                   "target logit f32) per step, every rank receives all rows",
+                                             "ms": gather_ms}
+        gemv_frac = {k: dict(v, frac=v["GB/s"] / peaks["hbm_gbs"]) for k, v in gemv.items()}
         line["gemv"] = {
             "metric": "bf16 GEMV y = W x achieved HBM GB/s (lsx_linear_into, the Gpu::linear drop-in)",
             "unit": "GB/s", "peak": peaks["hbm_gbs"],
             "config": {"shapes": [f"{n}x{k}" for n, k in GEMV_SHAPES], "x": "f32", "y": "f32",
                        "l2": "weight copies rotated so each pass reads >= 256 MB",
                        "timing": "CUDA graph of the launches, CUDA events, rank 0"},
-            "results": gemv,
+            "roofline": {"bound": "hbm", "unit": "GB/s", "peak": peaks["hbm_gbs"],
+                         "bytes": "2NK + 4K + 4N per launch",
+                         "note": "shapes below 12 MB are launch- and latency-bound: their time per launch (us) "
+                                 "is the figure to read"},
+            "results": gemv_frac,
         }
-        if not args.no_cpu_baseline and world == 1:
+        if long4b is not None:
+            line["long4b_batch"] = long4b
+        if score8b is not None:
+            line["score8b"] = score8b
+        if vocab is not None:
+            line["readout_vocab"] = vocab
+        if cpu:
             v, cores, sample = cpu_decode_rate(ckpt)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
             rv, rcores, rsample = cpu_readout_rate(*inputs)
             line["readout"]["cpu_baseline"] = {"value": rv, "unit": "rows/s", "cores": rcores, "kind": "port",
                                                "sample": rsample}
+        if world == 1 and not args.no_triton:
+            tb = triton_baseline_leg(ckpt)
+            rt, gr = tb.get("runtime", {}), tb.get("graph", {})
+            line["triton_baseline"] = tb
+            ratios = {}
+            if "decode" in rt:
+                ratios["decode_e2e_vs_runtime"] = line["e2e"]["value"] / rt["decode"]["tok_s"]
+            if "decode" in gr:
+                ratios["decode_vs_graph"] = line["value"] / gr["decode"]["tok_s"]
+            if "readout" in rt:
+                ratios["readout_e2e_vs_runtime"] = line["readout"]["e2e"]["value"] / rt["readout"]["rows_s"]
+            if "readout" in gr:
+                ratios["readout_vs_graph"] = line["readout"]["value"] / gr["readout"]["rows_s"]
+            if "gemv" in gr:
+                ratios["gemv_vs_graph"] = {k: gemv[k]["GB/s"] / gr["gemv"][k]["GB/s"] for k in gemv if k in gr["gemv"]}
+            tb["ratios"] = ratios
         print(json.dumps(line))
     dist.close()
 

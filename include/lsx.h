@@ -308,6 +308,26 @@ int lsx_readout_shard_device(lsx_ctx* ctx, const lsx_tensor* weight_shard, const
 int lsx_readout_merge_device(lsx_ctx* ctx, const uint64_t* other_key, const float* target_logit,
                              const uint32_t* targets, size_t rows, double* margin_out, uint32_t* argmax_out,
                              float* target_logit_out);
+/* lsx_readout_shard_device with the shard's per-row partials written in one
+   signed-orderable int64 buffer partials [2 x rows]: element i < rows is the
+   packed best-other key with its top bit flipped, element rows + i the target
+   logit's total-order key (-inf, the lowest, when the target lies outside the
+   shard).  An element-wise signed maximum merges shards, so the whole exchange is
+   one all-reduce MAX of 16 bytes per row (ncclInt64) with no conversion before or
+   after it; lsx_readout_partials_merge_device then gives margins, first argmaxes
+   and target logits equal to lsx_readout_margin_device's over the whole
+   vocabulary.  Asynchronous on the context's stream; status as
+   lsx_readout_shard_device's (lsx_readout_status on the workspace). */
+int lsx_readout_partials_device(lsx_ctx* ctx, const lsx_tensor* weight_shard, const lsx_tensor* bias_shard,
+                                size_t vocab_offset, size_t shard_vocab, size_t width, const void* hidden,
+                                lsx_dtype hidden_kind, size_t rows, const uint32_t* targets,
+                                const lsx_rotation* rotation, int64_t* partials, void* workspace,
+                                size_t workspace_bytes);
+/* Margins (minimum_margin, src/diagnosis.rs:490-492), first argmaxes
+   (src/diagnosis.rs:58-70) and target logits from merged packed partials; device
+   pointers, any output may be NULL. */
+int lsx_readout_partials_merge_device(lsx_ctx* ctx, const int64_t* partials, const uint32_t* targets, size_t rows,
+                                      double* margin_out, uint32_t* argmax_out, float* target_logit_out);
 /* The device-pointer readout margin without an edit, for callers that must not
    allocate device memory (their memory is already fully committed, or an
    allocation at that point would be illegal or would stall other work).  It has

@@ -108,6 +108,8 @@ SIGNATURES = {
     "lsx_compact_margin": (I, [P, P, P, SZ, SZ, SZ, FP, UP, DP, UP, UP]),
     "lsx_readout_shard_device": (I, [P, P, P, SZ, SZ, SZ, P, I, SZ, P, P, P, P, P, SZ]),
     "lsx_readout_merge_device": (I, [P, P, P, P, SZ, P, P, P]),
+    "lsx_readout_partials_device": (I, [P, P, P, SZ, SZ, SZ, P, I, SZ, P, P, P, P, SZ]),
+    "lsx_readout_partials_merge_device": (I, [P, P, P, SZ, P, P, P]),
     "lsx_feasible_create": (I, [D, PP]),
     "lsx_feasible_free": (I, [P]),
     "lsx_feasible_constrain": (I, [P, D, D, D]),

@@ -1197,6 +1197,40 @@ __global__ void readout_finalize_kernel(const unsigned long long* other_key, con
     if (other_out) other_out[i] = oi;
 }
 
+// Vocabulary-shard partials in one signed-orderable int64 buffer [2 x M]: the
+// best-other key with its top bit flipped (so signed order is the key's unsigned
+// order), then the target logit's total-order key (non-negative).  An element-wise
+// signed maximum over the shards -- one all-reduce MAX -- merges them.
+__device__ __forceinline__ long long logit_order(float v) {
+    const uint32_t b = __float_as_uint(v);
+    return (long long)((b & 0x80000000u) ? ~b : (b | 0x80000000u));
+}
+__device__ __forceinline__ float order_logit(long long o) {
+    const uint32_t u = (uint32_t)o;
+    return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+
+__global__ void shard_pack_kernel(long long* partials, const float* target_logit, int M) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M) return;
+    partials[i] = (long long)((unsigned long long)partials[i] ^ 0x8000000000000000ull);
+    partials[M + i] = logit_order(target_logit[i]);
+}
+
+__global__ void shard_merge_kernel(const long long* partials, const uint32_t* targets, int M, double* margin,
+                                   uint32_t* argmax, float* target_out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M) return;
+    const unsigned long long k = (unsigned long long)partials[i] ^ 0x8000000000000000ull;
+    const float ov = packed_value(k);
+    const uint32_t oi = packed_index(k);
+    const float tv = order_logit(partials[M + i]);
+    const uint32_t t = targets[i];
+    if (margin) margin[i] = (double)tv - (double)ov;
+    if (argmax) argmax[i] = (tv > ov || (tv == ov && t < oi)) ? t : oi;
+    if (target_out) target_out[i] = tv;
+}
+
 // ------------------------------------------------------ compact readout ----
 // CompactReadout::evaluate (src/diagnosis.rs:643-665) fused with the margin rules:
 // for observation o, z_o = image c_o + baseline_o (image [V, r] f32 row-major, the
@@ -1460,6 +1494,7 @@ struct ShardOut {
     size_t vocab_offset;
     unsigned long long* other_key;
     float* target_logit;
+    long long* partials;  // packed form [2 x rows] (other_key and target_logit unused), or NULL
 };
 
 // Enqueues the whole validation on ctx->stream.  All pointers are device pointers.
@@ -1486,8 +1521,11 @@ int readout_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bi
     uint8_t* ws = (uint8_t*)workspace;
     cudaStream_t s = ctx->stream;
     int* status = (int*)(ws + L.status_off);
-    unsigned long long* keys = shard ? shard->other_key : (unsigned long long*)(ws + L.key_off);
-    float* tlog = shard ? shard->target_logit : (float*)(ws + L.tlog_off);
+    const bool packed = shard && shard->partials;
+    unsigned long long* keys = packed  ? (unsigned long long*)shard->partials
+                               : shard ? shard->other_key
+                                       : (unsigned long long*)(ws + L.key_off);
+    float* tlog = shard && !packed ? shard->target_logit : (float*)(ws + L.tlog_off);
     if (shard)
         LSX_ENSURE(shard->vocab_offset + vocab <= 2147483647ull, "check the vocabulary shard range");
     __nv_bfloat16* plane_hi = f32_hidden ? (__nv_bfloat16*)(ws + L.planes_off) : nullptr;
@@ -1630,6 +1668,9 @@ int readout_enqueue(lsx_ctx* ctx, const lsx_tensor* weight, const lsx_tensor* bi
     if (!shard) {
         readout_finalize_kernel<<<(M + 255) / 256, 256, 0, s>>>(keys, tlog, targets, M, margin, argmax, target_logit);
         LSX_CUDA(cudaGetLastError(), "readout finalize");
+    } else if (packed) {
+        shard_pack_kernel<<<(M + 255) / 256, 256, 0, s>>>(shard->partials, tlog, M);
+        LSX_CUDA(cudaGetLastError(), "shard partials pack");
     }
     if (host_status) {
         LSX_CUDA(cudaMemcpyAsync(host_status, status, 8, cudaMemcpyDeviceToHost, s), "status download");
@@ -1729,9 +1770,34 @@ int lsx_readout_shard_device(lsx_ctx* ctx, const lsx_tensor* weight_shard, const
                              void* workspace, size_t workspace_bytes) {
     LSX_ENSURE(ctx && hidden && targets && other_key_out && target_logit_out, "invalid argument");
     cudaSetDevice(ctx->device);
-    const ShardOut shard{vocab_offset, (unsigned long long*)other_key_out, target_logit_out};
+    const ShardOut shard{vocab_offset, (unsigned long long*)other_key_out, target_logit_out, nullptr};
     return readout_enqueue(ctx, weight_shard, bias_shard, shard_vocab, width, hidden, hidden_kind, rows, targets,
                            rotation, nullptr, nullptr, nullptr, workspace, workspace_bytes, nullptr, &shard);
+}
+
+int lsx_readout_partials_device(lsx_ctx* ctx, const lsx_tensor* weight_shard, const lsx_tensor* bias_shard,
+                                size_t vocab_offset, size_t shard_vocab, size_t width, const void* hidden,
+                                lsx_dtype hidden_kind, size_t rows, const uint32_t* targets,
+                                const lsx_rotation* rotation, int64_t* partials, void* workspace,
+                                size_t workspace_bytes) {
+    LSX_ENSURE(ctx && hidden && targets && partials, "invalid argument");
+    LSX_ENSURE(rows > 0 && rows <= 1073741823ull, "check the row count");  // 2 x rows indexes an int
+    LSX_CUDA(cudaSetDevice(ctx->device), "select device");
+    const ShardOut shard{vocab_offset, nullptr, nullptr, (long long*)partials};
+    return readout_enqueue(ctx, weight_shard, bias_shard, shard_vocab, width, hidden, hidden_kind, rows, targets,
+                           rotation, nullptr, nullptr, nullptr, workspace, workspace_bytes, nullptr, &shard);
+}
+
+int lsx_readout_partials_merge_device(lsx_ctx* ctx, const int64_t* partials, const uint32_t* targets, size_t rows,
+                                      double* margin_out, uint32_t* argmax_out, float* target_logit_out) {
+    LSX_ENSURE(ctx && partials && targets, "invalid argument");
+    LSX_ENSURE(rows > 0 && rows <= 1073741823ull, "check the row count");
+    LSX_CUDA(cudaSetDevice(ctx->device), "select device");
+    const int M = (int)rows;
+    shard_merge_kernel<<<(M + 255) / 256, 256, 0, ctx->stream>>>((const long long*)partials, targets, M, margin_out,
+                                                                 argmax_out, target_logit_out);
+    LSX_CUDA(cudaGetLastError(), "shard partials merge");
+    return LSX_OK;
 }
 
 int lsx_readout_merge_device(lsx_ctx* ctx, const uint64_t* other_key, const float* target_logit,

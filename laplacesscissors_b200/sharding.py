@@ -96,6 +96,29 @@ def shard_partials(logits: np.ndarray, targets: np.ndarray, v0: int) -> tuple[np
     return keys, tl
 
 
+def pack_partials(keys: np.ndarray, target_logit: np.ndarray) -> np.ndarray:
+    """The packed partials of lsx_readout_partials_device from (keys, target
+    logits): int64 [2 n], the keys with their top bit flipped, then the target
+    logits' total-order keys; an element-wise signed maximum merges shards."""
+    k = (np.asarray(keys, dtype=np.uint64) ^ np.uint64(1 << 63)).view(np.int64)
+    bits = np.ascontiguousarray(target_logit, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    order = np.where(bits & 0x80000000, (~bits) & 0xFFFFFFFF, bits | 0x80000000).astype(np.int64)
+    return np.concatenate([k, order])
+
+
+def unpack_partials(partials: np.ndarray, targets: np.ndarray):
+    """(margin f64, first argmax u32, target logit f32) from merged packed partials."""
+    p = np.asarray(partials, dtype=np.int64)
+    n = p.size // 2
+    other, other_idx = unpack_key(p[:n].view(np.uint64) ^ np.uint64(1 << 63))
+    order = p[n:].astype(np.uint64)
+    bits = np.where(order & 0x80000000, order & 0x7FFFFFFF, (~order) & 0xFFFFFFFF).astype(np.uint32)
+    tl = bits.view(np.float32)
+    tgt = np.asarray(targets, dtype=np.uint32)
+    amax = np.where((tl > other) | ((tl == other) & (tgt < other_idx)), tgt, other_idx).astype(np.uint32)
+    return tl.astype(np.float64) - other.astype(np.float64), amax, tl
+
+
 def merge_partials_(keys, target_logit, group=None) -> None:
     """In-place max-merge of vocabulary-shard partials across `group`: `keys` is an
     int64 tensor holding the bits of the packed unsigned keys, `target_logit` f32.
@@ -140,21 +163,25 @@ def merge_vocab_partials(keys: np.ndarray, target_logit: np.ndarray, targets: np
 
 def vocab_sharded_margin(gpu, weight_shard, bias_shard, vocab_offset: int, shard_vocab: int, width: int,
                          hidden_ptr: int, hidden_kind: int, rows: int, targets_ptr: int, rotation=None, group=None,
-                         workspace=None):
+                         workspace=None, partials=None, outputs=None):
     """Readout validation with the lm_head split by rows across the ranks of
     `group` (one GPU per rank), on device-resident inputs.
 
     This rank holds lm_head rows [vocab_offset, vocab_offset + shard_vocab)
     (`weight_shard`, a BF16 Tensor) and scores every hidden row against them with
-    lsx_readout_shard_device; one NCCL all-reduce MAX over the packed competitor
-    keys and the target logits (merge_partials_) combines the shards, and lsx_readout_merge_device
-    turns the merged partials into margins and first argmaxes.  All work is ordered
-    on the library's stream.  `hidden_ptr` / `targets_ptr` are device addresses
-    ([rows, width] of `hidden_kind`; global target ids as u32).  Returns device
-    tensors (margin f64, argmax int32 holding the u32 ids, target logit f32)."""
+    lsx_readout_partials_device, which leaves the shard's per-row partials in one
+    signed-orderable int64 buffer [2 x rows]; one NCCL all-reduce MAX of that
+    buffer merges the shards, and lsx_readout_partials_merge_device turns the
+    merged partials into margins and first argmaxes.  All work is ordered on the
+    library's stream; nothing runs between the kernels and the collective.
+    `hidden_ptr` / `targets_ptr` are device addresses ([rows, width] of
+    `hidden_kind`; global target ids as u32).  `workspace`, `partials` (int64
+    [2 * rows]) and `outputs` (margin f64, argmax int32, target logit f32, each
+    [rows]) may be passed in to reuse buffers.  Returns the output tensors."""
     import ctypes as C
 
     import torch
+    import torch.distributed as dist
 
     from ._lib import check, lib
     dev = torch.device("cuda", gpu.device)
@@ -164,18 +191,23 @@ def vocab_sharded_margin(gpu, weight_shard, bias_shard, vocab_offset: int, shard
         if workspace is None:
             workspace = torch.empty(lib.lsx_readout_workspace_bytes(shard_vocab, width, rows, rot),
                                     dtype=torch.uint8, device=dev)
-        keys = torch.empty(rows, dtype=torch.int64, device=dev)
-        tlog = torch.empty(rows, dtype=torch.float32, device=dev)
-        check(lib.lsx_readout_shard_device(gpu.handle, weight_shard.handle, bias_shard.handle if bias_shard else None,
-                                           int(vocab_offset), int(shard_vocab), int(width), C.c_void_p(hidden_ptr),
-                                           int(hidden_kind), int(rows), C.c_void_p(targets_ptr), rot,
-                                           C.c_void_p(keys.data_ptr()), C.c_void_p(tlog.data_ptr()),
-                                           C.c_void_p(workspace.data_ptr()), workspace.numel()))
-        merge_partials_(keys, tlog, group)
-        margin = torch.empty(rows, dtype=torch.float64, device=dev)
-        amax = torch.empty(rows, dtype=torch.int32, device=dev)
-        tl = torch.empty(rows, dtype=torch.float32, device=dev)
-        check(lib.lsx_readout_merge_device(gpu.handle, C.c_void_p(keys.data_ptr()), C.c_void_p(tlog.data_ptr()),
-                                           C.c_void_p(targets_ptr), int(rows), C.c_void_p(margin.data_ptr()),
-                                           C.c_void_p(amax.data_ptr()), C.c_void_p(tl.data_ptr())))
-    return margin, amax, tl
+        if partials is None:
+            partials = torch.empty(2 * rows, dtype=torch.int64, device=dev)
+        if outputs is None:
+            outputs = (torch.empty(rows, dtype=torch.float64, device=dev),
+                       torch.empty(rows, dtype=torch.int32, device=dev),
+                       torch.empty(rows, dtype=torch.float32, device=dev))
+        check(lib.lsx_readout_partials_device(gpu.handle, weight_shard.handle,
+                                              bias_shard.handle if bias_shard else None, int(vocab_offset),
+                                              int(shard_vocab), int(width), C.c_void_p(hidden_ptr), int(hidden_kind),
+                                              int(rows), C.c_void_p(targets_ptr), rot,
+                                              C.c_void_p(partials.data_ptr()), C.c_void_p(workspace.data_ptr()),
+                                              workspace.numel()))
+        if dist.is_initialized() and dist.get_world_size(group) > 1:
+            dist.all_reduce(partials, op=dist.ReduceOp.MAX, group=group)
+        margin, amax, tl = outputs
+        check(lib.lsx_readout_partials_merge_device(gpu.handle, C.c_void_p(partials.data_ptr()),
+                                                    C.c_void_p(targets_ptr), int(rows),
+                                                    C.c_void_p(margin.data_ptr()), C.c_void_p(amax.data_ptr()),
+                                                    C.c_void_p(tl.data_ptr())))
+    return outputs

@@ -9,8 +9,8 @@ import numpy as np
 import pytest
 
 from laplacesscissors_b200 import diagnosis
-from laplacesscissors_b200.sharding import (merge_vocab_partials, gather_rows, pack_key, row_shard,
-                                            shard_partials, unpack_key, vocab_shard)
+from laplacesscissors_b200.sharding import (merge_vocab_partials, gather_rows, pack_key, pack_partials, row_shard,
+                                            shard_partials, unpack_key, unpack_partials, vocab_shard)
 
 
 @pytest.mark.parametrize("total,world", [(4096, 8), (10, 3), (151936, 8), (5, 8), (0, 2)])
@@ -60,6 +60,13 @@ def _worker(rank, world, port, q):
         v0, v1 = vocab_shard(vocab, world, rank)
         keys, tl = shard_partials(z[:, v0:v1], targets, v0)
         margin, amax, tlog = merge_vocab_partials(keys, tl, targets)
+        # the packed form of the GPU path: one all-reduce MAX over int64 [2 rows]
+        import torch
+        packed = torch.from_numpy(pack_partials(keys, tl))
+        dist.all_reduce(packed, op=dist.ReduceOp.MAX)
+        p_margin, p_amax, p_tl = unpack_partials(packed.numpy(), targets)
+        assert np.array_equal(p_margin, margin) and np.array_equal(p_amax, amax)
+        assert np.array_equal(p_tl.view(np.uint32), tlog.view(np.uint32))
         lo, hi = row_shard(rows, world, rank)
         got = gather_rows({"margin": margin[lo:hi], "argmax": amax[lo:hi], "target": tlog[lo:hi]}, rows)
         q.put((rank, margin, amax, tlog, got["margin"], got["argmax"], got["target"], z, targets))

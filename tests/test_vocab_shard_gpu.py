@@ -129,3 +129,48 @@ def test_sharded_entry_single_rank(gpu):
     got = (margin.cpu().numpy(), amax.cpu().numpy().view(np.uint32), tl.cpu().numpy())
     for a, b in zip(got, ref):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("hidden_kind,edit", [("bf16", None), ("f32", "joint")])
+def test_packed_partials_equal_unsharded(gpu, hidden_kind, edit):
+    """lsx_readout_partials_device per shard, an element-wise signed maximum of the
+    packed int64 partials (what one all-reduce MAX computes across ranks), then
+    lsx_readout_partials_merge_device: equal to the unsharded readout bit for bit."""
+    import torch
+    V, H, n = 3001, 256, 300
+    w = synth.normal_bf16(3, 0, V * H, 0.02)
+    targets = synth.readout_targets(3, n, V)
+    targets[:3] = [0, 1001, V - 1]
+    if hidden_kind == "bf16":
+        hidden, kind = synth.readout_hidden(3, n, H), BF16
+    else:
+        hidden, kind = synth.normal_f32(5, 9, n * H).reshape(n, H), F32
+    spec = edit_of(edit, H)
+    rot = DeviceRotation.upload_edit(gpu, spec, H) if spec else None
+    r = rot.handle if rot else None
+    h, t = device_inputs(gpu, hidden, targets)
+    ref = unsharded(gpu, w, None, V, H, h, kind, t, rot)
+    w2 = w.reshape(V, H)
+    merged, keep = None, []
+    for v0, v1 in [(0, 1000), (1000, 1002), (1002, V)]:
+        shard = gpu.upload_raw(np.ascontiguousarray(w2[v0:v1]), BF16)
+        ws = torch.empty(lib.lsx_readout_workspace_bytes(v1 - v0, H, n, r), dtype=torch.uint8, device=h.device)
+        part = torch.empty(2 * n, dtype=torch.int64, device=h.device)
+        torch.cuda.synchronize(h.device)
+        check(lib.lsx_readout_partials_device(gpu.handle, shard.handle, None, v0, v1 - v0, H,
+                                              C.c_void_p(h.data_ptr()), kind, n, C.c_void_p(t.data_ptr()), r,
+                                              C.c_void_p(part.data_ptr()), C.c_void_p(ws.data_ptr()), ws.numel()))
+        check(lib.lsx_readout_status(gpu.handle, C.c_void_p(ws.data_ptr())))
+        merged = part if merged is None else torch.maximum(merged, part)
+        keep.append((shard, ws))
+    margin = torch.empty(n, dtype=torch.float64, device=h.device)
+    amax = torch.empty(n, dtype=torch.int32, device=h.device)
+    tl = torch.empty(n, dtype=torch.float32, device=h.device)
+    torch.cuda.synchronize(h.device)
+    check(lib.lsx_readout_partials_merge_device(gpu.handle, C.c_void_p(merged.data_ptr()), C.c_void_p(t.data_ptr()),
+                                                n, C.c_void_p(margin.data_ptr()), C.c_void_p(amax.data_ptr()),
+                                                C.c_void_p(tl.data_ptr())))
+    gpu.synchronize()
+    got = (margin.cpu().numpy(), amax.cpu().numpy().view(np.uint32), tl.cpu().numpy())
+    for a, b in zip(got, ref):
+        assert np.array_equal(a, b), np.nonzero(a != b)[0][:8]
