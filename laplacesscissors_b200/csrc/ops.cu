@@ -8,6 +8,7 @@
 #include <cmath>
 #include <vector>
 
+#include "device_common.cuh"
 #include "lsx_internal.h"
 
 namespace lsx {
@@ -161,6 +162,120 @@ __global__ void __launch_bounds__(256) gemv_vector_kernel(const void* __restrict
     if (g == 0 && r < rows) out[r] = bias ? acc + bias[r] : acc;
 }
 
+// Streaming bf16 GEMV for matrices that span the GPU (kernels/ops.py:14-28 with W
+// bf16 and x f32): one CTA per SM owns a contiguous block of rows, which is one
+// contiguous byte range of W, and streams it through a ring of shared-memory
+// stages with 1-D bulk copies issued by a producer warp, so each SM keeps up to
+// kStreamStages x 32 KB of weights in flight whatever the compute warps are doing.
+// x is staged once per CTA in shared memory; each compute warp takes two rows of a
+// stage at a time, so every x load serves two rows.  Waits are bounded: a stage
+// that never lands (a failed copy) ends the CTA's work and its rows read NaN.
+constexpr int kStreamWarps = 8;
+constexpr int kStreamThreads = (kStreamWarps + 1) * 32;
+constexpr int kStreamChunk = 32768;  // bytes per stage at most
+constexpr int kStreamStages = 6;
+
+struct StreamPlan {
+    int rows_per_stage, stages;
+    size_t smem;
+};
+
+StreamPlan stream_plan(int cols, size_t smem_limit) {
+    StreamPlan p{};
+    p.rows_per_stage = (kStreamChunk / (2 * cols)) & ~1;  // even: the warps take rows in pairs
+    const size_t stage = (size_t)p.rows_per_stage * cols * 2;
+    const size_t fixed = (size_t)cols * 4 + 2 * kStreamStages * 8 + 128;
+    p.stages = 0;
+    for (int st = kStreamStages; st >= 2; --st)
+        if (fixed + st * stage <= smem_limit) {
+            p.stages = st;
+            break;
+        }
+    p.smem = fixed + (size_t)p.stages * stage;
+    return p;
+}
+
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    gemv_stream_kernel(const __nv_bfloat16* __restrict__ W, const float* __restrict__ x,
+                       const float* __restrict__ bias, int rows, int cols, int rows_per_stage, int stages,
+                       float* __restrict__ out) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const size_t stage_bytes = (size_t)rows_per_stage * cols * 2;
+    float* xs = reinterpret_cast<float*>(smem + (size_t)stages * stage_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs + cols);
+    uint64_t* empty = full + kStreamStages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = (int)(((long long)blockIdx.x * rows) / gridDim.x);
+    const int r1 = (int)(((long long)(blockIdx.x + 1) * rows) / gridDim.x);
+    const int nchunks = (r1 - r0 + rows_per_stage - 1) / rows_per_stage;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kStreamWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == kStreamWarps) {  // ------------------------------ producer
+        if (lane == 0) {
+            const uint64_t policy = l2_evict_first_policy();
+            for (int ch = 0; ch < nchunks; ++ch) {
+                const int slot = ch % stages;
+                if (ch >= stages && !mbar_wait_bounded(&empty[slot], (uint32_t)(((ch / stages) - 1) & 1))) break;
+                const int a = r0 + ch * rows_per_stage, n = min(rows_per_stage, r1 - a);
+                const uint32_t bytes = (uint32_t)n * (uint32_t)cols * 2u;
+                mbar_expect_tx(&full[slot], bytes);
+                bulk_load_hint(smem + (size_t)slot * stage_bytes, W + (size_t)a * cols, bytes, &full[slot], policy);
+            }
+        }
+        return;
+    }
+    // -------------------------------------------------------------- compute
+    // x is staged while the first weight stages are already in flight (named
+    // barrier 1 joins the compute warps only).
+    for (int i = threadIdx.x; i < cols / 4; i += kStreamWarps * 32)
+        reinterpret_cast<float4*>(xs)[i] = __ldg(reinterpret_cast<const float4*>(x) + i);
+    asm volatile("bar.sync 1, %0;" ::"n"(kStreamWarps * 32) : "memory");
+    // Row pairs are dealt to the warps round-robin across stages (rows_per_stage is
+    // even), so wide rows (a few per stage) still keep every warp busy.  Every warp
+    // waits for every stage before it releases it: a release then always belongs
+    // to the stage's current use.
+    const int nk = cols >> 3;  // 16-byte chunks per row
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
+    const int pairs_per_stage = rows_per_stage / 2;
+    bool ok = true;
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int slot = ch % stages;
+        const int a = r0 + ch * rows_per_stage, n = min(rows_per_stage, r1 - a);
+        ok = ok && mbar_wait_bounded(&full[slot], (uint32_t)((ch / stages) & 1));
+        const uint8_t* base = smem + (size_t)slot * stage_bytes;
+        const int first = (kStreamWarps + warp - (ch * pairs_per_stage) % kStreamWarps) % kStreamWarps;
+        for (int i = 2 * first; i < n; i += 2 * kStreamWarps) {
+            const bool two = i + 1 < n;
+            const uint4* w0 = reinterpret_cast<const uint4*>(base + (size_t)i * cols * 2);
+            const uint4* w1 = reinterpret_cast<const uint4*>(base + (size_t)(two ? i + 1 : i) * cols * 2);
+            float s0 = 0.f, s1 = 0.f;
+            if (ok) {
+                for (int c = lane; c < nk; c += 32) {
+                    const float4 xa = x4[2 * c], xb = x4[2 * c + 1];
+                    s0 += dot8<LSX_BF16>(w0[c], xa, xb);
+                    s1 += dot8<LSX_BF16>(w1[c], xa, xb);
+                }
+            }
+            s0 = warp_sum(s0);
+            s1 = warp_sum(s1);
+            if (lane == 0) {
+                const int r = a + i;
+                out[r] = ok ? (bias ? s0 + bias[r] : s0) : __int_as_float(0x7fc00000);
+                if (two) out[r + 1] = ok ? (bias ? s1 + bias[r + 1] : s1) : __int_as_float(0x7fc00000);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (!ok) return;
+}
+
 // Any shape or alignment: one warp per row, scalar loads.
 __global__ void gemv_scalar_kernel(const void* __restrict__ W, int kind, const float* __restrict__ x,
                                    const float* __restrict__ bias, int rows, int cols,
@@ -198,10 +313,30 @@ static cudaError_t launch_gemv_kind(cudaStream_t s, int sm, const void* w, const
     }
 }
 
+// Matrices of at least this many bytes stream through the shared-memory ring.
+constexpr size_t kStreamMinBytes = size_t(32) << 20;
+
 cudaError_t launch_matvec(cudaStream_t s, int sm, const void* w, int kind, const float* x, const float* bias,
                           size_t rows, size_t cols, float* out) {
     bool aligned = ((uintptr_t)w % 16 == 0) && ((uintptr_t)x % 16 == 0);
     bool vector = aligned && (kind == LSX_F32 ? cols % 4 == 0 : cols % 8 == 0);
+    if (vector && kind == LSX_BF16 && rows * cols * 2 >= kStreamMinBytes && cols <= 8192 &&
+        rows >= (size_t)4 * sm) {
+        int device = 0, limit = 0;
+        cudaError_t e = cudaGetDevice(&device);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+        if (e != cudaSuccess) return e;
+        const StreamPlan plan = stream_plan((int)cols, (size_t)limit);
+        if (plan.stages >= 2 && plan.rows_per_stage >= 2) {
+            e = cudaFuncSetAttribute((const void*)gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)plan.smem);
+            if (e != cudaSuccess) return e;
+            gemv_stream_kernel<<<sm, kStreamThreads, plan.smem, s>>>((const __nv_bfloat16*)w, x, bias, (int)rows,
+                                                                     (int)cols, plan.rows_per_stage, plan.stages,
+                                                                     out);
+            return cudaGetLastError();
+        }
+    }
     if (vector) {
         if (kind == LSX_BF16) return launch_gemv_kind<LSX_BF16>(s, sm, w, x, bias, (int)rows, (int)cols, out);
         if (kind == LSX_F16) return launch_gemv_kind<LSX_F16>(s, sm, w, x, bias, (int)rows, (int)cols, out);

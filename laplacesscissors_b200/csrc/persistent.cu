@@ -55,6 +55,9 @@ constexpr int kWarps = 7;                    // compute warps (2 warps per SM su
 constexpr int kThreads = (kWarps + 1) * 32;  // + producer warp
 constexpr int kCompute = kWarps * 32;
 constexpr long long kSpin = 4000000000ll;     // ~2 s at B200 clocks
+// Argmax partials sit one per 128-byte line: every CTA polls every partial, and
+// packed into a few lines those polls queued on a handful of L2 slices.
+constexpr int kArgStride = 16;
 
 // Clock cycles an exchange wait may spin before it gives up: kSpin, or the
 // failure-path test hook's shorter limit (DecodeState::spin_limit).  Set by thread 0
@@ -133,6 +136,20 @@ __device__ __forceinline__ bool compute_and(bool v) {
 __device__ __forceinline__ void raise_abort(DecodeState* st, int code) { atomicCAS(&st->status, 0, code); }
 __device__ __forceinline__ bool aborted(DecodeState* st) { return ld_relaxed_int(&st->status) != 0; }
 
+// Clock cycles a wait spins before it also watches the abort flag (~10 us; a
+// healthy exchange completes in about one).  Reading the one abort word on every
+// polling round of every warp of every CTA queued a thousand requests per round
+// on a single L2 line, in front of the exchange data that shares its slice.
+constexpr long long kAbortWatchAfter = 20000;
+
+// True when a wait that started at `start` should give up: past its spin limit,
+// or past kAbortWatchAfter with another CTA having aborted the run.
+__device__ __forceinline__ bool give_up(long long start, DecodeState* st) {
+    const long long waited = clock64() - start;
+    if (waited < kAbortWatchAfter) return false;
+    return waited > s_spin || aborted(st);
+}
+
 // Argmax partial: total-order value (32) | 0x7FFFF - index (19) | epoch (13).
 __device__ __forceinline__ unsigned long long arg_word(unsigned long long key, uint32_t epoch) {
     const uint32_t value = (uint32_t)(key >> 32);
@@ -178,7 +195,7 @@ __device__ bool poll_vector(const unsigned long long* src, int n, uint32_t epoch
             }
             if (start == 0) {
                 start = clock64();
-            } else if (clock64() - start > s_spin || aborted(st)) {
+            } else if (give_up(start, st)) {
                 ok = false;
                 break;
             }
@@ -234,7 +251,7 @@ __device__ bool poll_segments(const unsigned long long* s0, int n0, float* d0, c
                 if ((uint32_t)(v[j] >> 32) != epoch) v[j] = ld_relaxed(src[j]);
             if (start == 0) {
                 start = clock64();
-            } else if (clock64() - start > s_spin || aborted(st)) {
+            } else if (give_up(start, st)) {
                 ok = false;
                 break;
             }
@@ -419,13 +436,26 @@ struct XRegs {
 
 // RMSNorm gains in the XRegs layout, fetched before the activations are waited for.
 template <int KCH>
+// Two 16-byte loads per 8-element slice (gains are 16-byte aligned library
+// allocations): scalar loads at a 32-byte lane stride touched 32 sectors per
+// instruction and delayed the residual polls behind them.
 struct GainX {
     float g[8 * (KCH > 0 ? KCH : 1)];
     __device__ __forceinline__ void load(const float* gain, int lane) {
+        const float4* g4 = reinterpret_cast<const float4*>(gain);
 #pragma unroll
-        for (int j = 0; j < KCH; ++j)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[8 * j + e] = gain ? __ldg(gain + 8 * (lane + 32 * j) + e) : 1.f;
+        for (int j = 0; j < KCH; ++j) {
+            const float4 a = gain ? __ldg(g4 + 2 * (lane + 32 * j)) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 b = gain ? __ldg(g4 + 2 * (lane + 32 * j) + 1) : make_float4(1.f, 1.f, 1.f, 1.f);
+            g[8 * j + 0] = a.x;
+            g[8 * j + 1] = a.y;
+            g[8 * j + 2] = a.z;
+            g[8 * j + 3] = a.w;
+            g[8 * j + 4] = b.x;
+            g[8 * j + 5] = b.y;
+            g[8 * j + 6] = b.z;
+            g[8 * j + 7] = b.w;
+        }
     }
 };
 
@@ -1421,18 +1451,18 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
             if (tid == 0 && !(c == hold_cta && step == hold_step)) {
                 unsigned long long b = 0ull;
                 for (int i = 0; i < kWarps; ++i) b = rb[i] > b ? rb[i] : b;
-                st_relaxed(a.t_arg + c, arg_word(b, e_head));
+                st_relaxed(a.t_arg + (size_t)c * kArgStride, arg_word(b, e_head));
             }
             // ---- gather the step's argmax from every CTA's partial
             unsigned long long* gathered = reinterpret_cast<unsigned long long*>(scratch);
             if (tid < G) {
-                const unsigned long long* src = a.t_arg + tid;
+                const unsigned long long* src = a.t_arg + (size_t)tid * kArgStride;
                 unsigned long long v = ld_relaxed(src);
                 long long start = 0;
                 while ((uint32_t)(v & 0x1FFFull) != (e_head & 0x1FFFu)) {
                     v = ld_relaxed(src);
                     if (start == 0) start = clock64();
-                    else if (clock64() - start > s_spin || aborted(st)) {
+                    else if (give_up(start, st)) {
                         ok = false;
                         break;
                     }
@@ -1589,6 +1619,9 @@ bool PersistentDecoder::eligible(const FusedConfig& c, const lsx_ctx* ctx, std::
 int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vector<FusedLayer>& layers) {
     std::string why;
     if (!eligible(c, ctx, &why)) return fail(LSX_E_UNSUPPORTED, "persistent decode plan: " + why);
+    for (const FusedLayer& L : layers)  // the register-resident RMSNorm gains are read 16 bytes at a time
+        LSX_ENSURE((uintptr_t)L.input_gain % 16 == 0 && (uintptr_t)L.post_gain % 16 == 0,
+                   "persistent decode plan: norm gains must be 16-byte aligned");
     ctx_ = ctx;
     config_ = c;
     grid_ = ctx->sm_count;
@@ -1607,7 +1640,7 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
     LSX_TRY(alloc((size_t)(qw + 2 * kw) * 8, (void**)&t_qkv_));
     LSX_TRY(alloc((size_t)qw * 8, (void**)&t_attn_));
     LSX_TRY(alloc((size_t)c.intermediate * 8, (void**)&t_feat_));
-    LSX_TRY(alloc((size_t)grid_ * 8, (void**)&t_arg_));
+    LSX_TRY(alloc((size_t)grid_ * kArgStride * 8, (void**)&t_arg_));
     // Split attention from position split_min_ - 1 on (LSX_DECODE_SPLIT_MIN overrides;
     // 0 turns it off).
     ns_ = split_slots(c, grid_);

@@ -1121,6 +1121,226 @@ __global__ void __launch_bounds__(kImageThreads, 1)
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem_base) : "memory");
 }
 
+// ---------------------------------------------------- few-row store GEMM ----
+// out[M, ldo] (=|+=) (A_hi + A_lo) W^T (+ bias) for M <= 32 activation rows (a
+// batched decode step): the weight is the A operand of the MMA (128 rows of W per
+// tile, one per TMEM lane) and the activations' two bf16 planes are the B operand
+// (N = 2 Mp columns: Mp hi rows, then Mp lo rows, Mp = M rounded up to 16), so a
+// tile's tensor work is 128 x 2Mp per K step instead of a 256-row MMA with 16 live
+// rows, and the pass is bound by streaming W from HBM.  Work items are (weight
+// tile, K slice); with few tiles the K loop is split so every SM streams a share,
+// each slice's product goes plain into its own partial plane, and
+// split_reduce_kernel sums the slices in order (then bias, then the accumulate).
+//   warp 0     TMA producer: W tile 128 x 64, hi and lo tiles Mp x 64 per stage
+//   warp 1     TMEM owner, single-thread MMA issuer (M = 128, N = 2 Mp, K = 16)
+//   warps 2-5  epilogue: lane = weight row n, column m + column Mp + m = out[m, n]
+constexpr int kFewThreads = 192;
+constexpr int kFewMaxRows = 32;
+
+struct FewParams {
+    int M, Mp, N, k_blocks, n_tiles, ksplits, stages;
+    const float* bias;
+    float* out;        // ksplits == 1: out[m * ldo + n] (=|+=) value + bias
+    int ldo, accumulate;
+    float* partial;    // ksplits > 1: partial[(s * M + m) * N + n] = slice s's product
+    int* status;
+};
+
+__global__ void __launch_bounds__(kFewThreads, 1)
+    few_rows_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_hi,
+                    const __grid_constant__ CUtensorMap map_lo, const FewParams p) {
+    constexpr int kTileW = 128 * RK * 2;  // 16 KB
+    const int tile_a = p.Mp * RK * 2;     // one plane's tile
+    const int stage_bytes = kTileW + 2 * tile_a;
+    const int S = p.stages;
+    const int ncol = 2 * p.Mp;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+    uint64_t* empty = full + S;
+    uint64_t* tmem_full = empty + S;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued_count = const_cast<int*>(abort_flag) + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int items = p.n_tiles * p.ksplits;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tmem_full[a], 1);
+            mbar_init(&tmem_empty[a], 4 * 32);
+        }
+        *abort_flag = 0;
+        *issued_count = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {  // TMEM: two accumulators of 2 Mp <= 64 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(smem_u32(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---------------- TMA producer ----------------
+            int stage = 0, issued = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+                const int tile = item / p.ksplits, slice = item % p.ksplits;
+                const int kb0 = (int)((long long)slice * p.k_blocks / p.ksplits);
+                const int kb1 = (int)((long long)(slice + 1) * p.k_blocks / p.ksplits);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sw = smem + (size_t)stage * stage_bytes;
+                    mbar_expect_tx(&full[stage], (uint32_t)stage_bytes);
+                    tma_load_2d(sw, &map_w, kb * RK, tile * 128, &full[stage]);
+                    tma_load_2d(sw + kTileW, &map_hi, kb * RK, 0, &full[stage]);
+                    tma_load_2d(sw + kTileW + tile_a, &map_lo, kb * RK, 0, &full[stage]);
+                    ++issued;
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            *issued_count = issued;
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---------------- MMA issuer ----------------
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(ncol >> 3) << 17) |
+                                   ((uint32_t)(128 >> 4) << 24);
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+                const int slice = item % p.ksplits;
+                const int kb0 = (int)((long long)slice * p.k_blocks / p.ksplits);
+                const int kb1 = (int)((long long)(slice + 1) * p.k_blocks / p.ksplits);
+                if (!wait_or_abort(&tmem_empty[acc], acc_phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * 64);
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (!wait_or_abort(&full[stage], phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sw = smem_u32(smem + (size_t)stage * stage_bytes);
+                    const uint64_t adesc = smem_desc_sw128(sw), bdesc = smem_desc_sw128(sw + kTileW);
+#pragma unroll
+                    for (int k = 0; k < RK / 16; ++k)
+                        tc_mma(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc, (kb > kb0 || k > 0));
+                    tc_commit(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tmem_full[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                atomicExch(&p.status[0], kDeviceTimeoutMma);
+                *abort_flag = 1;
+            }
+        }
+        __syncwarp();
+    } else {  // ---------------- epilogue warps 2..5 ----------------
+        const int quarter = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool nonfinite = false;
+        for (int item = blockIdx.x; item < items; item += gridDim.x) {
+            const int tile = item / p.ksplits, slice = item % p.ksplits;
+            const bool ok = wait_or_abort(&tmem_full[acc], acc_phase, abort_flag);
+            if (__any_sync(0xffffffffu, !ok)) {
+                if (lane == 0) {
+                    atomicExch(&p.status[0], kDeviceTimeoutEpilogue);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int n = tile * 128 + quarter * 32 + lane;
+            const bool live = n < p.N;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 64);
+            uint32_t hi[32], lo[32];
+            tc_ld32(taddr, hi);
+            tc_wait_ld_regs(hi);
+            if (p.Mp > 16) {
+                tc_ld32(taddr + 32u, lo);
+                tc_wait_ld_regs(lo);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) lo[j] = hi[16 + j];
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);
+            if (live) {
+                const float b = (p.ksplits == 1 && p.bias) ? p.bias[n] : 0.f;
+#pragma unroll
+                for (int m = 0; m < kFewMaxRows; ++m) {
+                    if (m < p.M) {
+                        const float v = __uint_as_float(hi[m]) + __uint_as_float(lo[m]);
+                        if (p.ksplits > 1) {
+                            p.partial[((size_t)slice * p.M + m) * p.N + n] = v;
+                        } else {
+                            float* o = p.out + (size_t)m * p.ldo + n;
+                            const float r = p.accumulate ? *o + (v + b) : v + b;
+                            nonfinite |= !isfinite(r);
+                            *o = r;
+                        }
+                    }
+                }
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (__any_sync(0xffffffffu, nonfinite) && lane == 0) atomicOr(&p.status[1], 1);
+    }
+
+    __syncthreads();
+    if (*abort_flag) {
+        if (threadIdx.x == 0) {
+            const int issued = *issued_count;
+            for (int i = 0; i < S && i < issued; ++i) {
+                const int last = issued - 1 - ((issued - 1 - i) % S);
+                mbar_wait_bounded(&full[i], (uint32_t)((last / S) & 1));
+            }
+        }
+        __syncthreads();
+    }
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem_base) : "memory");
+}
+
 constexpr int kRankBlock = 16;
 constexpr int kMaxEditRank = 256;
 
@@ -1416,6 +1636,69 @@ cudaError_t launch_pair(lsx_ctx* ctx, const CUtensorMap& ma, const CUtensorMap& 
 
 }  // namespace
 
+// The few-row store GEMM (few_rows_kernel): K slices chosen so the (tile, slice)
+// items cover the SMs in whole waves, the cost being waves x K blocks per item
+// with a small charge per extra slice for the partial planes and their reduce.
+int few_rows_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int M, int K,
+                     const __nv_bfloat16* w, int N, const float* bias, float* out, int ldo, bool accumulate,
+                     int* status) {
+    const int Mp = M <= 16 ? 16 : 32;
+    CUtensorMap mw, mhi, mlo;
+    LSX_TRY(make_map(&mw, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, 128));
+    LSX_TRY(make_map(&mhi, a_hi, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, (uint32_t)Mp));
+    LSX_TRY(make_map(&mlo, a_lo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, (uint32_t)Mp));
+    FewParams p{};
+    p.M = M;
+    p.Mp = Mp;
+    p.N = N;
+    p.k_blocks = (K + RK - 1) / RK;
+    p.n_tiles = (N + 127) / 128;
+    p.bias = bias;
+    p.out = out;
+    p.ldo = ldo;
+    p.accumulate = accumulate ? 1 : 0;
+    p.status = status;
+    const int G = ctx->sm_count;
+    int best_ks = 1;
+    double best_cost = 1e300;
+    for (int ks = 1; ks <= 16 && ks <= std::max(1, p.k_blocks / 2); ++ks) {
+        const double waves = std::ceil((double)p.n_tiles * ks / G);
+        const double cost = waves * std::ceil((double)p.k_blocks / ks) * (1.0 + 0.03 * (ks - 1));
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best_ks = ks;
+        }
+    }
+    if (const char* v = getenv("LSX_FEW_ROWS_SPLITS")) best_ks = std::max(1, std::min(16, atoi(v)));
+    p.ksplits = best_ks;
+    const int stage_bytes = 128 * RK * 2 + 2 * Mp * RK * 2;
+    const size_t fixed = 1024 + 8 * 8 * 2 + 64;
+    p.stages = (int)std::min<size_t>(8, (ctx->smem_optin - fixed) / stage_bytes);
+    LSX_ENSURE(p.stages >= 2, "few-row GEMM: shared memory");
+    const size_t smem = (size_t)p.stages * stage_bytes + 1024 + (2 * p.stages + 4) * 8 + 16;
+    void* part = nullptr;
+    if (p.ksplits > 1) {
+        LSX_TRY(device_alloc(ctx, (size_t)p.ksplits * M * N * 4, &part));
+        p.partial = (float*)part;
+    }
+    cudaError_t e = cudaFuncSetAttribute((const void*)few_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e == cudaSuccess) {
+        const int items = p.n_tiles * p.ksplits;
+        few_rows_kernel<<<std::min(items, G), kFewThreads, smem, ctx->stream>>>(mw, mhi, mlo, p);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && p.ksplits > 1) {
+        const size_t total = (size_t)M * N;
+        split_reduce_kernel<<<(int)std::min<size_t>((total + 255) / 256, 4096), 256, 0, ctx->stream>>>(
+            (const float*)part, p.ksplits, M, N, bias, out, ldo, accumulate ? 1 : 0, status);
+        e = cudaGetLastError();
+    }
+    if (part) device_release(ctx, part);  // stream-ordered: later users of the block run after the reduce
+    LSX_CUDA(e, "few-row GEMM launch");
+    return LSX_OK;
+}
+
 // out[M, ldo] (=|+=) (A_hi + A_lo) W^T (+ bias) on the tensor cores: A as two bf16
 // planes [M, K] (an f32 operand split hi/lo), W bf16 [N, K]; f32 accumulate.
 // status[0] receives a device error code, status[1] the non-finite flag.
@@ -1440,6 +1723,11 @@ int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bflo
     p.out = out;
     p.ldo = ldo;
     p.accumulate = accumulate ? 1 : 0;
+    // A batched decode step (a few activation rows): the weight as the 128-row
+    // operand (LSX_GEMM_FEW_ROWS=0 keeps the CTA-pair path).
+    const char* few = getenv("LSX_GEMM_FEW_ROWS");
+    if (M <= kFewMaxRows && !(few && few[0] == '0'))
+        return few_rows_enqueue(ctx, a_hi, a_lo, M, K, w, N, bias, out, ldo, accumulate, status);
     const char* single = getenv("LSX_GEMM_SINGLE");
     if (!(single && single[0] == '1') && ctx->sm_count >= 2) {
         // CTA pairs (cta_group::2): each CTA loads half of the weight tile
