@@ -92,8 +92,10 @@ void device_release(lsx_ctx* ctx, void* p);
 
 // ---- kernel launchers (ops.cu) ----
 cudaError_t launch_take_row(cudaStream_t s, const void* w, int kind, size_t row, size_t width, float* out);
+// `stable_weight`: no kernel writes w (it was uploaded from the host), so a large
+// GEMV may start streaming it while the preceding kernel on the stream still runs.
 cudaError_t launch_matvec(cudaStream_t s, int sm_count, const void* w, int kind, const float* x,
-                          const float* bias, size_t rows, size_t cols, float* out);
+                          const float* bias, size_t rows, size_t cols, float* out, bool stable_weight = false);
 cudaError_t launch_norm(cudaStream_t s, const float* x, const float* gain, const float* bias,
                         size_t groups, size_t width, float eps, int center, float* out);
 cudaError_t launch_rope(cudaStream_t s, const float* x, size_t position, size_t heads, size_t dim,

@@ -790,7 +790,8 @@ int run_norm(lsx_model* m, const lsx_model::Norm& n, const float* x, float* out)
 }
 int run_proj(lsx_model* m, const lsx_model::Proj& p, const float* x, float* out, bool with_bias = true) {
     LSX_K(launch_matvec(m->ctx->stream, m->ctx->sm_count, p.weight->data, p.weight->kind, x,
-                        (with_bias && p.bias) ? (const float*)p.bias->data : nullptr, p.out, p.in, out),
+                        (with_bias && p.bias) ? (const float*)p.bias->data : nullptr, p.out, p.in, out,
+                        true),  // checkpoint weights: uploaded once, never written
           "matvec");
     return LSX_OK;
 }

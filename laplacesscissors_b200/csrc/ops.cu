@@ -104,6 +104,11 @@ __global__ void __launch_bounds__(256) gemv_vector_kernel(const void* __restrict
     const int r = blockIdx.x * RPC + t / G;
     const int g = t % G;
     float acc = 0.f;
+    if (threadIdx.x == 0) pdl_launch_dependents();
+    // x and the output depend on earlier kernels; the weights do not, so the first
+    // weight loads are issued before waiting for the preceding grid (a no-op unless
+    // launched as a programmatic dependent)
+    bool waited = false;
     if (r < rows) {
         if (KIND == LSX_F32) {
             const int chunks = cols >> 2;
@@ -114,6 +119,10 @@ __global__ void __launch_bounds__(256) gemv_vector_kernel(const void* __restrict
                 for (int u = 0; u < UNROLL; ++u) {
                     int c = base + u * G;
                     w[u] = c < chunks ? load_stream(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+                }
+                if (!waited) {
+                    pdl_wait();
+                    waited = true;
                 }
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u) {
@@ -137,6 +146,10 @@ __global__ void __launch_bounds__(256) gemv_vector_kernel(const void* __restrict
                     int c = base + u * G;
                     w[u] = c < chunks ? load_stream(row + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
                 }
+                if (!waited) {
+                    pdl_wait();
+                    waited = true;
+                }
 #pragma unroll
                 for (int u = 0; u < UNROLL; ++u) {
                     int c = base + u * G;
@@ -149,6 +162,7 @@ __global__ void __launch_bounds__(256) gemv_vector_kernel(const void* __restrict
             }
         }
     }
+    if (!waited) pdl_wait();  // before the output write
     acc = warp_sum(acc);
     if (G > 32) {
         if ((t & 31) == 0) partial[t >> 5] = acc;
@@ -214,6 +228,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
             mbar_init(&empty[i], kStreamWarps);
         }
         fence_barrier_init();
+        pdl_launch_dependents();  // the next kernel may start fetching its own weights
     }
     __syncthreads();
     if (warp == kStreamWarps) {  // ------------------------------ producer
@@ -232,7 +247,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     }
     // -------------------------------------------------------------- compute
     // x is staged while the first weight stages are already in flight (named
-    // barrier 1 joins the compute warps only).
+    // barrier 1 joins the compute warps only).  Weights never depend on earlier
+    // kernels; x and the outputs do, so they wait for the preceding grid here (a
+    // no-op unless this kernel was launched as a programmatic dependent).
+    pdl_wait();
     for (int i = threadIdx.x; i < cols / 4; i += kStreamWarps * 32)
         reinterpret_cast<float4*>(xs)[i] = __ldg(reinterpret_cast<const float4*>(x) + i);
     asm volatile("bar.sync 1, %0;" ::"n"(kStreamWarps * 32) : "memory");
@@ -292,24 +310,31 @@ __global__ void gemv_scalar_kernel(const void* __restrict__ W, int kind, const f
 
 template <int KIND, int G>
 static cudaError_t launch_gemv_g(cudaStream_t s, const void* w, const float* x, const float* b, int rows,
-                                 int cols, float* out) {
+                                 int cols, float* out, bool stable_weight) {
     constexpr int RPC = 256 / G;
-    int grid = (rows + RPC - 1) / RPC;
-    gemv_vector_kernel<KIND, G><<<grid, 256, 0, s>>>(w, x, b, rows, cols, out);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((rows + RPC - 1) / RPC);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = stable_weight ? 1 : 0;  // early weight loads need weights no kernel writes
+    return cudaLaunchKernelEx(&cfg, gemv_vector_kernel<KIND, G>, w, x, b, rows, cols, out);
 }
 
 template <int KIND>
 static cudaError_t launch_gemv_kind(cudaStream_t s, int sm, const void* w, const float* x, const float* b,
-                                    int rows, int cols, float* out) {
+                                    int rows, int cols, float* out, bool stable_weight) {
     int chunks = KIND == LSX_F32 ? cols / 4 : cols / 8;
     int G = 32;
     while (G < 256 && (long)rows * G / 256 < 2L * sm && chunks >= 4 * G) G *= 2;
     switch (G) {
-    case 32: return launch_gemv_g<KIND, 32>(s, w, x, b, rows, cols, out);
-    case 64: return launch_gemv_g<KIND, 64>(s, w, x, b, rows, cols, out);
-    case 128: return launch_gemv_g<KIND, 128>(s, w, x, b, rows, cols, out);
-    default: return launch_gemv_g<KIND, 256>(s, w, x, b, rows, cols, out);
+    case 32: return launch_gemv_g<KIND, 32>(s, w, x, b, rows, cols, out, stable_weight);
+    case 64: return launch_gemv_g<KIND, 64>(s, w, x, b, rows, cols, out, stable_weight);
+    case 128: return launch_gemv_g<KIND, 128>(s, w, x, b, rows, cols, out, stable_weight);
+    default: return launch_gemv_g<KIND, 256>(s, w, x, b, rows, cols, out, stable_weight);
     }
 }
 
@@ -317,7 +342,7 @@ static cudaError_t launch_gemv_kind(cudaStream_t s, int sm, const void* w, const
 constexpr size_t kStreamMinBytes = size_t(32) << 20;
 
 cudaError_t launch_matvec(cudaStream_t s, int sm, const void* w, int kind, const float* x, const float* bias,
-                          size_t rows, size_t cols, float* out) {
+                          size_t rows, size_t cols, float* out, bool stable_weight) {
     bool aligned = ((uintptr_t)w % 16 == 0) && ((uintptr_t)x % 16 == 0);
     bool vector = aligned && (kind == LSX_F32 ? cols % 4 == 0 : cols % 8 == 0);
     if (vector && kind == LSX_BF16 && rows * cols * 2 >= kStreamMinBytes && cols <= 8192 &&
@@ -331,16 +356,26 @@ cudaError_t launch_matvec(cudaStream_t s, int sm, const void* w, int kind, const
             e = cudaFuncSetAttribute((const void*)gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)plan.smem);
             if (e != cudaSuccess) return e;
-            gemv_stream_kernel<<<sm, kStreamThreads, plan.smem, s>>>((const __nv_bfloat16*)w, x, bias, (int)rows,
-                                                                     (int)cols, plan.rows_per_stage, plan.stages,
-                                                                     out);
-            return cudaGetLastError();
+            // programmatic dependent launch: the weight stream starts while the
+            // previous kernel on the stream finishes; x is read after it completes
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(sm);
+            cfg.blockDim = dim3(kStreamThreads);
+            cfg.dynamicSmemBytes = plan.smem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = stable_weight ? 1 : 0;
+            return cudaLaunchKernelEx(&cfg, gemv_stream_kernel, (const __nv_bfloat16*)w, x, bias, (int)rows,
+                                      (int)cols, plan.rows_per_stage, plan.stages, out);
         }
     }
     if (vector) {
-        if (kind == LSX_BF16) return launch_gemv_kind<LSX_BF16>(s, sm, w, x, bias, (int)rows, (int)cols, out);
-        if (kind == LSX_F16) return launch_gemv_kind<LSX_F16>(s, sm, w, x, bias, (int)rows, (int)cols, out);
-        return launch_gemv_kind<LSX_F32>(s, sm, w, x, bias, (int)rows, (int)cols, out);
+        if (kind == LSX_BF16) return launch_gemv_kind<LSX_BF16>(s, sm, w, x, bias, (int)rows, (int)cols, out, stable_weight);
+        if (kind == LSX_F16) return launch_gemv_kind<LSX_F16>(s, sm, w, x, bias, (int)rows, (int)cols, out, stable_weight);
+        return launch_gemv_kind<LSX_F32>(s, sm, w, x, bias, (int)rows, (int)cols, out, stable_weight);
     }
     int warps_per_block = 8;
     int grid = (int)((rows + warps_per_block - 1) / warps_per_block);
@@ -689,8 +724,10 @@ int lsx_linear_into(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* w, cons
                    (!bias || bias->count == rows) && out->count == rows,
                "check the dimensions of the linear op");
     cudaSetDevice(ctx->device);
+    // a BF16 tensor the library owns was uploaded from the host (every op output is
+    // F32), so no kernel writes it; wrapped caller memory might be
     LSX_CUDA(launch_matvec(ctx->stream, ctx->sm_count, w->data, w->kind, (const float*)x->data,
-                           bias ? (const float*)bias->data : nullptr, rows, cols, (float*)out->data),
+                           bias ? (const float*)bias->data : nullptr, rows, cols, (float*)out->data, w->owned),
              "matvec");
     return LSX_OK;
 }
@@ -707,7 +744,7 @@ int lsx_linear(lsx_ctx* ctx, const lsx_tensor* x, const lsx_tensor* w, const lsx
     LSX_TRY(reserve(ctx, rows, LSX_F32, &o));
     return finish(ctx,
                   launch_matvec(ctx->stream, ctx->sm_count, w->data, w->kind, (const float*)x->data,
-                                bias ? (const float*)bias->data : nullptr, rows, cols, (float*)o->data),
+                                bias ? (const float*)bias->data : nullptr, rows, cols, (float*)o->data, w->owned),
                   o, out, "matvec");
 }
 

@@ -1153,10 +1153,10 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
     // gate/up: whole (gate, up) pairs; at H = 1024 a CTA holds 40-42 rows, six per warp
     constexpr int NRG = KH > 0 && KH <= 4 ? 8 : 2;
     constexpr int NVG = KH > 0 && KH <= 4 ? 6 : 2;
-    // o and down own ~7 rows per CTA at hidden 1024: four rows per warp pass keep
-    // two warps busy and read x from shared memory twice rather than seven times.
-    constexpr int NRQ = KQ > 4 ? 4 : rows_for(KQ);  // o
-    constexpr int NRI = KI > 4 ? 4 : rows_for(KI);  // down
+    // o and down own ~7 rows per CTA at hidden 1024: one row per warp (four rows
+    // per warp, x read twice instead of seven times, measured 1.8x slower rows)
+    constexpr int NRQ = KQ > 4 ? 1 : rows_for(KQ);  // o
+    constexpr int NRI = KI > 4 ? 1 : rows_for(KI);  // down
     constexpr int PB = DPL >= 8 ? 4 : 8;            // attention positions per warp batch
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;

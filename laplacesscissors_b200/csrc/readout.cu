@@ -807,6 +807,7 @@ __global__ void __launch_bounds__(kReadoutThreads, 1)
 __global__ void split_reduce_kernel(const float* __restrict__ partial, int ksplits, int M, int N,
                                     const float* __restrict__ bias, float* __restrict__ out, int ldo, int accumulate,
                                     int* status) {
+    pdl_wait();  // a no-op unless launched as a programmatic dependent of the GEMM
     const size_t total = (size_t)M * N, plane = total;
     bool bad = false;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -1140,7 +1141,7 @@ constexpr int kFewMaxRows = 32;
 struct FewParams {
     int M, Mp, N, k_blocks, n_tiles, ksplits, stages;
     const float* bias;
-    float* out;        // ksplits == 1: out[m * ldo + n] (=|+=) value + bias
+    float* out;        // out[m * ldo + n] (=|+=) value + bias
     int ldo, accumulate;
     float* partial;    // ksplits > 1: partial[(s * M + m) * N + n] = slice s's product
     int* status;
@@ -1179,6 +1180,7 @@ __global__ void __launch_bounds__(kFewThreads, 1)
         *abort_flag = 0;
         *issued_count = 0;
         fence_barrier_init();
+        pdl_launch_dependents();
     }
     if (warp == 1) {  // TMEM: two accumulators of 2 Mp <= 64 columns
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(smem_u32(tmem_slot))
@@ -1278,8 +1280,16 @@ __global__ void __launch_bounds__(kFewThreads, 1)
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
             const int tile = item / p.ksplits, slice = item % p.ksplits;
             const bool ok = wait_or_abort(&tmem_full[acc], acc_phase, abort_flag);
-            if (__any_sync(0xffffffffu, !ok)) {
-                if (lane == 0) {
+            // one decision for all four epilogue warps, which meet at named barriers below
+            uint32_t bad;
+            asm volatile(
+                "{\n\t.reg .pred p, q;\n\tsetp.eq.u32 p, %1, 0;\n\tbar.red.or.pred q, 3, 128, p;\n\t"
+                "selp.u32 %0, 1, 0, q;\n\t}"
+                : "=r"(bad)
+                : "r"((uint32_t)ok)
+                : "memory");
+            if (bad) {
+                if (quarter == 0 && lane == 0) {
                     atomicExch(&p.status[0], kDeviceTimeoutEpilogue);
                     *abort_flag = 1;
                 }
@@ -1301,15 +1311,13 @@ __global__ void __launch_bounds__(kFewThreads, 1)
             }
             tc_fence_before();
             mbar_arrive(&tmem_empty[acc]);
-            if (live) {
-                const float b = (p.ksplits == 1 && p.bias) ? p.bias[n] : 0.f;
+            const float b = (live && p.bias) ? p.bias[n] : 0.f;
+            if (p.ksplits == 1) {
+                if (live) {
 #pragma unroll
-                for (int m = 0; m < kFewMaxRows; ++m) {
-                    if (m < p.M) {
-                        const float v = __uint_as_float(hi[m]) + __uint_as_float(lo[m]);
-                        if (p.ksplits > 1) {
-                            p.partial[((size_t)slice * p.M + m) * p.N + n] = v;
-                        } else {
+                    for (int m = 0; m < kFewMaxRows; ++m) {
+                        if (m < p.M) {
+                            const float v = __uint_as_float(hi[m]) + __uint_as_float(lo[m]);
                             float* o = p.out + (size_t)m * p.ldo + n;
                             const float r = p.accumulate ? *o + (v + b) : v + b;
                             nonfinite |= !isfinite(r);
@@ -1317,6 +1325,11 @@ __global__ void __launch_bounds__(kFewThreads, 1)
                         }
                     }
                 }
+            } else if (live) {  // this slice's product; split_reduce_kernel sums the slices in order
+#pragma unroll
+                for (int m = 0; m < kFewMaxRows; ++m)
+                    if (m < p.M)
+                        p.partial[((size_t)slice * p.M + m) * p.N + n] = __uint_as_float(hi[m]) + __uint_as_float(lo[m]);
             }
             if (++acc == 2) {
                 acc = 0;
@@ -1689,10 +1702,20 @@ int few_rows_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat1
         e = cudaGetLastError();
     }
     if (e == cudaSuccess && p.ksplits > 1) {
+        // the in-order sum of the slices, launched as a programmatic dependent so its
+        // launch overlaps the GEMM's tail (it waits for the GEMM before reading)
         const size_t total = (size_t)M * N;
-        split_reduce_kernel<<<(int)std::min<size_t>((total + 255) / 256, 4096), 256, 0, ctx->stream>>>(
-            (const float*)part, p.ksplits, M, N, bias, out, ldo, accumulate ? 1 : 0, status);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)std::min<size_t>((total + 255) / 256, 4096));
+        cfg.blockDim = dim3(256);
+        cfg.stream = ctx->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, split_reduce_kernel, (const float*)part, p.ksplits, M, N, bias, out, ldo,
+                               accumulate ? 1 : 0, status);
     }
     if (part) device_release(ctx, part);  // stream-ordered: later users of the block run after the reduce
     LSX_CUDA(e, "few-row GEMM launch");
