@@ -762,6 +762,44 @@ __device__ __forceinline__ void lane_row_load(const float* src, float (&x)[E]) {
     }
 }
 
+// Packed f32 pairs: Blackwell's fma.rn.f32x2 does two multiply-adds per instruction.
+__device__ __forceinline__ unsigned long long pair_of(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void pair_fma(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float pair_lo(unsigned long long v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float pair_hi(unsigned long long v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// Sums CNT per-lane values over the 16 lanes of a half-warp at once: each halving
+// round exchanges half of the values with the lane OFF apart, so after log2(CNT)
+// rounds each lane carries one value and the plain rounds complete its sum.  Lane
+// hl of the half ends with the total of value hl / (16 / CNT).
+template <int CNT, int OFF>
+struct HalfReduce {
+    static __device__ __forceinline__ void run(float* v, int lane) {
+        if constexpr (OFF > 0) {
+            if constexpr (CNT > 1) {
+                constexpr int half = CNT / 2;
+                const bool up = (lane & OFF) != 0;
+#pragma unroll
+                for (int i = 0; i < half; ++i) {
+                    const float keep = up ? v[i + half] : v[i];
+                    const float send = up ? v[i] : v[i + half];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+                }
+                HalfReduce<half, OFF / 2>::run(v, lane);
+            } else {
+                v[0] += __shfl_xor_sync(0xffffffffu, v[0], OFF);
+                HalfReduce<1, OFF / 2>::run(v, lane);
+            }
+        }
+    }
+};
+
 template <int DPL, int R>
 __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attention_part_kernel(
     const float* __restrict__ qkv, const float* __restrict__ keys, const float* __restrict__ values, int QH, int KVH,
@@ -780,15 +818,18 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
     const float* qrow = qkv + (size_t)c * (QH + 2 * KVH) * D;
     // ring slot: [K of the two halves' positions | V of the same], D floats each
     float* ring = smem + warp * (S * 4 * D) + half * D + hl * E;
-    float q[R][E], m[R], l[R], acc[R][E];
+    // q and the output accumulators as packed pairs of this lane's E elements
+    unsigned long long q2[R][E / 2], acc2[R][E / 2];
+    float m[R], l[R];
 #pragma unroll
     for (int i = 0; i < R; ++i) {
         m[i] = -INFINITY;
         l[i] = 0.f;
+        const float* qh = qrow + (size_t)(g * R + i) * D + hl * E;
 #pragma unroll
-        for (int j = 0; j < E; ++j) {
-            q[i][j] = qrow[(size_t)(g * R + i) * D + hl * E + j];
-            acc[i][j] = 0.f;
+        for (int j = 0; j < E / 2; ++j) {
+            q2[i][j] = pair_of(qh[2 * j], qh[2 * j + 1]);
+            acc2[i][j] = 0ull;
         }
     }
     const int first = t0 + walker;
@@ -819,26 +860,41 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
         float k[E], v[E];
         lane_row_load<E>(ring + slot * 4 * D, k);
         lane_row_load<E>(ring + slot * 4 * D + 2 * D, v);
+        // the R heads' partial dots, then one transposed butterfly over the half:
+        // lane hl holds head hl / (16 / R)'s score, which the other lanes read back
+        float sc[R];
 #pragma unroll
         for (int h = 0; h < R; ++h) {
-            float x = 0.f;
+            unsigned long long a = 0ull;
 #pragma unroll
-            for (int j = 0; j < E; ++j) x = fmaf(q[h][j], k[j], x);
-            for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-            // the butterfly leaves the same sum in every lane of the half
-            if (live) {
-                const float sv = x * scale;
+            for (int j = 0; j < E / 2; ++j) pair_fma(a, q2[h][j], pair_of(k[2 * j], k[2 * j + 1]));
+            sc[h] = pair_lo(a) + pair_hi(a);
+        }
+        HalfReduce<R, 8>::run(sc, hl);
+        const float mine = sc[0];
+#pragma unroll
+        for (int h = 0; h < R; ++h) sc[h] = __shfl_sync(0xffffffffu, mine, (lane & 16) | (h * (16 / R)));
+        if (live) {  // the same in all lanes of a half
+#pragma unroll
+            for (int h = 0; h < R; ++h) {
+                const float sv = sc[h] * scale;
                 if (sv > m[h]) {
                     const float carry = expf(m[h] - sv);
                     l[h] *= carry;
+                    const unsigned long long c2 = pair_of(carry, carry);
 #pragma unroll
-                    for (int j = 0; j < E; ++j) acc[h][j] *= carry;
+                    for (int j = 0; j < E / 2; ++j) {
+                        unsigned long long z = 0ull;
+                        pair_fma(z, acc2[h][j], c2);
+                        acc2[h][j] = z;
+                    }
                     m[h] = sv;
                 }
                 const float p = expf(sv - m[h]);
                 l[h] += p;
+                const unsigned long long p2 = pair_of(p, p);
 #pragma unroll
-                for (int j = 0; j < E; ++j) acc[h][j] = fmaf(p, v[j], acc[h][j]);
+                for (int j = 0; j < E / 2; ++j) pair_fma(acc2[h][j], p2, pair_of(v[2 * j], v[2 * j + 1]));
             }
         }
     }
@@ -853,7 +909,10 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
             w[1] = l[i];
         }
 #pragma unroll
-        for (int j = 0; j < E; ++j) w[2 + hl * E + j] = acc[i][j];
+        for (int j = 0; j < E / 2; ++j) {
+            w[2 + hl * E + 2 * j] = pair_lo(acc2[i][j]);
+            w[2 + hl * E + 2 * j + 1] = pair_hi(acc2[i][j]);
+        }
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < R * (D + 2); idx += blockDim.x) {

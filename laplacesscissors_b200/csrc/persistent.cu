@@ -1318,9 +1318,12 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     GainRegs gs;
                     if (KH > 0) gx.load(Lr.input_gain, lane);
                     else gs.load(Lr.input_gain, a.H);
-                    const bool ready = first_window_landed(ring, cur, op_qkv);
+                    // the exchange first, then the op's first weight window: when the
+                    // weights land late the wait costs max(data, weights), not their sum
+                    // plus a round trip
                     if (layer > 0) ok = compute_and(poll_vector(a.t_resid, a.H, e_qkv - 1u, xs, st, true));
                     if (!ok) break;
+                    const bool ready = first_window_landed(ring, cur, op_qkv);
                     LSX_PHASE_MARK(1);
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red, true);
                     e.out = a.t_qkv;
@@ -1340,9 +1343,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                 }
                 LSX_PHASE_MARK(4);
                 // o: residual += Wo attn
-                bool ready = first_window_landed(ring, cur, op_o);
                 ok = compute_and(poll_vector(a.t_attn, a.QH * a.D, e_attn, xs, st, true));
                 if (!ok) break;
+                bool ready = first_window_landed(ring, cur, op_o);
                 LSX_PHASE_MARK(5);
                 e.out = a.t_resid;
                 e.epoch = e_o;
@@ -1357,9 +1360,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     GainRegs gs;
                     if (KH > 0) gx.load(Lr.post_gain, lane);
                     else gs.load(Lr.post_gain, a.H);
-                    ready = first_window_landed(ring, cur, op_gu);
                     ok = compute_and(poll_vector(a.t_resid, a.H, e_o, xs, st, true));
                     if (!ok) break;
+                    ready = first_window_landed(ring, cur, op_gu);
                     LSX_PHASE_MARK(7);
                     if (KH == 0) rms_norm_inplace(xs, a.H, gs, a.eps, red, true);
                     e.out = a.t_feat;
@@ -1370,9 +1373,9 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                     LSX_PHASE_MARK(9);
                 }
                 // down: residual += Wd feature
-                ready = first_window_landed(ring, cur, op_down);
                 ok = compute_and(poll_vector(a.t_feat, a.I, e_gu, xs, st, true));
                 if (!ok) break;
+                ready = first_window_landed(ring, cur, op_down);
                 LSX_PHASE_MARK(10);
                 e.out = a.t_resid;
                 e.epoch = e_down;
