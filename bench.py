@@ -196,7 +196,7 @@ def cpu_decode_rate(ckpt: Path, generations: int = 1):
         f"{generations} whole generation(s) of 55 decode steps (oracle, f64 reductions, {threads} threads)"
 
 
-def cpu_readout_rate(w, hidden, targets, edit, seconds: float = 15.0):
+def cpu_readout_rate(w, hidden, targets, edit, seconds: float = 8.0):
     from laplacesscissors_b200 import synth
     from oracle import binding as oracle
     threads = cpu_threads()
@@ -682,7 +682,7 @@ def vocab_leg(gpu, dist, steps: int, warmup: int):
     }
 
 
-def triton_baseline_leg(ckpt: Path, steps: int = 3) -> dict:
+def triton_baseline_leg(ckpt: Path, steps: int = 2) -> dict:
     """The reference's own Triton kernels on this GPU (baseline/triton_reference.py,
     two subprocesses: the reference's runtime pattern, and its kernels alone in a
     CUDA graph)."""
@@ -690,7 +690,7 @@ def triton_baseline_leg(ckpt: Path, steps: int = 3) -> dict:
     script = ROOT / "baseline" / "triton_reference.py"
     for mode in ("runtime", "graph"):
         cmd = [sys.executable, str(script), "--mode", mode, "--checkpoint", str(ckpt), "--steps", str(steps),
-               "--warmup", "1"]
+               "--warmup", "1", "--readout-rows", "128"]
         try:
             r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
             line = r.stdout.strip().splitlines()[-1] if r.stdout.strip() else ""
