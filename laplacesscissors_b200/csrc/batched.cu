@@ -73,6 +73,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // x[m] = embedding row of tokens[m] (Model::embedding_tensor, src/model.rs:620-631).
 __global__ void embed_rows_kernel(const void* __restrict__ emb, int kind, float scale, const uint32_t* __restrict__ tokens,
                                   int H, float* __restrict__ x) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t m = blockIdx.x;
     const size_t base = (size_t)tokens[m] * H;
     for (int i = threadIdx.x; i < H; i += blockDim.x) {
@@ -90,6 +92,8 @@ __global__ void embed_rows_kernel(const void* __restrict__ emb, int kind, float 
 __global__ void rms_planes_kernel(const float* __restrict__ x, const int* __restrict__ rows, int H,
                                   const float* __restrict__ gain, float eps, __nv_bfloat16* __restrict__ hi,
                                   __nv_bfloat16* __restrict__ lo, float* __restrict__ out = nullptr) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float red[32];
     const size_t r = blockIdx.x;
     const float* xr = x + (size_t)(rows ? rows[r] : (int)r) * H;
@@ -179,6 +183,8 @@ __global__ void edit_rows_kernel(const float* __restrict__ h, int H, int kind, f
 template <int DPL>
 __global__ void qk_rope_kernel(float* __restrict__ qkv, int M, int T, int QH, int KVH, const float* __restrict__ q_gain,
                                const float* __restrict__ k_gain, float eps, const float2* __restrict__ rope) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int D = DPL * 32;
     const int lane = threadIdx.x & 31;
     const long long wid = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -651,6 +657,8 @@ bool launch_attention_tiled(cudaStream_t s, const float* qkv, int M, int T, int 
 // Four features per thread (two 16-byte loads, 8-byte plane stores) when I % 4 == 0.
 __global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, int I, int kind,
                                     __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t step = (size_t)gridDim.x * blockDim.x;
     if ((I & 3) == 0) {
         const size_t quads = total >> 2;
@@ -691,6 +699,8 @@ __global__ void gated_planes_kernel(const float* __restrict__ gu, size_t total, 
 __global__ void kv_store_kernel(const float* __restrict__ qkv, size_t total, int QH, int KVH, int D,
                                 float* __restrict__ keys, float* __restrict__ values, int T, int pos0,
                                 size_t case_stride, size_t group_stride, size_t pos_stride) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t kw = (size_t)KVH * D, stride = (size_t)(QH + 2 * KVH) * D;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const size_t m = i / kw, e = i % kw;
@@ -804,6 +814,8 @@ template <int DPL, int R>
 __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attention_part_kernel(
     const float* __restrict__ qkv, const float* __restrict__ keys, const float* __restrict__ values, int QH, int KVH,
     int pos, size_t case_stride, int splits, float scale, float* __restrict__ part) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int D = DPL * 32, E = D / 16, W = AttentionWalk<DPL>::kWarps, S = AttentionWalk<DPL>::kDepth;
     constexpr int kWalkers = 2 * W;
     extern __shared__ __align__(16) float smem[];  // attention_walk_smem<DPL, R>() bytes
@@ -938,6 +950,8 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
 template <int DPL>
 __global__ void cached_attention_merge_kernel(const float* __restrict__ part, int QH, int splits,
                                               __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int D = DPL * 32;
     const int c = blockIdx.x / QH, h = blockIdx.x % QH;
     const float* p = part + ((size_t)c * QH + h) * splits * (D + 2);
@@ -961,6 +975,8 @@ __global__ void cached_attention_merge_kernel(const float* __restrict__ part, in
 __global__ void __launch_bounds__(1024) row_argmax_tokens_kernel(const float* __restrict__ logits, int V,
                                                                  uint32_t* __restrict__ tokens,
                                                                  uint32_t* __restrict__ history, int* status) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ unsigned long long kbest[32];
     const float* z = logits + (size_t)blockIdx.x * V;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = blockDim.x >> 5;
@@ -1121,6 +1137,26 @@ int BatchedScorer::prefill(const uint32_t* tokens, size_t n) {
     return run(tokens, 1, n, 0, 0, nullptr, nullptr, Outputs{}, true);
 }
 
+// Launches `kernel` on `s` as a programmatic dependent of the kernel before it: its
+// CTAs may be scheduled while that kernel finishes, and its first instruction waits
+// for it (pdl_wait), so only the launch latency overlaps.  Used for the chain of
+// small kernels of a batched decode step.
+template <typename... Params, typename... Args>
+static cudaError_t chain_launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <int DPL>
 static bool launch_cached_attention(cudaStream_t s, const float* qkv, const float* keys, const float* values, int B,
                                     int QH, int KVH, int pos, size_t case_stride, int splits, float scale,
@@ -1131,8 +1167,8 @@ static bool launch_cached_attention(cudaStream_t s, const float* qkv, const floa
         if (cudaFuncSetAttribute((const void*)kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
             return false;
-        kernel<<<blocks, threads, smem, s>>>(qkv, keys, values, QH, KVH, pos, case_stride, splits, scale, part);
-        return true;
+        return chain_launch(kernel, dim3(blocks), dim3(threads), smem, s, qkv, keys, values, QH, KVH, pos,
+                            case_stride, splits, scale, part) == cudaSuccess;
     };
     bool ok;
     if (R == 1)
@@ -1144,8 +1180,8 @@ static bool launch_cached_attention(cudaStream_t s, const float* qkv, const floa
     else
         return false;
     if (!ok) return false;
-    cached_attention_merge_kernel<DPL><<<B * QH, 128, 0, s>>>(part, QH, splits, hi, lo);
-    return true;
+    return chain_launch(cached_attention_merge_kernel<DPL>, dim3(B * QH), dim3(128), 0, s, (const float*)part, QH,
+                        splits, hi, lo) == cudaSuccess;
 }
 
 int BatchedScorer::generate_batch(const uint32_t* prompts, size_t batch, size_t P, size_t maximum,
@@ -1221,49 +1257,67 @@ int BatchedScorer::generate_batch(const uint32_t* prompts, size_t batch, size_t 
     const int kv_blocks = (int)((B * kw + 255) / 256);
     for (size_t step = 0; step < maximum; ++step) {
         const int pos = (int)(P - 1 + step);
-        embed_rows_kernel<<<M, 256, 0, s>>>(c.embedding, c.embedding_kind, c.embedding_scale, d_tokens, H, x);
-        LSX_CUDA(cudaGetLastError(), "embedding rows");
+        LSX_CUDA(chain_launch(embed_rows_kernel, dim3(M), dim3(256), 0, s, c.embedding, c.embedding_kind,
+                              c.embedding_scale, (const uint32_t*)d_tokens, H, x),
+                 "embedding rows");
         for (size_t li = 0; li < layers_.size(); ++li) {
             const FusedLayer& Ly = layers_[li];
             float* bk = batch_cache_ + li * layer_stride;
             float* bv = bk + layer_stride / 2;
-            rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.input_gain, c.eps, hi, lo);
+            LSX_CUDA(chain_launch(rms_planes_kernel, dim3(M), dim3(256), 0, s, (const float*)x, (const int*)nullptr, H,
+                                  Ly.input_gain, c.eps, hi, lo, (float*)nullptr),
+                     "batched decode norm");
             LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wqkv, qkvw, Ly.bqkv, work, qkvw, false, status));
             const float2* rp = rope + (size_t)pos * half;
             bool ok;
             if (D == 128) {
-                qk_rope_kernel<4><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
-                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride,
-                                                          cap * D, D);
+                LSX_CUDA(chain_launch(qk_rope_kernel<4>, dim3(qk_blocks), dim3(256), 0, s, work, M, 1, QH, KVH,
+                                      Ly.q_gain, Ly.k_gain, c.qk_eps, rp),
+                         "batched decode rope");
+                LSX_CUDA(chain_launch(kv_store_kernel, dim3(kv_blocks), dim3(256), 0, s, (const float*)work, B * kw, QH,
+                                      KVH, D, bk, bv, 1, pos, case_stride, cap * D, (size_t)D),
+                         "batched decode cache append");
                 ok = launch_cached_attention<4>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
                                                 hi, lo);
             } else if (D == 64) {
-                qk_rope_kernel<2><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
-                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride,
-                                                          cap * D, D);
+                LSX_CUDA(chain_launch(qk_rope_kernel<2>, dim3(qk_blocks), dim3(256), 0, s, work, M, 1, QH, KVH,
+                                      Ly.q_gain, Ly.k_gain, c.qk_eps, rp),
+                         "batched decode rope");
+                LSX_CUDA(chain_launch(kv_store_kernel, dim3(kv_blocks), dim3(256), 0, s, (const float*)work, B * kw, QH,
+                                      KVH, D, bk, bv, 1, pos, case_stride, cap * D, (size_t)D),
+                         "batched decode cache append");
                 ok = launch_cached_attention<2>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
                                                 hi, lo);
             } else {
-                qk_rope_kernel<8><<<qk_blocks, 256, 0, s>>>(work, M, 1, QH, KVH, Ly.q_gain, Ly.k_gain, c.qk_eps, rp);
-                kv_store_kernel<<<kv_blocks, 256, 0, s>>>(work, B * kw, QH, KVH, D, bk, bv, 1, pos, case_stride,
-                                                          cap * D, D);
+                LSX_CUDA(chain_launch(qk_rope_kernel<8>, dim3(qk_blocks), dim3(256), 0, s, work, M, 1, QH, KVH,
+                                      Ly.q_gain, Ly.k_gain, c.qk_eps, rp),
+                         "batched decode rope");
+                LSX_CUDA(chain_launch(kv_store_kernel, dim3(kv_blocks), dim3(256), 0, s, (const float*)work, B * kw, QH,
+                                      KVH, D, bk, bv, 1, pos, case_stride, cap * D, (size_t)D),
+                         "batched decode cache append");
                 ok = launch_cached_attention<8>(s, work, bk, bv, M, QH, KVH, pos, case_stride, splits, c.scale, part,
                                                 hi, lo);
             }
             LSX_ENSURE(ok, "batched generation: attention launch (group ratio, shared memory)");
             LSX_CUDA(cudaGetLastError(), "batched decode attention");
             LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));
-            rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.post_gain, c.eps, hi, lo);
+            LSX_CUDA(chain_launch(rms_planes_kernel, dim3(M), dim3(256), 0, s, (const float*)x, (const int*)nullptr, H,
+                                  Ly.post_gain, c.eps, hi, lo, (float*)nullptr),
+                     "batched decode norm");
             LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wgu, 2 * I, Ly.bgu, work, 2 * I, false, status));
             const size_t feats = (size_t)M * I;
-            gated_planes_kernel<<<(int)std::min<size_t>((feats + 255) / 256, 148 * 16), 256, 0, s>>>(
-                work, feats, I, c.activation, hi, lo);
+            LSX_CUDA(chain_launch(gated_planes_kernel, dim3((unsigned)std::min<size_t>((feats + 255) / 256, 148 * 16)),
+                                  dim3(256), 0, s, (const float*)work, feats, I, c.activation, hi, lo),
+                     "batched decode gate");
             LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
         }
-        rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, c.final_gain, c.eps, hi, lo);
+        LSX_CUDA(chain_launch(rms_planes_kernel, dim3(M), dim3(256), 0, s, (const float*)x, (const int*)nullptr, H,
+                              c.final_gain, c.eps, hi, lo, (float*)nullptr),
+                 "batched decode norm");
         LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, c.head, V, c.head_bias, logits, V, false, status));
-        row_argmax_tokens_kernel<<<M, 1024, 0, s>>>(logits, V, d_tokens, history + step * B, status);
-        LSX_CUDA(cudaGetLastError(), "batched decode step");
+        LSX_CUDA(chain_launch(row_argmax_tokens_kernel, dim3(M), dim3(1024), 0, s, (const float*)logits, V, d_tokens,
+                              history + step * B, status),
+                 "batched decode step");
     }
     std::vector<uint32_t> hist(maximum * B);
     int host_status[2] = {0, 0};

@@ -1194,6 +1194,21 @@ __global__ void __launch_bounds__(kFewThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {  // ---------------- TMA producer ----------------
+            // The weight tiles of the first S stages do not depend on earlier kernels:
+            // they are requested before waiting for the preceding grid (a no-op
+            // unless launched as a programmatic dependent); the activation tiles,
+            // which the preceding kernel writes, after it.
+            int pre = 0;
+            for (int item = blockIdx.x; item < items && pre < S; item += gridDim.x) {
+                const int tile = item / p.ksplits, slice = item % p.ksplits;
+                const int kb0 = (int)((long long)slice * p.k_blocks / p.ksplits);
+                const int kb1 = (int)((long long)(slice + 1) * p.k_blocks / p.ksplits);
+                for (int kb = kb0; kb < kb1 && pre < S; ++kb, ++pre) {
+                    mbar_expect_tx(&full[pre], (uint32_t)stage_bytes);
+                    tma_load_2d(smem + (size_t)pre * stage_bytes, &map_w, kb * RK, tile * 128, &full[pre]);
+                }
+            }
+            pdl_wait();
             int stage = 0, issued = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -1202,13 +1217,15 @@ __global__ void __launch_bounds__(kFewThreads, 1)
                 const int kb0 = (int)((long long)slice * p.k_blocks / p.ksplits);
                 const int kb1 = (int)((long long)(slice + 1) * p.k_blocks / p.ksplits);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
                     uint8_t* sw = smem + (size_t)stage * stage_bytes;
-                    mbar_expect_tx(&full[stage], (uint32_t)stage_bytes);
-                    tma_load_2d(sw, &map_w, kb * RK, tile * 128, &full[stage]);
+                    if (issued >= pre) {  // a stage's first use was prefilled with its weight tile
+                        if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&full[stage], (uint32_t)stage_bytes);
+                        tma_load_2d(sw, &map_w, kb * RK, tile * 128, &full[stage]);
+                    }
                     tma_load_2d(sw + kTileW, &map_hi, kb * RK, 0, &full[stage]);
                     tma_load_2d(sw + kTileW + tile_a, &map_lo, kb * RK, 0, &full[stage]);
                     ++issued;
@@ -1273,6 +1290,7 @@ __global__ void __launch_bounds__(kFewThreads, 1)
         }
         __syncwarp();
     } else {  // ---------------- epilogue warps 2..5 ----------------
+        pdl_wait();  // out (accumulated into) and bias may come from earlier kernels
         const int quarter = warp & 3;
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -1697,9 +1715,20 @@ int few_rows_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat1
     cudaError_t e = cudaFuncSetAttribute((const void*)few_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e == cudaSuccess) {
+        // as a programmatic dependent of the kernel before it: the weight tiles stream
+        // while that kernel finishes (the activations are read after it completes)
         const int items = p.n_tiles * p.ksplits;
-        few_rows_kernel<<<std::min(items, G), kFewThreads, smem, ctx->stream>>>(mw, mhi, mlo, p);
-        e = cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(std::min(items, G));
+        cfg.blockDim = dim3(kFewThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = ctx->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, few_rows_kernel, mw, mhi, mlo, p);
     }
     if (e == cudaSuccess && p.ksplits > 1) {
         // the in-order sum of the slices, launched as a programmatic dependent so its
