@@ -717,9 +717,10 @@ __global__ void kv_store_kernel(const float* __restrict__ qkv, size_t total, int
 // reads one contiguous stretch of memory.
 // Block (case c, KV group g, split s) takes positions [s chunk, (s + 1) chunk) of
 // 0 .. pos of case c's cache. Each half-warp is one walker: walker w of the block
-// takes positions start + w, start + w + walkers, ...; a lane owns D / 16
-// consecutive elements of a row, so one 4-step butterfly reduces two positions'
-// dot products at once. Each walker carries the R query heads of the group (the K
+// takes positions start + w, start + w + walkers, ...; lane hl of a half owns the
+// D / 16 elements 64 u + 4 hl .. 64 u + 4 hl + 3 (u < D / 64) of a row, so every
+// 16-byte copy or load instruction of the half covers 256 contiguous bytes, and one
+// 4-step butterfly reduces two positions' dot products at once. Each walker carries the R query heads of the group (the K
 // and V rows are read once for all of them) with a running softmax per head
 // (kernels/ops.py:88-99); the walkers' states merge in shared memory, and the block
 // writes per head a partial state (max, sum, unnormalised output[D]) for
@@ -743,14 +744,15 @@ constexpr size_t attention_walk_smem() {
     return 4 * (ring > state ? ring : state);
 }
 
-// this lane's E floats of one row, global -> shared, asynchronously
+// this lane's E floats of one row (four at every 64 floats from src), global ->
+// shared at the same offsets from dst, asynchronously
 template <int E>
 __device__ __forceinline__ void lane_row_async(float* dst, const float* src) {
     static_assert(E % 4 == 0, "16-byte copies");
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
 #pragma unroll
-    for (int j = 0; j < E; j += 4)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 4 * j), "l"(src + j) : "memory");
+    for (int u = 0; u < E / 4; ++u)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + 256 * u), "l"(src + 64 * u) : "memory");
 }
 
 __device__ __forceinline__ void async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -760,17 +762,21 @@ __device__ __forceinline__ void async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// this lane's E floats of one row (four at every 64 floats), element order as copied
 template <int E>
 __device__ __forceinline__ void lane_row_load(const float* src, float (&x)[E]) {
 #pragma unroll
-    for (int j = 0; j < E; j += 4) {
-        const float4 t = *reinterpret_cast<const float4*>(src + j);
-        x[j] = t.x;
-        x[j + 1] = t.y;
-        x[j + 2] = t.z;
-        x[j + 3] = t.w;
+    for (int u = 0; u < E / 4; ++u) {
+        const float4 t = *reinterpret_cast<const float4*>(src + 64 * u);
+        x[4 * u] = t.x;
+        x[4 * u + 1] = t.y;
+        x[4 * u + 2] = t.z;
+        x[4 * u + 3] = t.w;
     }
 }
+
+// Row offset of a lane's local element e (0 <= e < E): lane hl owns 64 u + 4 hl + r.
+__device__ __forceinline__ int lane_elem(int e, int hl) { return ((e >> 2) << 6) + 4 * hl + (e & 3); }
 
 // Packed f32 pairs: Blackwell's fma.rn.f32x2 does two multiply-adds per instruction.
 __device__ __forceinline__ unsigned long long pair_of(float a, float b) {
@@ -825,11 +831,11 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
     const int n = pos + 1, chunk = (n + splits - 1) / splits;
     const int t0 = s * chunk, t1 = min(n, t0 + chunk);
     const size_t group = (size_t)c * case_stride + (size_t)g * (case_stride / KVH);
-    const float* kb = keys + group + hl * E;
-    const float* vb = values + group + hl * E;
+    const float* kb = keys + group + hl * 4;
+    const float* vb = values + group + hl * 4;
     const float* qrow = qkv + (size_t)c * (QH + 2 * KVH) * D;
     // ring slot: [K of the two halves' positions | V of the same], D floats each
-    float* ring = smem + warp * (S * 4 * D) + half * D + hl * E;
+    float* ring = smem + warp * (S * 4 * D) + half * D + hl * 4;
     // q and the output accumulators as packed pairs of this lane's E elements
     unsigned long long q2[R][E / 2], acc2[R][E / 2];
     float m[R], l[R];
@@ -837,10 +843,10 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
     for (int i = 0; i < R; ++i) {
         m[i] = -INFINITY;
         l[i] = 0.f;
-        const float* qh = qrow + (size_t)(g * R + i) * D + hl * E;
+        const float* qh = qrow + (size_t)(g * R + i) * D;
 #pragma unroll
         for (int j = 0; j < E / 2; ++j) {
-            q2[i][j] = pair_of(qh[2 * j], qh[2 * j + 1]);
+            q2[i][j] = pair_of(qh[lane_elem(2 * j, hl)], qh[lane_elem(2 * j + 1, hl)]);
             acc2[i][j] = 0ull;
         }
     }
@@ -922,8 +928,8 @@ __global__ void __launch_bounds__(32 * AttentionWalk<DPL>::kWarps) cached_attent
         }
 #pragma unroll
         for (int j = 0; j < E / 2; ++j) {
-            w[2 + hl * E + 2 * j] = pair_lo(acc2[i][j]);
-            w[2 + hl * E + 2 * j + 1] = pair_hi(acc2[i][j]);
+            w[2 + lane_elem(2 * j, hl)] = pair_lo(acc2[i][j]);
+            w[2 + lane_elem(2 * j + 1, hl)] = pair_hi(acc2[i][j]);
         }
     }
     __syncthreads();
