@@ -9,8 +9,7 @@ through the model) per second, device-timed with CUDA events on the library's
 stream.  `e2e` is the same generation through the C ABI call lsx_model_generate
 with host buffers (prompt upload, token and Frame downloads inside the timing).
 
-Sub-objects of the same line, one per configuration of the survey's measurement
-table:
+Sub-objects of the same line, one per measured configuration:
   readout         fused readout-margin validation of 4096 RMSNorm'd bf16 hidden
                   states against lm_head [151936, 1024] with a rank-16 Givens edit
   gemv            the bf16 GEMV microbenchmark (five shapes)
@@ -1203,7 +1202,7 @@ def long_decode(args, local):
 
 
 def decoder_flops_per_token(cfg: dict) -> int:
-    """2 x the decoder's matrix parameters (the survey's per-token decoder flops)."""
+    """2 x the decoder's matrix parameters (the decoder flops of one token)."""
     H, I, D = cfg["hidden"], cfg["intermediate"], cfg["head_dim"]
     q, kv = cfg["heads"] * D, cfg["kv_heads"] * D
     return 2 * cfg["layers"] * (H * (q + 2 * kv) + q * H + 3 * H * I)

@@ -1,4 +1,4 @@
-"""Decode parity at the other model widths of the survey's configs: Qwen3-4B
+"""Decode parity at the other measured model widths: Qwen3-4B
 (hidden 2560, 32/8 heads, I 9728, tied) and Qwen3-8B (hidden 4096, I 12288,
 untied head) shapes with 2 layers, through the persistent engine, against the
 oracle: greedy tokens identical except at oracle near-ties (|margin| < 1e-3),
