@@ -98,6 +98,7 @@ struct PArgs {
     int slots;
     int slot_bytes;
     int inflight;  // chunks the producer keeps in flight at most (0: every free slot)
+    int inflight_layers;  // the same during the layers' ops (the head streams with `inflight`)
     SmemLayout sm;
 };
 
@@ -1248,7 +1249,8 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_decode_kernel(const PA
                         }
                         // bound the bytes in flight per SM: a deep queue of bulk copies
                         // delays the small exchange loads behind it
-                        while (a.inflight > 0 && issued - landed >= a.inflight && go) {
+                        const int cap = oi < 4 * a.L ? a.inflight_layers : a.inflight;
+                        while (cap > 0 && issued - landed >= cap && go) {
                             if (!mbar_wait_bounded(&ring.full[lslot], lphase)) {
                                 raise_abort(st, kDeviceTimeoutWeights);
                                 go = false;
@@ -1697,6 +1699,13 @@ int PersistentDecoder::build(lsx_ctx* ctx, const FusedConfig& c, const std::vect
     // LSX_DECODE_INFLIGHT overrides.
     inflight_ = std::min(6, slots_ - 1);
     if (const char* v = std::getenv("LSX_DECODE_INFLIGHT")) inflight_ = std::max(0, std::min(std::atoi(v), slots_ - 1));
+    // At hidden 1024 two chunks per SM carry the layers' weights (they need about a
+    // third of HBM's bandwidth): 1% faster generations than six, one was 9% slower
+    // (measured at that width only; wider models keep the head's cap).
+    // LSX_DECODE_INFLIGHT_LAYERS overrides.
+    inflight_layers_ = c.hidden <= 1024 ? std::min(2, slots_ - 1) : inflight_;
+    if (const char* v = std::getenv("LSX_DECODE_INFLIGHT_LAYERS"))
+        inflight_layers_ = std::max(0, std::min(std::atoi(v), slots_ - 1));
     layer_count_ = (int)layers.size();
     smem_ = (size_t)layout_for(c, slots_, slot_bytes, grid_, layers.size()).total;
     PKernel k = kernel_for(c);
@@ -1746,6 +1755,7 @@ int PersistentDecoder::run(int steps) {
     a.slots = slots_;
     a.slot_bytes = slot_bytes_for(c);
     a.inflight = inflight_;
+    a.inflight_layers = inflight_layers_;
     a.sm = layout_for(c, slots_, a.slot_bytes, grid_, (size_t)layer_count_);
     void* args[] = {&a};
     LSX_CUDA(cudaLaunchCooperativeKernel((const void*)kernel_for(c), dim3(grid_), dim3(kThreads), args, smem_,

@@ -33,6 +33,7 @@ private:
     size_t smem_ = 0;
     int slots_ = 0;
     int inflight_ = 0;
+    int inflight_layers_ = 0;
     int ns_ = 0, split_min_ = 0;  // split attention: slots per KV group, first position + 1
     int grid_ = 0;
     int layer_count_ = 0;
