@@ -195,6 +195,27 @@ def cpu_decode_rate(ckpt: Path, generations: int = 1):
         f"{generations} whole generation(s) of 55 decode steps (oracle, f64 reductions, {threads} threads)"
 
 
+def cpu_gemv_rates(seconds: float = 0.5) -> tuple[dict, int]:
+    """The oracle's GEMV (f64 accumulation over bf16 W, f32 x) on the host cores for
+    every microbenchmark shape, each repeated for about `seconds`: GB/s of the same
+    2NK + 4K + 4N bytes per GEMV.  Inputs from the oracle's own generator."""
+    from oracle import binding as oracle
+    from oracle import synth as osynth
+    threads = cpu_threads()
+    out = {}
+    for n, k in GEMV_SHAPES:
+        w = osynth.normal_bf16(7, 100 + n, n * k, 0.02)
+        x = osynth.normal_f32(7, 200 + k, k)
+        oracle.matvec(w, oracle.BF16, x, None, n, k, threads)
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < seconds:
+            oracle.matvec(w, oracle.BF16, x, None, n, k, threads)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        out[f"{n}x{k}"] = (2 * n * k + 4 * k + 4 * n) / dt / 1e9
+    return out, threads
+
+
 def cpu_readout_rate(w, hidden, targets, edit, seconds: float = 8.0):
     from laplacesscissors_b200 import synth
     from oracle import binding as oracle
@@ -282,12 +303,16 @@ def run_decode(gpu, ckpt: Path, steps: int, warmup: int, dist, e2e: bool = True)
 GEMV_SHAPES = [(2048, 1024), (6144, 1024), (1024, 3072), (151936, 1024), (12288, 4096)]
 
 
-def run_gemv(gpu, iters: int = 20):
+def run_gemv(gpu, iters: int = 20, e2e_iters: int = 200):
     """The bf16 GEMV microbenchmark: y = W x through lsx_linear_into (the drop-in
     for Gpu::linear / kernels/ops.py matvec), W [N, K] bf16 N(0, 0.02), x f32 from
     bf16 N(0, 1), y f32.  Launches over enough weight copies to exceed L2 (>= 256 MB
     per pass) are captured once in a CUDA graph so launch gaps do not count;
-    CUDA events time `iters` replays.  bytes = 2NK + 4K + 4N per GEMV."""
+    CUDA events time `iters` replays.  bytes = 2NK + 4K + 4N per GEMV.
+    End to end, per GEMV as the reference's Model calls it: x uploaded from the
+    host (lsx_upload_f32), Gpu::linear (lsx_linear, a fresh output), y read back
+    to the host (lsx_read); W stays resident and rotates over the same copies;
+    host clock over `e2e_iters` GEMVs."""
     import ctypes as C
     from cuda.bindings import runtime as rt
 
@@ -325,6 +350,15 @@ def run_gemv(gpu, iters: int = 20):
         ms = ok(rt.cudaEventElapsedTime(start, stop)) / (iters * copies)
         nbytes = 2 * n * k + 4 * k + 4 * n
         out[f"{n}x{k}"] = {"us": ms * 1e3, "GB/s": nbytes / (ms * 1e-3) / 1e9, "weight_copies": copies}
+        x_host = gpu.read(x)
+        for r in range(3):
+            gpu.read(gpu.linear(gpu.upload_f32(x_host), ws[r % copies], None, n, k))
+        t0 = time.perf_counter()
+        for r in range(e2e_iters):
+            y_host = gpu.read(gpu.linear(gpu.upload_f32(x_host), ws[r % copies], None, n, k))
+        dt = (time.perf_counter() - t0) / e2e_iters
+        assert y_host.size == n
+        out[f"{n}x{k}"]["e2e"] = {"us": dt * 1e6, "GB/s": nbytes / dt / 1e9, "h2d_bytes": 4 * k, "d2h_bytes": 4 * n}
         ok(rt.cudaGraphExecDestroy(exe))
         ok(rt.cudaGraphDestroy(graph))
         ok(rt.cudaEventDestroy(start))
@@ -840,7 +874,18 @@ def main():
                          "note": "shapes below 12 MB are launch- and latency-bound: their time per launch (us) "
                                  "is the figure to read"},
             "results": gemv_frac,
+            "e2e": {"value": {k: v["e2e"]["GB/s"] for k, v in gemv.items()}, "unit": "GB/s",
+                    "us": {k: v["e2e"]["us"] for k, v in gemv.items()},
+                    "h2d_bytes_per_step": {k: v["e2e"]["h2d_bytes"] for k, v in gemv.items()},
+                    "d2h_bytes_per_step": {k: v["e2e"]["d2h_bytes"] for k, v in gemv.items()},
+                    "path": "per GEMV: lsx_upload_f32 (host x) -> lsx_linear -> lsx_read (host y), W resident; "
+                            "host clock"},
         }
+        if cpu:
+            rates, threads = cpu_gemv_rates()
+            line["gemv"]["cpu_baseline"] = {"value": rates, "unit": "GB/s", "cores": threads, "kind": "port",
+                                            "sample": "the oracle's GEMV of every shape repeated for ~0.5 s "
+                                                      f"(f64 accumulation, {threads} threads)"}
         if long4b is not None:
             line["long4b_batch"] = long4b
         if score8b is not None:
