@@ -41,17 +41,11 @@ namespace lsx {
 int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int M, int K,
                         const __nv_bfloat16* w, int N, const float* bias, float* out, int ldo, bool accumulate,
                         int* status);
+int gemm_gated_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int M, int K,
+                       const __nv_bfloat16* w, int N, const float* bias, int act_kind, __nv_bfloat16* out_hi,
+                       __nv_bfloat16* out_lo, int* status, bool* fused);
 
 namespace {
-
-__device__ __forceinline__ float act_fn(float x, int kind) {
-    switch (kind) {
-    case 0: return x / (1.f + expf(-x));
-    case 1: return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
-    case 2: return fmaxf(x, 0.f);
-    default: return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
-    }
-}
 
 __device__ __forceinline__ void split_store(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, float v) {
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
@@ -1442,12 +1436,24 @@ int BatchedScorer::run(const uint32_t* tokens, size_t cases, size_t T, size_t fi
         LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, QH * D, Ly.wo, H, Ly.bo, x, H, true, status));
         rms_planes_kernel<<<M, 256, 0, s>>>(x, nullptr, H, Ly.post_gain, c.eps, hi, lo);
         LSX_CUDA(cudaGetLastError(), "post norm");
-        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wgu, 2 * I, Ly.bgu, work, 2 * I, false, status));
+        // gate/up with the gated product in the GEMM's epilogue: the features' planes
+        // go to the work buffer (free until the next layer's q/k/v), which holds the
+        // f32 gate/up product otherwise
         const size_t feats = (size_t)M * I;
-        gated_planes_kernel<<<(int)std::min<size_t>((feats + 255) / 256, 148 * 16), 256, 0, s>>>(work, feats, I,
-                                                                                               c.activation, hi, lo);
-        LSX_CUDA(cudaGetLastError(), "gated product");
-        LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
+        __nv_bfloat16* f_hi = reinterpret_cast<__nv_bfloat16*>(work);
+        __nv_bfloat16* f_lo = f_hi + feats;
+        bool fused = false;
+        LSX_TRY(gemm_gated_enqueue(ctx_, hi, lo, M, H, Ly.wgu, 2 * I, Ly.bgu, c.activation, f_hi, f_lo, status,
+                                   &fused));
+        if (fused) {
+            LSX_TRY(gemm_planes_enqueue(ctx_, f_hi, f_lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
+        } else {
+            LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, H, Ly.wgu, 2 * I, Ly.bgu, work, 2 * I, false, status));
+            gated_planes_kernel<<<(int)std::min<size_t>((feats + 255) / 256, 148 * 16), 256, 0, s>>>(
+                work, feats, I, c.activation, hi, lo);
+            LSX_CUDA(cudaGetLastError(), "gated product");
+            LSX_TRY(gemm_planes_enqueue(ctx_, hi, lo, M, I, Ly.wd, H, Ly.bd, x, H, true, status));
+        }
     }
     int host_status[2] = {0, 0};
     if (scored == 0) {  // prefill: the KV cache is the result

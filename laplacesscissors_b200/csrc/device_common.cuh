@@ -16,6 +16,17 @@ enum : int {
     kDeviceTimeoutEpilogue = 3,
 };
 
+// The gate activations of the MLPs (kernels/ops.py gated: 0 SiLU, 1 GELU (erf),
+// 2 ReLU, 3 GELU (tanh)).
+__device__ __forceinline__ float act_fn(float x, int kind) {
+    switch (kind) {
+    case 0: return x / (1.f + expf(-x));
+    case 1: return 0.5f * x * (1.f + erff(x * 0.7071067811865476f));
+    case 2: return fmaxf(x, 0.f);
+    default: return 0.5f * x * (1.f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+    }
+}
+
 // About one second at B200 clocks; a healthy wait completes in microseconds.
 constexpr long long kWaitCycles = 2000000000ll;
 

@@ -64,6 +64,14 @@ struct ReadoutParams {
     // partial + s * M * V (row stride V, no bias), summed by split_reduce_kernel
     int ksplits;
     float* partial;
+    // store mode, gated (gated = activation kind + 1; 0: off): the columns are
+    // interleaved (gate, up) pairs, and instead of out the epilogue writes
+    // act(gate + bias) * (up + bias) for column pair j as bf16 hi and lo terms at
+    // g_hi / g_lo [row * ldg + j] (the next GEMM's A planes)
+    int gated;
+    __nv_bfloat16* g_hi;
+    __nv_bfloat16* g_lo;
+    int ldg;
 };
 
 enum { kModeMargin = 0, kModeStore = 2 };
@@ -222,8 +230,64 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // tile's 256 columns (+ bias), 32 columns per TMEM load.  With `accumulate` the
 // row's current values for the next 32 columns are loaded while the present ones
 // are summed, so each chunk costs one memory round trip at most.
+// The gated form of store_tile: 16 (gate, up) column pairs per 32-column chunk.
+__device__ __forceinline__ void store_tile_gated(uint32_t taddr, int row, bool live, int n0, const ReadoutParams& p,
+                                                 bool& nonfinite) {
+    const int kind = p.gated - 1;
+    const bool vec = (p.ldg & 7) == 0;
+#pragma unroll 1
+    for (int c = 0; c < RN / 32; ++c) {
+        uint32_t r[32];
+        tc_ld32(taddr + (uint32_t)(c * 32), r);
+        tc_wait_ld();
+        const int nb = n0 + c * 32;
+        if (!live || nb >= p.V) continue;
+        uint32_t hw[8], lw[8];  // bf16 pairs: feature 2 j in the low half, 2 j + 1 in the high half
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int col = nb + 2 * i;
+            float g = __uint_as_float(r[2 * i]), u = __uint_as_float(r[2 * i + 1]);
+            if (p.bias && col + 1 < p.V) {
+                g += p.bias[col];
+                u += p.bias[col + 1];
+            }
+            if (col + 1 < p.V) nonfinite |= !(isfinite(g) && isfinite(u));
+            const float v = act_fn(g, kind) * u;
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            const uint32_t hb = __bfloat16_as_ushort(h);
+            const uint32_t lb = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
+            if (i & 1) {
+                hw[i >> 1] |= hb << 16;
+                lw[i >> 1] |= lb << 16;
+            } else {
+                hw[i >> 1] = hb;
+                lw[i >> 1] = lb;
+            }
+        }
+        const size_t o = (size_t)row * p.ldg + (size_t)(nb >> 1);
+        if (vec && nb + 32 <= p.V) {
+            reinterpret_cast<uint4*>(p.g_hi + o)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            reinterpret_cast<uint4*>(p.g_hi + o)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            reinterpret_cast<uint4*>(p.g_lo + o)[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            reinterpret_cast<uint4*>(p.g_lo + o)[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (nb + 2 * i + 1 < p.V) {
+                    p.g_hi[o + i] = __ushort_as_bfloat16((unsigned short)(hw[i >> 1] >> (16 * (i & 1))));
+                    p.g_lo[o + i] = __ushort_as_bfloat16((unsigned short)(lw[i >> 1] >> (16 * (i & 1))));
+                }
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ void store_tile(uint32_t taddr, int row, bool live, int n0, const ReadoutParams& p,
                                            bool& nonfinite) {
+    if (p.gated) {
+        store_tile_gated(taddr, row, live, n0, p, nonfinite);
+        return;
+    }
     float* orow = p.out + (size_t)(live ? row : 0) * p.ldo;
     const bool vec = (p.ldo & 3) == 0;
     float4 cur[8], nxt[8];
@@ -1818,6 +1882,72 @@ int gemm_planes_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bflo
     const int total = p.m_tiles * p.n_tiles;
     k<<<std::min(total, ctx->sm_count), kReadoutThreads, smem, ctx->stream>>>(ma, ma2, mb, ma, mb, p);
     LSX_CUDA(cudaGetLastError(), "GEMM launch");
+    return LSX_OK;
+}
+
+// The gate/up GEMM with the gated product in its epilogue: out_hi / out_lo
+// [M, N / 2] receive act(gate) * up as the next GEMM's bf16 A planes (the columns
+// of W are interleaved (gate, up) rows), so the f32 [M, N] product is never
+// written.  Only the CTA-pair and single-CTA paths without a K split carry the
+// gated epilogue: *fused is false (and nothing is enqueued) for the shapes that
+// would take the few-row or split path, and the caller runs the two-kernel form.
+int gemm_gated_enqueue(lsx_ctx* ctx, const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int M, int K,
+                       const __nv_bfloat16* w, int N, const float* bias, int act_kind, __nv_bfloat16* out_hi,
+                       __nv_bfloat16* out_lo, int* status, bool* fused) {
+    LSX_ENSURE(fused != nullptr, "check the GEMM arguments");
+    *fused = false;
+    LSX_ENSURE(M > 0 && N > 0 && K > 0 && K % 8 == 0 && N % 2 == 0, "check the GEMM dimensions");
+    const char* few = getenv("LSX_GEMM_FEW_ROWS");
+    if (M <= kFewMaxRows && !(few && few[0] == '0')) return LSX_OK;
+    if (const char* g = getenv("LSX_GEMM_GATED")) {
+        if (g[0] == '0') return LSX_OK;
+    }
+    if ((uintptr_t)out_hi % 16 != 0 || (uintptr_t)out_lo % 16 != 0) return LSX_OK;
+    const char* single = getenv("LSX_GEMM_SINGLE");
+    const bool pair = !(single && single[0] == '1') && ctx->sm_count >= 2;
+    const int n_tiles = (N + RN - 1) / RN;
+    if (pair) {
+        const int pairs = ctx->sm_count / 2, k_blocks = (K + RK - 1) / RK;
+        const int tiles = ((M + kPairRows - 1) / kPairRows) * n_tiles;
+        const int ksplits = tiles * 2 <= pairs ? std::min(std::min(pairs / tiles, k_blocks / 4), 16) : 1;
+        if (ksplits > 1) return LSX_OK;
+    }
+    CUtensorMap ma, ma2, mb;
+    LSX_TRY(make_map(&ma, a_hi, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, RM));
+    LSX_TRY(make_map(&ma2, a_lo, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, RM));
+    LSX_TRY(make_map(&mb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, RN));
+    ReadoutParams p{};
+    p.M = M;
+    p.V = N;
+    p.H = K;
+    p.k_blocks = (K + RK - 1) / RK;
+    p.ext_blocks = 0;
+    p.m_tiles = (M + RM - 1) / RM;
+    p.n_tiles = n_tiles;
+    p.bias = bias;
+    p.status = status;
+    p.out = nullptr;
+    p.ldo = N;
+    p.accumulate = 0;
+    p.ksplits = 1;
+    p.gated = act_kind + 1;
+    p.g_hi = out_hi;
+    p.g_lo = out_lo;
+    p.ldg = N / 2;
+    if (pair) {
+        CUtensorMap mbh;
+        LSX_TRY(make_map(&mbh, w, (uint64_t)K, (uint64_t)N, (uint64_t)K * 2, kHalfN));
+        LSX_CUDA((launch_pair<2, 4, kModeStore>(ctx, ma, ma2, mbh, ma, mbh, p)), "gated GEMM launch");
+    } else {
+        auto k = readout_margin_kernel<2, 3, kModeStore>;
+        const size_t smem = readout_smem<2, 3>();
+        LSX_CUDA(cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "GEMM smem attribute");
+        const int total = p.m_tiles * p.n_tiles;
+        k<<<std::min(total, ctx->sm_count), kReadoutThreads, smem, ctx->stream>>>(ma, ma2, mb, ma, mb, p);
+        LSX_CUDA(cudaGetLastError(), "gated GEMM launch");
+    }
+    *fused = true;
     return LSX_OK;
 }
 
