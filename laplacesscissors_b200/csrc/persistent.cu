@@ -787,13 +787,18 @@ __device__ __forceinline__ bool attention_head(const PArgs& a, const FusedLayer&
         RowReduce<PB, 16>::run(sc, lane);
         const bool valid = warp + kWarps * (i0 + my_b) <= pos;
         const float s = valid ? sc[0] * a.scale : -INFINITY;
+        // the kLanesPerPos lanes of a position hold the same score, so the maximum and
+        // the sum over positions need only the rounds across position groups (the sum
+        // adds the same values in the same order as a full-warp sum of one lane each)
         float mb = s;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        for (int o = 16; o >= kLanesPerPos; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
         const float mn = fmaxf(m, mb);
         const float carry = expf(m - mn);
         const float p = valid ? expf(s - mn) : 0.f;
-        const float psum = warp_allsum(lane % kLanesPerPos == 0 ? p : 0.f);
+        float psum = p;
+#pragma unroll
+        for (int o = 16; o >= kLanesPerPos; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
         l = l * carry + psum;
 #pragma unroll
         for (int j = 0; j < DPL; ++j) acc[j] *= carry;
