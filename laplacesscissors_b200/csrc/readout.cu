@@ -1436,7 +1436,6 @@ __global__ void __launch_bounds__(kFewThreads, 1)
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(tmem_base) : "memory");
 }
 
-constexpr int kRankBlock = 16;
 constexpr int kMaxEditRank = 256;
 
 // c = (R - I) U h per hidden row (one warp per row) from the edit coordinates

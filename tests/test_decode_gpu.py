@@ -208,3 +208,30 @@ def test_qwen3_0_6b_engines_agree(gpu, qwen06b_dir):
     assert list(ta) == list(tb)
     for x, y in zip(fa, fb):
         assert rel_l2(x.logits, y.logits) < 1e-5
+
+
+def test_qwen3_0_6b_weight_stream_depth_changes_no_bits(gpu, qwen06b_dir):
+    """How many weight chunks the persistent kernel keeps in flight during the layers
+    (two by default at this width, LSX_DECODE_INFLIGHT_LAYERS) only changes when the
+    weights arrive, never what is computed: tokens, hidden states and logits are the
+    same bits with one, two and six chunks."""
+    prompt = synth.prompt_tokens(7, 24, 151936)
+    runs = []
+    saved = os.environ.get("LSX_DECODE_INFLIGHT_LAYERS")
+    try:
+        for depth in ("1", "2", "6"):
+            os.environ["LSX_DECODE_INFLIGHT_LAYERS"] = depth
+            model = lsx.Model.load(qwen06b_dir, gpu, 64)
+            assert model.info().persistent
+            runs.append(model.generate(prompt, 6, frames=True))
+            del model
+    finally:
+        if saved is None:
+            os.environ.pop("LSX_DECODE_INFLIGHT_LAYERS", None)
+        else:
+            os.environ["LSX_DECODE_INFLIGHT_LAYERS"] = saved
+    t0, _, f0 = runs[0]
+    for t, _, f in runs[1:]:
+        assert list(map(int, t)) == list(map(int, t0))
+        for a, b in zip(f, f0):
+            assert np.array_equal(a.hidden, b.hidden) and np.array_equal(a.logits, b.logits)

@@ -201,6 +201,30 @@ def test_batched_scores_wide_shapes(gpu, oracle, shape, vocab):
         check_argmax(amax[c], ref_amax, oracle, d, prompts[c], targets[c], capacity=80)
 
 
+def test_gated_epilogue_equals_two_kernel_form(gpu):
+    """The gate/up GEMM writing act(gate) * up as the down GEMM's bf16 planes from
+    its epilogue, against the two-kernel form (the f32 gate/up product, then
+    gated_planes_kernel; LSX_GEMM_GATED=0): the batched losses, argmaxes, margins and
+    logits are the same bits.  216 rows, so the CTA-pair GEMMs carry the epilogue."""
+    vocab = 8192
+    d = Path(tempfile.mkdtemp(prefix="lsx-gated-"))
+    synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(synth.QWEN3_0_6B, layers=2, vocab=vocab)), seed=8)
+    model = lsx.Model.load(d, gpu, 80)
+    prompts, targets = batch_cases(8, 3, 64, 9, vocab)
+    fused = model.score_batch(prompts, targets, logits=True)
+    saved = os.environ.get("LSX_GEMM_GATED")
+    os.environ["LSX_GEMM_GATED"] = "0"
+    try:
+        plain = model.score_batch(prompts, targets, logits=True)
+    finally:
+        if saved is None:
+            os.environ.pop("LSX_GEMM_GATED", None)
+        else:
+            os.environ["LSX_GEMM_GATED"] = saved
+    for a, b in zip(fused, plain):
+        assert np.array_equal(a, b)
+
+
 def test_batched_edited_scores_match_sequential(gpu, golden_tiny):
     """The "after" pass (src/scaling.rs:199-203): the edited readout of the
     unedited hidden states, batched, against lsx_model_score with the same plane
