@@ -440,155 +440,130 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(256, 1) causal_attention_mma_kernel(const float* __restrict__ qkv, int M, int T,
-                                                                     int QH, int KVH, float scale,
-                                                                     __nv_bfloat16* __restrict__ hi,
-                                                                     __nv_bfloat16* __restrict__ lo) {
-    extern __shared__ __align__(16) __nv_bfloat16 fa_smem[];
-    __nv_bfloat16* k_hi = fa_smem;                        // [kFaKeys][kFaKStride]
-    __nv_bfloat16* k_lo = k_hi + kFaKeys * kFaKStride;
-    __nv_bfloat16* v_hi = k_lo + kFaKeys * kFaKStride;    // V^T [kFaD][kFaVStride]
-    __nv_bfloat16* v_lo = v_hi + kFaD * kFaVStride;
-    const int R = QH / KVH;
-    const int qtiles = (T + 15) / 16;
-    int bid = blockIdx.x;
-    const int qt = bid % qtiles;
-    bid /= qtiles;
-    const int g = bid % KVH, c = bid / KVH;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = g * R + warp;
-    const int first = c * T, q0 = qt * 16;
-    const int r = lane >> 2, cq = (lane & 3) * 2;  // fragment row and column pair
-    const size_t stride = (size_t)(QH + 2 * KVH) * kFaD;
-    const float* kbase = qkv + (size_t)QH * kFaD + (size_t)g * kFaD;
-    const float* vbase = kbase + (size_t)KVH * kFaD;
+// Q fragments (hi, lo) of the 16 query rows q0 .. q0 + 15 of head h (rows past T - 1
+// repeat row T - 1): 8 k-steps of 16 dims.
+__device__ __forceinline__ void fa_load_q(const float* qkv, size_t stride, int first, int q0, int T, int h, int r,
+                                          int cq, uint32_t (&qa_hi)[8][4], uint32_t (&qa_lo)[8][4]) {
+    const int ra = min(q0 + r, T - 1), rb = min(q0 + r + 8, T - 1);
+    const float* qa = qkv + (size_t)(first + ra) * stride + (size_t)h * kFaD;
+    const float* qb = qkv + (size_t)(first + rb) * stride + (size_t)h * kFaD;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+        const int d0 = kk * 16 + cq;
+        const float2 x0 = *reinterpret_cast<const float2*>(qa + d0);
+        const float2 x1 = *reinterpret_cast<const float2*>(qb + d0);
+        const float2 x2 = *reinterpret_cast<const float2*>(qa + d0 + 8);
+        const float2 x3 = *reinterpret_cast<const float2*>(qb + d0 + 8);
+        split2(x0.x, x0.y, qa_hi[kk][0], qa_lo[kk][0]);
+        split2(x1.x, x1.y, qa_hi[kk][1], qa_lo[kk][1]);
+        split2(x2.x, x2.y, qa_hi[kk][2], qa_lo[kk][2]);
+        split2(x3.x, x3.y, qa_hi[kk][3], qa_lo[kk][3]);
+    }
+}
 
-    // Q fragments (hi, lo) for the 16 query rows of head h: 8 k-steps of 16 dims.
-    uint32_t qa_hi[8][4], qa_lo[8][4];
-    {
-        const int ra = min(q0 + r, T - 1), rb = min(q0 + r + 8, T - 1);
-        const float* qa = qkv + (size_t)(first + ra) * stride + (size_t)h * kFaD;
-        const float* qb = qkv + (size_t)(first + rb) * stride + (size_t)h * kFaD;
+// One warp's online-softmax update of its 16 query rows q0 .. q0 + 15 by the 64 keys
+// k0 .. k0 + 63, staged as K rows krow0 .. krow0 + 63 of (k_hi, k_lo) [key][kFaKStride]
+// and V^T columns vcol0 .. vcol0 + 63 of (v_hi, v_lo) [dim][vstride]: S = Q K^T, the
+// causal mask, the running maxima and sums, then O += P V (kernels/ops.py:88-99 per
+// tile).  Groups of 8 keys past q0 + 15 (or past T) are masked for every row of the
+// warp, so their S and P V products are skipped: their probabilities are exactly 0
+// and their terms would add exactly 0.  q0 is the same in all lanes, as every lane
+// takes part in each mma.sync.
+__device__ __forceinline__ void fa_tile(const uint32_t (&qa_hi)[8][4], const uint32_t (&qa_lo)[8][4],
+                                        float (&o)[16][4], float& m_a, float& m_b, float& l_a, float& l_b,
+                                        const __nv_bfloat16* k_hi, const __nv_bfloat16* k_lo,
+                                        const __nv_bfloat16* v_hi, const __nv_bfloat16* v_lo, int krow0, int vstride,
+                                        int vcol0, int k0, int q0, int T, float scale, int r, int cq) {
+    const int q_a = q0 + r, q_b = q0 + r + 8;
+    const int live = min(8, (min(q0 + 16, T) - k0 + 7) >> 3);  // n-tiles some row may see
+    // S = Q K^T over this tile: 8 n-tiles of 8 keys.
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        if (nt >= live) continue;
+        const int key = krow0 + nt * 8 + r;  // B fragment column (key) of this lane
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
             const int d0 = kk * 16 + cq;
-            const float2 x0 = *reinterpret_cast<const float2*>(qa + d0);
-            const float2 x1 = *reinterpret_cast<const float2*>(qb + d0);
-            const float2 x2 = *reinterpret_cast<const float2*>(qa + d0 + 8);
-            const float2 x3 = *reinterpret_cast<const float2*>(qb + d0 + 8);
-            split2(x0.x, x0.y, qa_hi[kk][0], qa_lo[kk][0]);
-            split2(x1.x, x1.y, qa_hi[kk][1], qa_lo[kk][1]);
-            split2(x2.x, x2.y, qa_hi[kk][2], qa_lo[kk][2]);
-            split2(x3.x, x3.y, qa_hi[kk][3], qa_lo[kk][3]);
+            const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + key * kFaKStride + d0);
+            const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + key * kFaKStride + d0 + 8);
+            const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + key * kFaKStride + d0);
+            const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + key * kFaKStride + d0 + 8);
+            mma_bf16(sc[nt], qa_lo[kk], bh0, bh1);
+            mma_bf16(sc[nt], qa_hi[kk], bl0, bl1);
+            mma_bf16(sc[nt], qa_hi[kk], bh0, bh1);
         }
     }
-    float o[16][4];
+    // causal mask, scale, running maxima of rows r and r + 8
+    float tile_a = -INFINITY, tile_b = -INFINITY;
 #pragma unroll
-    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows r and r + 8
-    const int q_a = q0 + r, q_b = q0 + r + 8;
-    const int key_end = min(T, q0 + 16);
-    for (int k0 = 0; k0 < key_end; k0 += kFaKeys) {
-        __syncthreads();  // the previous tile is no longer read
-        for (int i = threadIdx.x; i < kFaKeys * (kFaD / 2); i += blockDim.x) {
-            const int key = i / (kFaD / 2), d = (i % (kFaD / 2)) * 2;
-            const int src = first + min(k0 + key, T - 1);
-            const float2 kv = *reinterpret_cast<const float2*>(kbase + (size_t)src * stride + d);
-            const float2 vv = *reinterpret_cast<const float2*>(vbase + (size_t)src * stride + d);
-            uint32_t kh, kl;
-            split2(kv.x, kv.y, kh, kl);
-            *reinterpret_cast<uint32_t*>(k_hi + key * kFaKStride + d) = kh;
-            *reinterpret_cast<uint32_t*>(k_lo + key * kFaKStride + d) = kl;
-            const __nv_bfloat16 v0 = __float2bfloat16_rn(vv.x), v1 = __float2bfloat16_rn(vv.y);
-            v_hi[d * kFaVStride + key] = v0;
-            v_hi[(d + 1) * kFaVStride + key] = v1;
-            v_lo[d * kFaVStride + key] = __float2bfloat16_rn(vv.x - __bfloat162float(v0));
-            v_lo[(d + 1) * kFaVStride + key] = __float2bfloat16_rn(vv.y - __bfloat162float(v1));
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int key = k0 + nt * 8 + cq + e;
+            sc[nt][e] = key <= q_a && key < T ? sc[nt][e] * scale : -INFINITY;
+            sc[nt][2 + e] = key <= q_b && key < T ? sc[nt][2 + e] * scale : -INFINITY;
+            tile_a = fmaxf(tile_a, sc[nt][e]);
+            tile_b = fmaxf(tile_b, sc[nt][2 + e]);
         }
-        __syncthreads();
-        if (warp >= R) continue;
-        // S = Q K^T over this tile: 8 n-tiles of 8 keys.
-        float sc[8][4];
+    }
+    tile_a = fmaxf(tile_a, __shfl_xor_sync(0xffffffffu, tile_a, 1));
+    tile_a = fmaxf(tile_a, __shfl_xor_sync(0xffffffffu, tile_a, 2));
+    tile_b = fmaxf(tile_b, __shfl_xor_sync(0xffffffffu, tile_b, 1));
+    tile_b = fmaxf(tile_b, __shfl_xor_sync(0xffffffffu, tile_b, 2));
+    const float mn_a = fmaxf(m_a, tile_a), mn_b = fmaxf(m_b, tile_b);
+    const float carry_a = expf(m_a - mn_a), carry_b = expf(m_b - mn_b);
+    m_a = mn_a;
+    m_b = mn_b;
+    float sum_a = 0.f, sum_b = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-            const int key = nt * 8 + r;  // B fragment column (key) of this lane
+    for (int nt = 0; nt < 8; ++nt) {
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const int d0 = kk * 16 + cq;
-                const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + key * kFaKStride + d0);
-                const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + key * kFaKStride + d0 + 8);
-                const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + key * kFaKStride + d0);
-                const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + key * kFaKStride + d0 + 8);
-                mma_bf16(sc[nt], qa_lo[kk], bh0, bh1);
-                mma_bf16(sc[nt], qa_hi[kk], bl0, bl1);
-                mma_bf16(sc[nt], qa_hi[kk], bh0, bh1);
-            }
+        for (int e = 0; e < 2; ++e) {
+            sc[nt][e] = expf(sc[nt][e] - mn_a);
+            sc[nt][2 + e] = expf(sc[nt][2 + e] - mn_b);
+            sum_a += sc[nt][e];
+            sum_b += sc[nt][2 + e];
         }
-        // causal mask, scale, running maxima of rows r and r + 8
-        float tile_a = -INFINITY, tile_b = -INFINITY;
+    }
+    l_a = l_a * carry_a + sum_a;
+    l_b = l_b * carry_b + sum_b;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+    for (int n = 0; n < 16; ++n) {
+        o[n][0] *= carry_a;
+        o[n][1] *= carry_a;
+        o[n][2] *= carry_b;
+        o[n][3] *= carry_b;
+    }
+    // O += P V: P's accumulator tiles (2j, 2j + 1) form the A operand of k-step j.
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int key = k0 + nt * 8 + cq + e;
-                sc[nt][e] = key <= q_a && key < T ? sc[nt][e] * scale : -INFINITY;
-                sc[nt][2 + e] = key <= q_b && key < T ? sc[nt][2 + e] * scale : -INFINITY;
-                tile_a = fmaxf(tile_a, sc[nt][e]);
-                tile_b = fmaxf(tile_b, sc[nt][2 + e]);
-            }
-        }
-        tile_a = fmaxf(tile_a, __shfl_xor_sync(0xffffffffu, tile_a, 1));
-        tile_a = fmaxf(tile_a, __shfl_xor_sync(0xffffffffu, tile_a, 2));
-        tile_b = fmaxf(tile_b, __shfl_xor_sync(0xffffffffu, tile_b, 1));
-        tile_b = fmaxf(tile_b, __shfl_xor_sync(0xffffffffu, tile_b, 2));
-        const float mn_a = fmaxf(m_a, tile_a), mn_b = fmaxf(m_b, tile_b);
-        const float carry_a = expf(m_a - mn_a), carry_b = expf(m_b - mn_b);
-        m_a = mn_a;
-        m_b = mn_b;
-        float sum_a = 0.f, sum_b = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                sc[nt][e] = expf(sc[nt][e] - mn_a);
-                sc[nt][2 + e] = expf(sc[nt][2 + e] - mn_b);
-                sum_a += sc[nt][e];
-                sum_b += sc[nt][2 + e];
-            }
-        }
-        l_a = l_a * carry_a + sum_a;
-        l_b = l_b * carry_b + sum_b;
+    for (int j = 0; j < 4; ++j) {
+        if (2 * j >= live) continue;  // P is exactly 0 on these keys
+        uint32_t pa_hi[4], pa_lo[4];
+        split2(sc[2 * j][0], sc[2 * j][1], pa_hi[0], pa_lo[0]);
+        split2(sc[2 * j][2], sc[2 * j][3], pa_hi[1], pa_lo[1]);
+        split2(sc[2 * j + 1][0], sc[2 * j + 1][1], pa_hi[2], pa_lo[2]);
+        split2(sc[2 * j + 1][2], sc[2 * j + 1][3], pa_hi[3], pa_lo[3]);
 #pragma unroll
         for (int n = 0; n < 16; ++n) {
-            o[n][0] *= carry_a;
-            o[n][1] *= carry_a;
-            o[n][2] *= carry_b;
-            o[n][3] *= carry_b;
-        }
-        // O += P V: P's accumulator tiles (2j, 2j + 1) form the A operand of k-step j.
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint32_t pa_hi[4], pa_lo[4];
-            split2(sc[2 * j][0], sc[2 * j][1], pa_hi[0], pa_lo[0]);
-            split2(sc[2 * j][2], sc[2 * j][3], pa_hi[1], pa_lo[1]);
-            split2(sc[2 * j + 1][0], sc[2 * j + 1][1], pa_hi[2], pa_lo[2]);
-            split2(sc[2 * j + 1][2], sc[2 * j + 1][3], pa_hi[3], pa_lo[3]);
-#pragma unroll
-            for (int n = 0; n < 16; ++n) {
-                const int d = n * 8 + r;  // B fragment column (dim) of this lane
-                const int kb = j * 16 + cq;
-                const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + d * kFaVStride + kb);
-                const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + d * kFaVStride + kb + 8);
-                const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + d * kFaVStride + kb);
-                const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + d * kFaVStride + kb + 8);
-                mma_bf16(o[n], pa_lo, bh0, bh1);
-                mma_bf16(o[n], pa_hi, bl0, bl1);
-                mma_bf16(o[n], pa_hi, bh0, bh1);
-            }
+            const int d = n * 8 + r;  // B fragment column (dim) of this lane
+            const int kb = vcol0 + j * 16 + cq;
+            const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + d * vstride + kb);
+            const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + d * vstride + kb + 8);
+            const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + d * vstride + kb);
+            const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + d * vstride + kb + 8);
+            mma_bf16(o[n], pa_lo, bh0, bh1);
+            mma_bf16(o[n], pa_hi, bl0, bl1);
+            mma_bf16(o[n], pa_hi, bh0, bh1);
         }
     }
-    if (warp >= R) return;
+}
+
+// The attention output of one warp's 16 query rows, normalised, as bf16 hi/lo.
+__device__ __forceinline__ void fa_store(const float (&o)[16][4], float l_a, float l_b, int first, int q0, int T,
+                                         int QH, int h, int r, int cq, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const int q_a = q0 + r, q_b = q0 + r + 8;
     l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
     l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
@@ -613,6 +588,118 @@ __global__ void __launch_bounds__(256, 1) causal_attention_mma_kernel(const floa
     }
 }
 
+// Keys src0 .. src0 + n - 1 (rows past T - 1 repeat row T - 1) of one case and KV group,
+// split into bf16 hi/lo: K rows from krow0 of (k_hi, k_lo) [key][kFaKStride], V^T
+// columns from vcol0 of (v_hi, v_lo) [dim][vstride].  All threads of the block.
+__device__ __forceinline__ void fa_stage(const float* kbase, const float* vbase, size_t stride, int first, int src0,
+                                         int n, int T, __nv_bfloat16* k_hi, __nv_bfloat16* k_lo,
+                                         __nv_bfloat16* v_hi, __nv_bfloat16* v_lo, int krow0, int vstride,
+                                         int vcol0) {
+    for (int i = threadIdx.x; i < n * (kFaD / 2); i += blockDim.x) {
+        const int key = i / (kFaD / 2), d = (i % (kFaD / 2)) * 2;
+        const int src = first + min(src0 + key, T - 1);
+        const float2 kv = *reinterpret_cast<const float2*>(kbase + (size_t)src * stride + d);
+        const float2 vv = *reinterpret_cast<const float2*>(vbase + (size_t)src * stride + d);
+        uint32_t kh, kl;
+        split2(kv.x, kv.y, kh, kl);
+        *reinterpret_cast<uint32_t*>(k_hi + (krow0 + key) * kFaKStride + d) = kh;
+        *reinterpret_cast<uint32_t*>(k_lo + (krow0 + key) * kFaKStride + d) = kl;
+        const __nv_bfloat16 v0 = __float2bfloat16_rn(vv.x), v1 = __float2bfloat16_rn(vv.y);
+        v_hi[d * vstride + vcol0 + key] = v0;
+        v_hi[(d + 1) * vstride + vcol0 + key] = v1;
+        v_lo[d * vstride + vcol0 + key] = __float2bfloat16_rn(vv.x - __bfloat162float(v0));
+        v_lo[(d + 1) * vstride + vcol0 + key] = __float2bfloat16_rn(vv.y - __bfloat162float(v1));
+    }
+}
+
+__global__ void __launch_bounds__(256, 1) causal_attention_mma_kernel(const float* __restrict__ qkv, int M, int T,
+                                                                     int QH, int KVH, float scale,
+                                                                     __nv_bfloat16* __restrict__ hi,
+                                                                     __nv_bfloat16* __restrict__ lo) {
+    extern __shared__ __align__(16) __nv_bfloat16 fa_smem[];
+    __nv_bfloat16* k_hi = fa_smem;                        // [kFaKeys][kFaKStride]
+    __nv_bfloat16* k_lo = k_hi + kFaKeys * kFaKStride;
+    __nv_bfloat16* v_hi = k_lo + kFaKeys * kFaKStride;    // V^T [kFaD][kFaVStride]
+    __nv_bfloat16* v_lo = v_hi + kFaD * kFaVStride;
+    const int R = QH / KVH;
+    const int qtiles = (T + 15) / 16;
+    int bid = blockIdx.x;
+    const int qt = bid % qtiles;
+    bid /= qtiles;
+    const int g = bid % KVH, c = bid / KVH;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = g * R + warp;
+    const int first = c * T, q0 = qt * 16;
+    const int r = lane >> 2, cq = (lane & 3) * 2;  // fragment row and column pair
+    const size_t stride = (size_t)(QH + 2 * KVH) * kFaD;
+    const float* kbase = qkv + (size_t)QH * kFaD + (size_t)g * kFaD;
+    const float* vbase = kbase + (size_t)KVH * kFaD;
+    uint32_t qa_hi[8][4], qa_lo[8][4];
+    fa_load_q(qkv, stride, first, q0, T, h, r, cq, qa_hi, qa_lo);
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;  // rows r and r + 8
+    const int key_end = min(T, q0 + 16);
+    for (int k0 = 0; k0 < key_end; k0 += kFaKeys) {
+        __syncthreads();  // the previous tile is no longer read
+        fa_stage(kbase, vbase, stride, first, k0, kFaKeys, T, k_hi, k_lo, v_hi, v_lo, 0, kFaVStride, 0);
+        __syncthreads();
+        if (warp >= R) continue;
+        fa_tile(qa_hi, qa_lo, o, m_a, m_b, l_a, l_b, k_hi, k_lo, v_hi, v_lo, 0, kFaVStride, 0, k0, q0, T, scale, r,
+                cq);
+    }
+    if (warp >= R) return;
+    fa_store(o, l_a, l_b, first, q0, T, QH, h, r, cq, hi, lo);
+}
+
+// Short cases (T <= kFaShortKeys, the scoring workload's cases): one block per case
+// and KV group stages all of the case's keys once, and its eight warps take the
+// (16-query tile, query head) tasks of the group in turn, with the per-tile
+// arithmetic of causal_attention_mma_kernel (so the results are the same bits).
+constexpr int kFaShortKeys = 128;
+constexpr int kFaShortVStride = kFaShortKeys + 8;
+
+__global__ void __launch_bounds__(256, 1) causal_attention_mma_case_kernel(const float* __restrict__ qkv, int M,
+                                                                          int T, int QH, int KVH, float scale,
+                                                                          __nv_bfloat16* __restrict__ hi,
+                                                                          __nv_bfloat16* __restrict__ lo) {
+    extern __shared__ __align__(16) __nv_bfloat16 fa_smem[];
+    __nv_bfloat16* k_hi = fa_smem;                             // [kFaShortKeys][kFaKStride]
+    __nv_bfloat16* k_lo = k_hi + kFaShortKeys * kFaKStride;
+    __nv_bfloat16* v_hi = k_lo + kFaShortKeys * kFaKStride;    // V^T [kFaD][kFaShortVStride]
+    __nv_bfloat16* v_lo = v_hi + kFaD * kFaShortVStride;
+    const int R = QH / KVH;
+    const int qtiles = (T + 15) / 16;
+    const int g = blockIdx.x % KVH, c = blockIdx.x / KVH;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    const int first = c * T;
+    const int r = lane >> 2, cq = (lane & 3) * 2;
+    const size_t stride = (size_t)(QH + 2 * KVH) * kFaD;
+    const float* kbase = qkv + (size_t)QH * kFaD + (size_t)g * kFaD;
+    const float* vbase = kbase + (size_t)KVH * kFaD;
+    const int staged = ((T + kFaKeys - 1) / kFaKeys) * kFaKeys;  // whole 64-key tiles, <= kFaShortKeys
+    fa_stage(kbase, vbase, stride, first, 0, staged, T, k_hi, k_lo, v_hi, v_lo, 0, kFaShortVStride, 0);
+    __syncthreads();
+    for (int task = warp; task < qtiles * R; task += warps) {  // the same in all lanes of a warp
+        const int qt = task / R, h = g * R + task % R;
+        const int q0 = qt * 16;
+        uint32_t qa_hi[8][4], qa_lo[8][4];
+        fa_load_q(qkv, stride, first, q0, T, h, r, cq, qa_hi, qa_lo);
+        float o[16][4];
+#pragma unroll
+        for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+        const int key_end = min(T, q0 + 16);
+        for (int k0 = 0; k0 < key_end; k0 += kFaKeys)
+            fa_tile(qa_hi, qa_lo, o, m_a, m_b, l_a, l_b, k_hi, k_lo, v_hi, v_lo, k0, kFaShortVStride, k0, k0, q0, T,
+                    scale, r, cq);
+        fa_store(o, l_a, l_b, first, q0, T, QH, h, r, cq, hi, lo);
+    }
+}
+
+constexpr size_t kFaShortSmem = (size_t)(2 * kFaShortKeys * kFaKStride + 2 * kFaD * kFaShortVStride) * 2;
+
 constexpr size_t kFaSmem = (size_t)(2 * kFaKeys * kFaKStride + 2 * kFaD * kFaVStride) * 2;
 
 // Tensor-core attention when head_dim is 128 and a group has at most eight query heads.
@@ -626,6 +713,16 @@ bool launch_attention_mma(cudaStream_t s, const float* qkv, int M, int T, int QH
         return false;
     }
     const int R = QH / KVH;
+    // short cases: one block per case and KV group (LSX_ATTENTION_PER_CASE=0: per 16-query tile)
+    const char* per_case = getenv("LSX_ATTENTION_PER_CASE");
+    if (T <= kFaShortKeys && !(per_case && per_case[0] == '0') &&
+        cudaFuncSetAttribute((const void*)causal_attention_mma_case_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaShortSmem) == cudaSuccess) {
+        causal_attention_mma_case_kernel<<<(M / T) * KVH, 256, kFaShortSmem, s>>>(qkv, M, T, QH, KVH, scale, hi,
+                                                                                  lo);
+        return true;
+    }
+    (void)cudaGetLastError();
     const int blocks = (M / T) * KVH * ((T + 15) / 16);
     causal_attention_mma_kernel<<<blocks, 32 * std::max(R, 4), kFaSmem, s>>>(qkv, M, T, QH, KVH, scale, hi, lo);
     return true;

@@ -225,6 +225,29 @@ def test_gated_epilogue_equals_two_kernel_form(gpu):
         assert np.array_equal(a, b)
 
 
+def test_per_case_attention_equals_query_tile_blocks(gpu):
+    """Short cases' attention with one block per (case, KV group) staging all keys
+    once, against one block per 16-query tile (LSX_ATTENTION_PER_CASE=0): the same
+    per-tile arithmetic, so the batched results are the same bits."""
+    vocab = 8192
+    d = Path(tempfile.mkdtemp(prefix="lsx-attcase-"))
+    synth.make_qwen3_checkpoint(d, synth.qwen3_config(**dict(synth.QWEN3_8B, layers=2, vocab=vocab)), seed=9)
+    model = lsx.Model.load(d, gpu, 80)
+    prompts, targets = batch_cases(9, 3, 64, 9, vocab)
+    per_case = model.score_batch(prompts, targets, logits=True)
+    saved = os.environ.get("LSX_ATTENTION_PER_CASE")
+    os.environ["LSX_ATTENTION_PER_CASE"] = "0"
+    try:
+        tiles = model.score_batch(prompts, targets, logits=True)
+    finally:
+        if saved is None:
+            os.environ.pop("LSX_ATTENTION_PER_CASE", None)
+        else:
+            os.environ["LSX_ATTENTION_PER_CASE"] = saved
+    for a, b in zip(per_case, tiles):
+        assert np.array_equal(a, b)
+
+
 def test_batched_edited_scores_match_sequential(gpu, golden_tiny):
     """The "after" pass (src/scaling.rs:199-203): the edited readout of the
     unedited hidden states, batched, against lsx_model_score with the same plane
