@@ -758,7 +758,9 @@ def main():
                                                           "(0: one lsx_model_score call per case)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling aid: device legs only, no e2e or CPU legs, warm-up as given")
-    ap.add_argument("--layers", type=int, default=28, help="profiling aid: decoder layers of the checkpoint")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling aid: decoder layers of the checkpoint (decode profile: default 28; score8b: a "
+                         "reduced Qwen3-8B-width model for ncu section captures, one rank)")
     args = ap.parse_args()
     rank, local, world = env_rank()
     if args.impl == "reference":
@@ -1112,7 +1114,7 @@ def profile_run(args, local):
     gpu = lsx.Gpu(local)
     out = {"profile": True}
     if args.workload in ("all", "decode"):
-        dec = run_decode(gpu, build_checkpoint(local, args.layers), args.steps, args.warmup, dist, e2e=False)
+        dec = run_decode(gpu, build_checkpoint(local, args.layers or 28), args.steps, args.warmup, dist, e2e=False)
         out["decode_ms_per_generation"] = dec["dev_ms"] / args.steps
         out["decode_graph"] = dec["graph"]
         out["kernels_per_step"] = dec["kernels_per_step"]
@@ -1320,8 +1322,14 @@ def scoring_batched(args, rank, local, world):
     from laplacesscissors_b200 import synth
     # One writer for the 16 GB checkpoint, before the process group exists (writing it
     # takes longer than a collective may wait); the other ranks wait for its marker.
+    # --layers: the same widths with fewer layers (profiling captures, one rank).
+    over = {} if args.layers is None else {"layers": args.layers}
+    if over and world != 1:
+        raise SystemExit("score8b --layers is a one-rank profiling aid")
     marker = Path(tempfile.gettempdir()) / "lsx-bench-qwen3_8b-seed7.complete"
-    if rank == 0:
+    if over:
+        model_checkpoint("QWEN3_8B", **over)
+    elif rank == 0:
         model_checkpoint("QWEN3_8B")
         marker.touch()
     else:
@@ -1332,9 +1340,9 @@ def scoring_batched(args, rank, local, world):
             time.sleep(1.0)
     dist = Dist(world, local)
     gpu = lsx.Gpu(local)
-    cfg = synth.QWEN3_8B
+    cfg = dict(synth.QWEN3_8B, **over)  # the flop count follows the checkpoint's layers
     eos, V, P, n = 151645, cfg["vocab"], 64, 9
-    model = lsx.Model.load(model_checkpoint("QWEN3_8B"), gpu, 80)
+    model = lsx.Model.load(model_checkpoint("QWEN3_8B", **over), gpu, 80)
     first_case = 100 + rank * args.cases
 
     def batch(first, count):
